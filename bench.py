@@ -1,0 +1,781 @@
+#!/usr/bin/env python
+"""Benchmark of the llm_quant quantization hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload nf4|group|rotquant|kv]
+
+N > 1 is launched one process per GPU (torchrun, NCCL); rank 0 prints one
+JSON line.  Default workload (``nf4``): whole-model NF4 (block 64, double
+quantization over 256 scales) quantize + dequantize of a Llama-3-8B-shaped
+weight set, 32 layers x {q, o 4096x4096; k, v 1024x4096; gate, up
+14336x4096; down 4096x14336}, bf16 ~ N(0, 0.02), the layers split in
+contiguous blocks across the ranks (strong scaling, no data-path
+collective; the final NCCL gather of packed codes + scales to rank 0 is
+timed separately).  One step = QLoRALinear.pack_base + _dequantize_base on
+every weight of the rank's layers.
+
+value     = algorithmic bytes of all ranks per step / max-over-ranks step time
+            (CUDA events, inputs resident in HBM; 14 GB of weights > L2).
+e2e       = the same bytes / time of the same public-API calls with the
+            weights copied from pinned host memory and the packed codes +
+            scales copied back, every step.
+roofline  = the dominant kernel timed alone with CUDA events on its stream.
+cpu_baseline / --impl reference = the CPU oracle's restatement of the
+            reference algorithm on a bounded sample, on the host cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from concurrent.futures import ThreadPoolExecutor
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "group-quant HBM GB/s (% of peak) at 1/2/4/8 GPU; W4A16 dequant-GEMM TFLOP/s"
+LLAMA3_8B = [("q", 4096, 4096), ("k", 1024, 4096), ("v", 1024, 4096), ("o", 4096, 4096),
+             ("gate", 14336, 4096), ("up", 14336, 4096), ("down", 4096, 14336)]
+NUM_LAYERS = 32
+
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of each workload's
+# dominant kernel, from the ncu captures summarised under profiles/ (None
+# until captured).
+NCU_TRAFFIC = {
+    "nf4": None,
+    "group": None,
+    "rotquant": None,
+    "kv": None,
+}
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+# ─────────────────────────────────────────────────────────────────────────────
+# process group / timing helpers
+# ─────────────────────────────────────────────────────────────────────────────
+
+class Ctx:
+    def __init__(self, gpus: int):
+        import torch
+        import torch.distributed as dist
+        self.torch, self.dist = torch, dist
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        if self.world != gpus:
+            raise SystemExit(f"--gpus {gpus} but WORLD_SIZE={self.world}")
+        self.dev = torch.device("cuda", self.local)
+        torch.cuda.set_device(self.dev)
+        if self.world > 1:
+            from datetime import timedelta
+            dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                    device_id=self.dev)
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier(device_ids=[self.local])
+
+    def max(self, v: float) -> float:
+        if self.world == 1:
+            return v
+        t = self.torch.tensor([v], dtype=self.torch.float64, device=self.dev)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, v: float) -> float:
+        if self.world == 1:
+            return v
+        t = self.torch.tensor([v], dtype=self.torch.float64, device=self.dev)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM)
+        return float(t.item())
+
+    def close(self):
+        if self.world > 1:
+            self.dist.destroy_process_group()
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, enabled: bool):
+        self.proc = None
+        self.path = None
+        if not enabled:
+            return
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "50"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self, gpus):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    idx = int(parts[0])
+                except ValueError:
+                    continue
+                if idx not in gpus:
+                    continue
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        util = [float(r[4]) if r[4].replace(".", "").isdigit() else 0.0 for r in rows]
+        loaded = [r for r, u in zip(rows, util) if u >= 50] or rows
+        sm = [float(r[1]) for r in loaded if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in loaded for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(loaded)}
+
+
+def capture(torch, fn, iters: int = 1):
+    """CUDA graph of `iters` back-to-back calls of fn (after one eager call).
+    The library's kernels are enqueued on torch's current stream, which is the
+    capture stream inside torch.cuda.graph, so they are recorded like any
+    other kernel; replays skip all host-side work."""
+    fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(iters):
+            fn()
+    torch.cuda.synchronize()
+    return g
+
+
+def cuda_time_ms(torch, fn, iters: int, stream=None) -> float:
+    """Average device time of one fn() call: `iters` calls captured in a CUDA
+    graph, replayed 3 times (after one warm replay), timed with CUDA events on
+    the replay stream."""
+    g = capture(torch, fn, iters)
+    g.replay()
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(s)
+    for _ in range(3):
+        g.replay()
+    e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / (3 * iters)
+    del g
+    return ms
+
+
+# ─────────────────────────────────────────────────────────────────────────────
+# CPU oracle timing (bounded sample; the oracle is the checker and baseline)
+# ─────────────────────────────────────────────────────────────────────────────
+
+def _threads():
+    return max(1, os.cpu_count() or 1)
+
+
+def cpu_time(fn_chunk, chunks, reps=3):
+    """Median wall time of running fn_chunk over chunks on all host threads."""
+    n = _threads()
+    ts = []
+    with ThreadPoolExecutor(max_workers=n) as ex:
+        list(ex.map(fn_chunk, chunks[:1]))  # warm-up
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            list(ex.map(fn_chunk, chunks))
+            ts.append(time.perf_counter() - t0)
+    return statistics.median(ts), n
+
+
+# ─────────────────────────────────────────────────────────────────────────────
+# workloads
+# ─────────────────────────────────────────────────────────────────────────────
+
+class NF4Workload:
+    name = "nf4"
+    workload = "qlora_nf4_llama3_8b_32layers_bf16_block64_dq256"
+
+    def __init__(self, ctx):
+        self.ctx = ctx
+        torch = ctx.torch
+        import llm_quant_b200 as L
+        from llm_quant_b200.sharded import layer_block
+        self.L = L
+        self.layers = list(layer_block(NUM_LAYERS, ctx.rank, ctx.world))
+        self.weights, self.mods = [], []
+        for li in self.layers:
+            g = torch.Generator(device=ctx.dev).manual_seed(1000 + li)
+            for _, o, k in LLAMA3_8B:
+                w = (torch.randn(o, k, generator=g, device=ctx.dev) * 0.02).to(torch.bfloat16)
+                self.weights.append(w)
+                self.mods.append(L.QLoRALinear(k, o, rank=16, group_size=64).to(ctx.dev))
+        self.n_local = sum(w.numel() for w in self.weights)
+        self.n_total = NUM_LAYERS * sum(o * k for _, o, k in LLAMA3_8B)
+
+    @staticmethod
+    def bytes_for(n: int) -> float:
+        """Algorithmic bytes of pack (read bf16, write packed codes, block
+        scales, q_scales, dq_scales) + unpack (read codes, q_scales, dq_scales;
+        write bf16) for n weights."""
+        ng = n / 64
+        nd = ng / 256
+        pack = 2 * n + n / 2 + 2 * ng + 2 * ng + 2 * nd
+        unpack = n / 2 + 2 * ng + 2 * nd + 2 * n
+        return pack + unpack
+
+    def step(self):
+        for m, w in zip(self.mods, self.weights):
+            m.pack_base(w)
+            m._dequantize_base()
+
+    def launches_per_step(self):
+        return 2 * len(self.weights)
+
+    def kernels(self):
+        """Time pack and unpack alone on the largest weight of the rank."""
+        torch = self.ctx.torch
+        i = max(range(len(self.weights)), key=lambda j: self.weights[j].numel())
+        w, m = self.weights[i], self.mods[i]
+        n = w.numel()
+        ng, nd = n / 64, n / 64 / 256
+        m.pack_base(w)
+        t_pack = cuda_time_ms(torch, lambda: m.pack_base(w), 20)
+        t_unpack = cuda_time_ms(torch, lambda: m._dequantize_base(), 20)
+        b_pack = 2 * n + n / 2 + 4 * ng + 2 * nd
+        b_unpack = n / 2 + 2 * ng + 2 * nd + 2 * n
+        return {
+            "nf4_quant_kernel (pack_base)": (b_pack, t_pack, n, "weights"),
+            "nf4_dequant_kernel (_dequantize_base)": (b_unpack, t_unpack, n, "weights"),
+        }
+
+    def e2e(self, steps, graph):
+        """The step's public-API calls (pack_base / _dequantize_base, replayed
+        from the step's CUDA graph) with every weight copied in from pinned
+        host memory first and the packed codes + scales copied back to pinned
+        host memory after, every step.  One layer's seven host weights are
+        reused as the source of every layer."""
+        torch = self.ctx.torch
+        host_in = [torch.empty(w.shape, dtype=w.dtype).pin_memory() for w in self.weights[:7]]
+        for h, w in zip(host_in, self.weights[:7]):
+            h.copy_(w.cpu())
+        res = [t for m in self.mods for t in
+               (m.nf4_codes_packed, m.nf4_scales, m.dq_q_scales, m.dq_scales)]
+        outs = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in res]
+        h2d = sum(w.numel() * w.element_size() for w in self.weights)
+        d2h = sum(t.numel() * t.element_size() for t in res)
+
+        def one_step():
+            for i, w in enumerate(self.weights):
+                w.copy_(host_in[i % 7], non_blocking=True)
+            graph.replay()
+            for o, t in zip(outs, res):
+                o.copy_(t, non_blocking=True)
+
+        one_step()
+        torch.cuda.synchronize()
+        self.ctx.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            one_step()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps, h2d, d2h
+
+    def gather(self):
+        """Final gather of every rank's packed codes + scales to rank 0."""
+        torch = self.ctx.torch
+        from llm_quant_b200.sharded import flatten_bytes, gather_to_rank0
+        flat = flatten_bytes([t for m in self.mods for t in
+                              (m.nf4_codes_packed, m.nf4_scales, m.dq_q_scales, m.dq_scales)])
+        torch.cuda.synchronize()
+        self.ctx.barrier()
+        t0 = time.perf_counter()
+        gather_to_rank0(flat)
+        torch.cuda.synchronize()
+        return (time.perf_counter() - t0) * 1e3, flat.numel()
+
+    @staticmethod
+    def cpu_baseline():
+        """Oracle NF4 pack (quant + double quant) + dequant of 2 M weights
+        (rows of the 4096-wide q projection of layer 0), on all host cores."""
+        from oracle import lq_oracle as O
+        rng = np.random.default_rng(0)
+        w = O.rnd((rng.standard_normal((512, 4096)) * 0.02).astype(np.float32), "bfloat16")
+        chunks = [w[i:i + 16] for i in range(0, 512, 16)]  # 64 Ki weights = 4 dq groups each
+
+        def run(c):
+            codes, s = O.nf4_quantize(c, "bfloat16", 64)
+            q, dq = O.double_quantize(s, "bfloat16", 256)
+            O.nf4_dequantize(codes, O.double_dequantize(q, dq, "bfloat16", 256), "bfloat16", 64)
+
+        t, n = cpu_time(run, chunks)
+        b = NF4Workload.bytes_for(w.size)
+        return {"value": b / t / 1e9, "unit": "GB/s", "cores": n, "kind": "port",
+                "sample": f"oracle NF4 pack+dequant of {w.size} bf16 weights ({len(chunks)} chunks "
+                          f"on {n} threads), median of 3"}
+
+
+class GroupWorkload:
+    """fake_quantize INT4 asym group 128 of fp32 [4096, 4096] weights (weak
+    scaling: each rank quantizes its own batch of 8 matrices per step)."""
+    name = "group"
+    workload = "fake_quantize_int4_asym_g128_fp32_4096x4096_x8_per_gpu"
+
+    def __init__(self, ctx):
+        torch = ctx.torch
+        import llm_quant_b200 as L
+        self.ctx, self.L = ctx, L
+        g = torch.Generator(device=ctx.dev).manual_seed(ctx.rank)
+        self.ws = [torch.randn(4096, 4096, generator=g, device=ctx.dev) * 0.02 for _ in range(8)]
+        self.n_local = sum(w.numel() for w in self.ws)
+        self.n_total = self.n_local * ctx.world
+
+    @staticmethod
+    def bytes_for(n):
+        return 8.0 * n
+
+    def step(self):
+        for w in self.ws:
+            self.L.fake_quantize(w, 4, False, self.L.QScheme.PER_GROUP, 128)
+
+    def launches_per_step(self):
+        return len(self.ws)
+
+    def kernels(self):
+        w = self.ws[0]
+        t = cuda_time_ms(self.ctx.torch, lambda: self.L.fake_quantize(
+            w, 4, False, self.L.QScheme.PER_GROUP, 128), 50)
+        return {"group_warp_kernel (fake_quantize)": (8.0 * w.numel(), t, w.numel(), "elements")}
+
+    def e2e(self, steps, graph):
+        """fake_quantize through the public API on matrices copied in from
+        pinned host memory, results copied back, every step."""
+        torch = self.ctx.torch
+        host = torch.empty(4096, 4096).pin_memory()
+        host.copy_(self.ws[0].cpu())
+        out = torch.empty(4096, 4096).pin_memory()
+        dev = torch.empty_like(self.ws[0])
+
+        def one():
+            for _ in self.ws:
+                dev.copy_(host, non_blocking=True)
+                y = self.L.fake_quantize(dev, 4, False, self.L.QScheme.PER_GROUP, 128)
+                out.copy_(y, non_blocking=True)
+
+        one()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            one()
+        e1.record()
+        torch.cuda.synchronize()
+        nb = host.numel() * 4 * len(self.ws)
+        return e0.elapsed_time(e1) / steps, nb, nb
+
+    def gather(self):
+        return 0.0, 0
+
+    @staticmethod
+    def cpu_baseline():
+        from oracle import lq_oracle as O
+        rng = np.random.default_rng(0)
+        w = (rng.standard_normal((1024, 4096)) * 0.02).astype(np.float32)
+        chunks = [w[i:i + 32] for i in range(0, 1024, 32)]
+        t, n = cpu_time(lambda c: O.fake_quantize(c, "float32", 4, False, "per_group", 128), chunks)
+        return {"value": 8.0 * w.size / t / 1e9, "unit": "GB/s", "cores": n, "kind": "port",
+                "sample": f"oracle fake_quantize of fp32 [1024, 4096] ({len(chunks)} chunks on "
+                          f"{n} threads), median of 3"}
+
+
+class RotQuantWorkload:
+    """QuaRot activation path: Hadamard (d = 4096) + per-token INT4 sym fake
+    quant of bf16 [8192, 4096] activations with 1% outlier channels x50,
+    fused in one kernel; 4 distinct batches rotate so inputs exceed L2
+    (weak scaling: each rank its own activations)."""
+    name = "rotquant"
+    workload = "quarot_fht4096_pertoken_int4_bf16_8192x4096"
+
+    def __init__(self, ctx):
+        torch = ctx.torch
+        import llm_quant_b200 as L
+        self.ctx, self.L = ctx, L
+        g = torch.Generator(device=ctx.dev).manual_seed(ctx.rank)
+        self.xs = []
+        for _ in range(4):
+            a = torch.randn(8192, 4096, generator=g, device=ctx.dev)
+            idx = torch.randperm(4096, generator=g, device=ctx.dev)[:41]
+            a[:, idx] *= 50
+            self.xs.append(a.to(torch.bfloat16))
+        self.n_local = self.xs[0].numel()
+        self.n_total = self.n_local * ctx.world
+        self.i = 0
+
+    @staticmethod
+    def bytes_for(n):
+        return 4.0 * n
+
+    def step(self):
+        self.L.hadamard_fake_quantize(self.xs[self.i % 4], 4, True)
+        self.i += 1
+
+    def launches_per_step(self):
+        return 1
+
+    def kernels(self):
+        c = [0]
+
+        def f():
+            self.L.hadamard_fake_quantize(self.xs[c[0] % 4], 4, True)
+            c[0] += 1
+        t = cuda_time_ms(self.ctx.torch, f, 40)
+        n = self.xs[0].numel()
+        return {"fht_block_kernel (hadamard_fake_quantize)": (4.0 * n, t, n, "elements")}
+
+    def e2e(self, steps, graph):
+        torch = self.ctx.torch
+        host = torch.empty(8192, 4096, dtype=torch.bfloat16).pin_memory()
+        host.copy_(self.xs[0].cpu())
+        out = torch.empty_like(host).pin_memory()
+        dev = torch.empty_like(self.xs[0])
+
+        def one():
+            dev.copy_(host, non_blocking=True)
+            out.copy_(self.L.hadamard_fake_quantize(dev, 4, True), non_blocking=True)
+
+        one()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            one()
+        e1.record()
+        torch.cuda.synchronize()
+        nb = host.numel() * 2
+        return e0.elapsed_time(e1) / steps, nb, nb
+
+    def gather(self):
+        return 0.0, 0
+
+    @staticmethod
+    def cpu_baseline():
+        from oracle import lq_oracle as O
+        rng = np.random.default_rng(0)
+        a = O.rnd(rng.standard_normal((256, 4096)).astype(np.float32), "bfloat16")
+        chunks = [a[i:i + 8] for i in range(0, 256, 8)]
+
+        def run(c):
+            h = O.fast_hadamard_transform(c, "bfloat16")
+            O.fake_quantize(h, "bfloat16", 4, True, "per_channel")
+
+        t, n = cpu_time(run, chunks)
+        return {"value": 4.0 * a.size / t / 1e9, "unit": "GB/s", "cores": n, "kind": "port",
+                "sample": f"oracle Hadamard + per-token INT4 of bf16 [256, 4096] ({n} threads), "
+                          "median of 3"}
+
+
+class KVWorkload:
+    """KV-cache quantization: 32 layers x K, V bf16 [16, 8, 8192, 128], K
+    per-channel INT8, V per-token INT4, 16 QuantizedKVCache.update calls of
+    512 tokens per layer, each returning the full fp32 K and V (the
+    reference's contract); layers split across ranks (strong scaling)."""
+    name = "kv"
+    workload = "kv_cache_32layers_bf16_16x8x8192x128_K_perchan_int8_V_pertoken_int4_16x512"
+    B, H, D, C, U = 16, 8, 128, 512, 16
+
+    def __init__(self, ctx):
+        torch = ctx.torch
+        import llm_quant_b200 as L
+        from llm_quant_b200.sharded import layer_block
+        self.ctx, self.L = ctx, L
+        self.layers = list(layer_block(NUM_LAYERS, ctx.rank, ctx.world))
+        # inputs of one layer (16 chunks of K and V) are generated once and
+        # reused by every layer of the rank: 2 x 256 MB
+        g = torch.Generator(device=ctx.dev).manual_seed(ctx.rank)
+        self.k = []
+        self.v = []
+        for _ in range(self.U):
+            k = torch.randn(self.B, self.H, self.C, self.D, generator=g, device=ctx.dev)
+            k[..., :4] *= 20
+            self.k.append(k.to(torch.bfloat16))
+            self.v.append(torch.randn(self.B, self.H, self.C, self.D, generator=g,
+                                      device=ctx.dev).to(torch.bfloat16))
+        E = self.B * self.H * self.C * self.U
+        self.E = E
+        self.n_local = len(self.layers)
+        self.n_total = NUM_LAYERS
+
+    def bytes_per_layer(self):
+        c = self.E // self.U
+        # per tensor: 16 x (read 2c + write 1c codes) + sum_i (read i*c codes + write 4*i*c)
+        return 2 * (self.U * 3 * c + sum(i * c + 4 * i * c for i in range(1, self.U + 1)))
+
+    def bytes_for(self, n_layers):
+        return self.bytes_per_layer() * n_layers
+
+    def _layer(self):
+        L = self.L
+        cache = L.QuantizedKVCache(1, L.PerChannelKVCacheQuantizer(8),
+                                   value_quantizer=L.PerTokenKVCacheQuantizer(4),
+                                   max_seq_len=self.C * self.U)
+        for j in range(self.U):
+            cache.update(0, self.k[j], self.v[j])
+
+    def step(self):
+        for _ in self.layers:
+            self._layer()
+
+    def launches_per_step(self):
+        return len(self.layers) * self.U * 4
+
+    def kernels(self):
+        torch = self.ctx.torch
+        L = self.L
+        cache = L.QuantizedKVCache(1, L.PerChannelKVCacheQuantizer(8),
+                                   value_quantizer=L.PerTokenKVCacheQuantizer(4),
+                                   max_seq_len=self.C * self.U)
+        for j in range(self.U):
+            cache.update(0, self.k[j], self.v[j])
+        side = cache._sides[0][0]
+        t = cuda_time_ms(torch, side.dequantize, 10)
+        n = side.T * self.B * self.H * self.D
+        return {"kv_dequant_kernel (full-cache fp32 read-out)": (5.0 * n, t, n, "elements")}
+
+    def e2e(self, steps, graph):
+        torch = self.ctx.torch
+        L = self.L
+        hk = [k.cpu().pin_memory() for k in self.k]
+        hv = [v.cpu().pin_memory() for v in self.v]
+        dk, dv = torch.empty_like(self.k[0]), torch.empty_like(self.v[0])
+        outk = torch.empty(self.B, self.H, self.C * self.U, self.D).pin_memory()
+        outv = torch.empty_like(outk).pin_memory()
+
+        def one():
+            for _ in self.layers:
+                cache = L.QuantizedKVCache(1, L.PerChannelKVCacheQuantizer(8),
+                                           value_quantizer=L.PerTokenKVCacheQuantizer(4),
+                                           max_seq_len=self.C * self.U)
+                for j in range(self.U):
+                    dk.copy_(hk[j], non_blocking=True)
+                    dv.copy_(hv[j], non_blocking=True)
+                    fk, fv = cache.update(0, dk, dv)
+                outk.copy_(fk, non_blocking=True)
+                outv.copy_(fv, non_blocking=True)
+
+        one()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            one()
+        e1.record()
+        torch.cuda.synchronize()
+        h2d = len(self.layers) * 2 * self.E * 2
+        d2h = len(self.layers) * 2 * self.E * 4
+        return e0.elapsed_time(e1) / steps, h2d, d2h
+
+    def gather(self):
+        return 0.0, 0
+
+    @staticmethod
+    def cpu_baseline():
+        from oracle import lq_oracle as O
+        rng = np.random.default_rng(0)
+        kq = dict(n_bits=8, symmetric=True, granularity="per_channel")
+        vq = dict(n_bits=4, symmetric=True, granularity="per_token")
+        chunks = []
+        for b in range(8):  # 8 (batch*head) slices x 16 updates of 512 tokens
+            ks = [O.rnd(rng.standard_normal((1, 1, 512, 128)).astype(np.float32), "bfloat16")
+                  for _ in range(16)]
+            vs = [O.rnd(rng.standard_normal((1, 1, 512, 128)).astype(np.float32), "bfloat16")
+                  for _ in range(16)]
+            chunks.append((ks, vs))
+
+        def run(c):
+            cache = O.QuantizedKVCacheOracle(1, "bfloat16", kq, vq)
+            for k, v in zip(*c):
+                cache.update(0, k, v)
+
+        t, n = cpu_time(run, chunks)
+        c = 512 * 128 * 8
+        b = 2 * (16 * 3 * c + sum(i * c + 4 * i * c for i in range(1, 17)))
+        return {"value": b / t / 1e9, "unit": "GB/s", "cores": n, "kind": "port",
+                "sample": f"oracle QuantizedKVCache, 8 (batch, head) slices x 16 updates of 512 "
+                          f"tokens, head_dim 128 ({n} threads), median of 3"}
+
+
+WORKLOADS = {"nf4": NF4Workload, "group": GroupWorkload, "rotquant": RotQuantWorkload,
+             "kv": KVWorkload}
+
+
+# ─────────────────────────────────────────────────────────────────────────────
+
+def run_reference(args):
+    """--impl reference: the CPU oracle (restatement of the reference's
+    algorithm) on the host cores, bounded sample per step; rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    W = WORKLOADS[args.workload]
+    for _ in range(args.warmup):
+        W.cpu_baseline()
+    vals, ts = [], []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        cb = W.cpu_baseline()
+        ts.append(time.perf_counter() - t0)
+        vals.append(cb["value"])
+    v = statistics.median(vals)
+    cb["value"] = v
+    line = {"metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * statistics.median(ts), "higher_is_better": True,
+            "scaling": "strong" if args.workload in ("nf4", "kv") else "weak",
+            "vs_baseline": None, "dtype": "bf16" if args.workload != "group" else "f32",
+            "data": "synthetic (seeded)", "impl": "reference",
+            "config": {"workload": W.workload, "sample": cb["sample"]},
+            "cpu_baseline": cb,
+            "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+    return 0
+
+
+def run_ours(args):
+    ctx = Ctx(args.gpus)
+    torch = ctx.torch
+    from llm_quant_b200 import _C
+    hbm, tflops, peak_kind = peaks()
+    W = WORKLOADS[args.workload](ctx)
+    torch.cuda.synchronize()
+    # one step captured as a CUDA graph; warm-up and timed steps replay it
+    l0 = _C.launch_count()
+    graph = capture(torch, W.step, 1)  # one eager call + one captured call
+    launches_per_step = (_C.launch_count() - l0) // 2
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    ctx.barrier()
+    clocks = ClockSampler(ctx.local == 0)
+    time.sleep(0.2 if ctx.local == 0 else 0.0)
+    ctx.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ctx.barrier()
+    ck = clocks.stop(set(range(ctx.world))) if ctx.local == 0 else None
+    ms = ctx.max(e0.elapsed_time(e1) / args.steps)
+    total_bytes = W.bytes_for(W.n_total)
+    value = total_bytes / (ms * 1e-3) / 1e9
+    launches = launches_per_step * args.steps
+    launches_all = int(ctx.sum(float(launches)))
+
+    # dominant kernel, timed alone
+    kern = W.kernels()
+    name, (kb, kms, units, unit_name) = max(kern.items(), key=lambda kv: kv[1][1])
+    achieved = kb / (kms * 1e-3) / 1e9
+    traffic = NCU_TRAFFIC.get(W.name)
+    roofline = {"bound": "hbm", "kernel": name, "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                "frac": achieved / hbm, "peak_kind": peak_kind,
+                "traffic": traffic if traffic is None else traffic * units,
+                "algorithmic_bytes_per_launch": kb, "launch_ms": kms,
+                "units_per_launch": f"{units} {unit_name}"}
+    kernels = {k: {"ms": v[1], "GB/s": v[0] / (v[1] * 1e-3) / 1e9,
+                   "frac_of_peak": v[0] / (v[1] * 1e-3) / 1e9 / hbm} for k, v in kern.items()}
+
+    e2e_ms, h2d, d2h = W.e2e(max(1, args.e2e_steps), graph)
+    e2e_ms = ctx.max(e2e_ms)
+    e2e = {"value": total_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
+           "h2d_bytes_per_step": int(ctx.sum(h2d)), "d2h_bytes_per_step": int(ctx.sum(d2h)),
+           "ms_per_step": e2e_ms}
+    gather_ms, gather_bytes = W.gather()
+    gather_ms = ctx.max(gather_ms)
+
+    cpu = None
+    if ctx.rank == 0 and ctx.world == 1 and not args.no_cpu:
+        cpu = W.cpu_baseline()
+    if ctx.rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": ctx.world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True,
+            "scaling": "strong" if W.name in ("nf4", "kv") else "weak",
+            "vs_baseline": None,
+            "dtype": "f32" if W.name == "group" else "bf16",
+            "data": "synthetic (seeded torch.randn on the device)",
+            "config": {"workload": W.workload, "parallelism": f"layer-shard x{ctx.world}"
+                       if W.name in ("nf4", "kv") else f"independent x{ctx.world}",
+                       "l2": "inputs larger than L2 (no flush)",
+                       "launch": "one CUDA graph per step",
+                       "algorithmic_bytes_per_step": total_bytes},
+            "roofline": roofline,
+            "kernels": kernels,
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": launches_all,
+            "clocks": ck,
+            "gather": {"ms": gather_ms, "bytes_rank0": gather_bytes} if ctx.world > 1 else None,
+        }
+        print(json.dumps(line))
+    ctx.close()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="nf4")
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)  # at least 3 warm-up steps
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,389 @@
+// lq_group.cu -- group / row quantization (min/max or absmax per group,
+// scale + zero point, round-half-even, clamp, fake-quant or integer codes).
+//
+// Layout: x is [rows, cols] row-major; every row is cut into groups of G
+// columns, the last one zero-padded (core/quantizer.py:89-95).  One "team" of
+// threads owns one group at a time and keeps it in registers, so x is read
+// from HBM exactly once and the output written once:
+//   * warp teams (1..32 lanes) for groups up to 32 x NVT x 16 bytes,
+//   * block teams (up to 1024 threads) for longer groups (per-token rows),
+//   * a streaming block path (two passes, the second from L2) beyond that.
+// The vector path moves 16 bytes per load/store (ld.global.nc.v4); it needs
+// G*sizeof(T) % 16 == 0, cols % G == 0 and 16-byte aligned pointers.
+#include "lq_common.cuh"
+
+namespace lq {
+namespace {
+
+enum { MODE_QPARAMS = 0, MODE_FAKE = 1, MODE_CODES = 2 };
+
+template <typename OutT, typename T> struct Store;
+template <typename T> struct Store<int8_t, T> {
+  __device__ __forceinline__ static int8_t cv(float v) { return (int8_t)tcast_i32(v); }
+};
+template <typename T> struct Store<int16_t, T> {
+  __device__ __forceinline__ static int16_t cv(float v) { return (int16_t)tcast_i32(v); }
+};
+template <typename T> struct Store<T, T> {
+  __device__ __forceinline__ static T cv(float v) { return Ty<T>::from_f(v); }
+};
+
+// Store V consecutive outputs (V * sizeof(OutT) bytes, naturally aligned).
+template <typename OutT, typename T, int V>
+__device__ __forceinline__ void store_vec(OutT* p, const float* vals) {
+  constexpr int BYTES = V * sizeof(OutT);
+  union {
+    OutT o[V];
+    uint32_t w[(BYTES + 3) / 4];
+    uint16_t h;
+    uint8_t b;
+  } u;
+#pragma unroll
+  for (int i = 0; i < V; ++i) u.o[i] = Store<OutT, T>::cv(vals[i]);
+  if constexpr (BYTES == 16) {
+    st_v4(p, make_uint4(u.w[0], u.w[1], u.w[2], u.w[3]));
+  } else if constexpr (BYTES == 8) {
+    *reinterpret_cast<uint2*>(p) = make_uint2(u.w[0], u.w[1]);
+  } else if constexpr (BYTES == 4) {
+    *reinterpret_cast<uint32_t*>(p) = u.w[0];
+  } else if constexpr (BYTES == 2) {
+    *reinterpret_cast<uint16_t*>(p) = u.h;
+  } else {
+    *reinterpret_cast<uint8_t*>(p) = u.b;
+  }
+}
+
+struct GroupArgs {
+  int64_t rows, cols, G, groups_per_row, total_groups;
+  float qmin, qmax, lo;
+  int sym;
+  // Output row remapping (KV append into a cache with spare capacity):
+  // input row r = (p, t) with t = r % rpp lands on output row
+  // p * opitch + ooff + t, and its scales on row p * spitch + soff + t.
+  int64_t rpp, opitch, ooff, spitch, soff;
+  __device__ __forceinline__ int64_t out_row(int64_t r) const {
+    return (r / rpp) * opitch + ooff + r % rpp;
+  }
+  __device__ __forceinline__ int64_t sc_index(int64_t g) const {
+    const int64_t r = g / groups_per_row;
+    return ((r / rpp) * spitch + soff + r % rpp) * groups_per_row + g % groups_per_row;
+  }
+};
+
+// Per-element output of the fused modes.
+template <typename T, int MODE>
+__device__ __forceinline__ float apply_q(float v, float scale, float zp, float qmin, float qmax) {
+  float t = tadd<T>(tdiv<T>(v, scale), zp);
+  if constexpr (MODE == MODE_FAKE) {
+    float q = tclamp(tste(t), qmin, qmax);
+    return tmul<T>(tsub<T>(q, zp), scale);
+  } else {
+    return tclamp(trint(t), qmin, qmax);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Register-resident group processing shared by warp teams and block teams.
+// Slot k of thread t holds elements e = (k*TPS + t)*V + i (VEC) or
+// e = k*TPS + t (scalar, V == 1).
+// ---------------------------------------------------------------------------
+template <typename T, int NVT, bool VEC>
+struct Tile {
+  static constexpr int V = VEC ? (16 / sizeof(T)) : 1;
+  float v[NVT * V];
+  unsigned inb;  // bit k: slot k belongs to the group (e < G)
+
+  __device__ __forceinline__ void load(const T* __restrict__ x, int64_t row, int64_t gcol0,
+                                       const GroupArgs& a, int t, int tps) {
+    inb = 0;
+    const T* base = x + row * a.cols + gcol0;
+#pragma unroll
+    for (int k = 0; k < NVT; ++k) {
+      int64_t e = (int64_t)(k * tps + t) * V;
+      bool in = e < a.G;
+      inb |= (in ? 1u : 0u) << k;
+      if constexpr (VEC) {
+        Vec16<T> u;
+        if (in) u.u = ld_nc_v4(base + e);
+        else u.u = make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int i = 0; i < V; ++i) v[k * V + i] = Ty<T>::to_f(u.v[i]);
+      } else {
+        // columns past `cols` are the zero padding of the last group
+        bool valid = in && (gcol0 + e < a.cols);
+        v[k] = valid ? Ty<T>::to_f(base[e]) : 0.0f;
+      }
+    }
+  }
+
+  __device__ __forceinline__ void reduce_local(MinMax& r, bool sym) const {
+    r.init();
+#pragma unroll
+    for (int k = 0; k < NVT; ++k) {
+      if (inb & (1u << k)) {
+#pragma unroll
+        for (int i = 0; i < V; ++i) r.add(sym ? fabsf(v[k * V + i]) : v[k * V + i]);
+      }
+    }
+  }
+
+  template <int MODE, typename OutT>
+  __device__ __forceinline__ void emit(OutT* __restrict__ out, int64_t row, int64_t gcol0,
+                                       const GroupArgs& a, int t, int tps, float scale,
+                                       float zp) {
+    OutT* base = out + a.out_row(row) * a.cols + gcol0;
+#pragma unroll
+    for (int k = 0; k < NVT; ++k) {
+      if (!(inb & (1u << k))) continue;
+      int64_t e = (int64_t)(k * tps + t) * V;
+      float o[V];
+#pragma unroll
+      for (int i = 0; i < V; ++i) o[i] = apply_q<T, MODE>(v[k * V + i], scale, zp, a.qmin, a.qmax);
+      if constexpr (VEC) {
+        store_vec<OutT, T, V>(base + e, o);
+      } else {
+        if (gcol0 + e < a.cols) base[e] = Store<OutT, T>::cv(o[0]);
+      }
+    }
+  }
+};
+
+// Warp teams: `tps` lanes (power of two <= 32) per group.
+template <typename T, int MODE, typename OutT, int NVT, bool VEC>
+__global__ void __launch_bounds__(256) group_warp_kernel(const T* __restrict__ x, GroupArgs a,
+                                                         int tps, OutT* __restrict__ out,
+                                                         T* __restrict__ scale_out,
+                                                         T* __restrict__ zp_out) {
+  const int lane = threadIdx.x & 31;
+  const int t = lane & (tps - 1);
+  const int64_t team = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / tps;
+  const int64_t nteams = ((int64_t)gridDim.x * blockDim.x) / tps;
+  // all lanes of a warp iterate the same number of times (shuffles below)
+  const int64_t warp_team0 = team - (lane / tps);
+  for (int64_t g0 = warp_team0; g0 < a.total_groups; g0 += nteams) {
+    const int64_t g = g0 + lane / tps;
+    const bool live = g < a.total_groups;
+    const int64_t row = live ? g / a.groups_per_row : 0;
+    const int64_t gcol0 = live ? (g % a.groups_per_row) * a.G : 0;
+    Tile<T, NVT, VEC> tile;
+    if (live) tile.load(x, row, gcol0, a, t, tps);
+    else tile.inb = 0;
+    MinMax r;
+    tile.reduce_local(r, a.sym);
+    for (int m = 1; m < tps; m <<= 1) r.shfl_xor_merge(m);
+    if (!live) continue;
+    float scale, zp;
+    qparams_from<T>(r, a.sym, a.qmin, a.qmax, a.lo, scale, zp);
+    if (t == 0 && scale_out) {
+      const int64_t si = a.sc_index(g);
+      scale_out[si] = Ty<T>::from_f(scale);
+      zp_out[si] = Ty<T>::from_f(zp);
+    }
+    if constexpr (MODE != MODE_QPARAMS) tile.template emit<MODE>(out, row, gcol0, a, t, tps, scale, zp);
+  }
+}
+
+// Block-wide NaN-aware min/max reduction; result broadcast to all threads.
+__device__ __forceinline__ MinMax block_reduce(MinMax r, MinMax* sm) {
+  for (int m = 16; m >= 1; m >>= 1) r.shfl_xor_merge(m);
+  const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  __syncthreads();  // sm may still be read from the previous group
+  if ((threadIdx.x & 31) == 0) sm[w] = r;
+  __syncthreads();
+  MinMax t = sm[0];
+  for (int i = 1; i < nw; ++i) t.merge(sm[i]);
+  return t;
+}
+
+// Block teams: one block (blockDim.x threads) per group.
+template <typename T, int MODE, typename OutT, int NVT, bool VEC>
+__global__ void __launch_bounds__(1024) group_block_kernel(const T* __restrict__ x, GroupArgs a,
+                                                           OutT* __restrict__ out,
+                                                           T* __restrict__ scale_out,
+                                                           T* __restrict__ zp_out) {
+  __shared__ MinMax sm[32];
+  const int t = threadIdx.x, tps = blockDim.x;
+  for (int64_t g = blockIdx.x; g < a.total_groups; g += gridDim.x) {
+    const int64_t row = g / a.groups_per_row;
+    const int64_t gcol0 = (g % a.groups_per_row) * a.G;
+    Tile<T, NVT, VEC> tile;
+    tile.load(x, row, gcol0, a, t, tps);
+    MinMax r;
+    tile.reduce_local(r, a.sym);
+    r = block_reduce(r, sm);
+    float scale, zp;
+    qparams_from<T>(r, a.sym, a.qmin, a.qmax, a.lo, scale, zp);
+    if (t == 0 && scale_out) {
+      const int64_t si = a.sc_index(g);
+      scale_out[si] = Ty<T>::from_f(scale);
+      zp_out[si] = Ty<T>::from_f(zp);
+    }
+    if constexpr (MODE != MODE_QPARAMS) tile.template emit<MODE>(out, row, gcol0, a, t, tps, scale, zp);
+  }
+}
+
+// Streaming block path for groups too long for registers: pass 1 reduces,
+// pass 2 re-reads (from L2) and writes.  Scalar, coalesced.
+template <typename T, int MODE, typename OutT>
+__global__ void __launch_bounds__(1024) group_stream_kernel(const T* __restrict__ x, GroupArgs a,
+                                                            OutT* __restrict__ out,
+                                                            T* __restrict__ scale_out,
+                                                            T* __restrict__ zp_out) {
+  __shared__ MinMax sm[32];
+  for (int64_t g = blockIdx.x; g < a.total_groups; g += gridDim.x) {
+    const int64_t row = g / a.groups_per_row;
+    const int64_t gcol0 = (g % a.groups_per_row) * a.G;
+    const T* base = x + row * a.cols + gcol0;
+    MinMax r;
+    r.init();
+    for (int64_t e = threadIdx.x; e < a.G; e += blockDim.x) {
+      float v = (gcol0 + e < a.cols) ? Ty<T>::to_f(base[e]) : 0.0f;
+      r.add(a.sym ? fabsf(v) : v);
+    }
+    r = block_reduce(r, sm);
+    float scale, zp;
+    qparams_from<T>(r, a.sym, a.qmin, a.qmax, a.lo, scale, zp);
+    if (threadIdx.x == 0 && scale_out) {
+      const int64_t si = a.sc_index(g);
+      scale_out[si] = Ty<T>::from_f(scale);
+      zp_out[si] = Ty<T>::from_f(zp);
+    }
+    if constexpr (MODE != MODE_QPARAMS) {
+      OutT* ob = out + a.out_row(row) * a.cols + gcol0;
+      for (int64_t e = threadIdx.x; e < a.G && gcol0 + e < a.cols; e += blockDim.x)
+        ob[e] = Store<OutT, T>::cv(apply_q<T, MODE>(Ty<T>::to_f(base[e]), scale, zp, a.qmin, a.qmax));
+    }
+  }
+}
+
+int grid_for(int64_t units, int per_block) {
+  int64_t want = (units + per_block - 1) / per_block;
+  int64_t cap = (int64_t)num_sms() * 16;
+  return (int)(want < cap ? (want > 0 ? want : 1) : cap);
+}
+
+template <typename T, int MODE, typename OutT, int NVT, bool VEC>
+int launch_warp(const T* x, const GroupArgs& a, int tps, OutT* out, T* s, T* z, cudaStream_t st) {
+  const int threads = 256;
+  int grid = grid_for(a.total_groups * tps, threads);
+  group_warp_kernel<T, MODE, OutT, NVT, VEC><<<grid, threads, 0, st>>>(x, a, tps, out, s, z);
+  return launched("group_warp_kernel");
+}
+
+template <typename T, int MODE, typename OutT, int NVT, bool VEC>
+int launch_block(const T* x, const GroupArgs& a, int threads, OutT* out, T* s, T* z,
+                 cudaStream_t st) {
+  int grid = grid_for(a.total_groups, 1);
+  group_block_kernel<T, MODE, OutT, NVT, VEC><<<grid, threads, 0, st>>>(x, a, out, s, z);
+  return launched("group_block_kernel");
+}
+
+// Pick a team shape for a group of G elements and launch.
+template <typename T, int MODE, typename OutT>
+int dispatch(const T* x, const GroupArgs& a, OutT* out, T* s, T* z, bool vec_ok,
+             cudaStream_t st) {
+  constexpr int V = 16 / sizeof(T);
+  const int64_t G = a.G;
+  if (vec_ok) {
+    const int64_t nv = G / V;  // vectors per group
+    if (nv <= 32) {
+      int tps = 1;
+      while (tps < nv) tps <<= 1;
+      return launch_warp<T, MODE, OutT, 1, true>(x, a, tps, out, s, z, st);
+    }
+    if (nv <= 64) return launch_warp<T, MODE, OutT, 2, true>(x, a, 32, out, s, z, st);
+    if (nv <= 128) return launch_warp<T, MODE, OutT, 4, true>(x, a, 32, out, s, z, st);
+    // block teams: up to 1024 threads x 2 vectors in registers
+    for (int threads = 128; threads <= 1024; threads *= 2) {
+      if (nv <= (int64_t)threads * 2) {
+        if (nv <= threads) return launch_block<T, MODE, OutT, 1, true>(x, a, threads, out, s, z, st);
+        return launch_block<T, MODE, OutT, 2, true>(x, a, threads, out, s, z, st);
+      }
+    }
+  } else {
+    if (G <= 32) {
+      int tps = 1;
+      while (tps < G) tps <<= 1;
+      return launch_warp<T, MODE, OutT, 1, false>(x, a, tps, out, s, z, st);
+    }
+    if (G <= 128) return launch_warp<T, MODE, OutT, 4, false>(x, a, 32, out, s, z, st);
+    if (G <= 512) return launch_warp<T, MODE, OutT, 16, false>(x, a, 32, out, s, z, st);
+    if (G <= 8192) return launch_block<T, MODE, OutT, 8, false>(x, a, 1024, out, s, z, st);
+  }
+  int grid = grid_for(a.total_groups, 1);
+  group_stream_kernel<T, MODE, OutT><<<grid, 1024, 0, st>>>(x, a, out, s, z);
+  return launched("group_stream_kernel");
+}
+
+template <typename T>
+int group_quant_t(const void* xv, int64_t rows, int64_t cols, int64_t G, int n_bits, int sym,
+                  int mode, void* out, int out_dtype, void* scale, void* zp, cudaStream_t st,
+                  int64_t rpp, int64_t opitch, int64_t ooff, int64_t spitch, int64_t soff) {
+  const T* x = static_cast<const T*>(xv);
+  GroupArgs a;
+  a.rpp = rpp;
+  a.opitch = opitch;
+  a.ooff = ooff;
+  a.spitch = spitch;
+  a.soff = soff;
+  a.rows = rows;
+  a.cols = cols;
+  a.G = G;
+  a.groups_per_row = (cols + G - 1) / G;
+  a.total_groups = rows * a.groups_per_row;
+  a.qmin = (float)qmin_of(n_bits, sym);
+  a.qmax = (float)qmax_of(n_bits, sym);
+  a.lo = lo_clamp_value<T>();
+  a.sym = sym;
+  constexpr int V = 16 / sizeof(T);
+  int osz = mode == MODE_QPARAMS ? 1 : dtype_size(out_dtype);
+  bool vec_ok = (G % V == 0) && (cols % G == 0) && aligned16(x) &&
+                (mode == MODE_QPARAMS || (reinterpret_cast<uintptr_t>(out) % (V * osz) == 0));
+  T* s = static_cast<T*>(scale);
+  T* z = static_cast<T*>(zp);
+  if (mode == MODE_QPARAMS) return dispatch<T, MODE_QPARAMS, T>(x, a, nullptr, s, z, vec_ok, st);
+  if (mode == MODE_FAKE) {
+    LQ_REQUIRE(out_dtype == Ty<T>::code, LQ_EDTYPE, "fake-quant output dtype must equal input dtype");
+    return dispatch<T, MODE_FAKE, T>(x, a, static_cast<T*>(out), s, z, vec_ok, st);
+  }
+  if (out_dtype == LQ_I8) return dispatch<T, MODE_CODES, int8_t>(x, a, static_cast<int8_t*>(out), s, z, vec_ok, st);
+  if (out_dtype == LQ_I16) return dispatch<T, MODE_CODES, int16_t>(x, a, static_cast<int16_t*>(out), s, z, vec_ok, st);
+  if (out_dtype == Ty<T>::code) return dispatch<T, MODE_CODES, T>(x, a, static_cast<T*>(out), s, z, vec_ok, st);
+  set_error("unsupported code dtype %d", out_dtype);
+  return LQ_EDTYPE;
+}
+
+}  // namespace
+
+// Shared with lq_kv.cu (KV append into capacity storage).
+int group_quant_remap(const void* x, int x_dtype, int64_t rows, int64_t cols, int64_t group,
+                      int n_bits, int symmetric, int mode, void* out, int out_dtype, void* scale,
+                      void* zero_point, void* stream, int64_t rpp, int64_t opitch, int64_t ooff,
+                      int64_t spitch, int64_t soff) {
+  cudaStream_t st = as_stream(stream);
+  switch (x_dtype) {
+    case LQ_F32: return group_quant_t<float>(x, rows, cols, group, n_bits, symmetric, mode, out, out_dtype, scale, zero_point, st, rpp, opitch, ooff, spitch, soff);
+    case LQ_F16: return group_quant_t<__half>(x, rows, cols, group, n_bits, symmetric, mode, out, out_dtype, scale, zero_point, st, rpp, opitch, ooff, spitch, soff);
+    case LQ_BF16: return group_quant_t<__nv_bfloat16>(x, rows, cols, group, n_bits, symmetric, mode, out, out_dtype, scale, zero_point, st, rpp, opitch, ooff, spitch, soff);
+    default: set_error("unsupported x dtype %d", x_dtype); return LQ_EDTYPE;
+  }
+}
+
+}  // namespace lq
+
+extern "C" int lq_group_quant(const void* x, int x_dtype, int64_t rows, int64_t cols,
+                              int64_t group, int n_bits, int symmetric, int mode, void* out,
+                              int out_dtype, void* scale, void* zero_point, void* stream) {
+  using namespace lq;
+  LQ_REQUIRE(rows >= 0 && cols >= 0 && group >= 1, LQ_EINVAL, "bad shape rows=%lld cols=%lld group=%lld",
+             (long long)rows, (long long)cols, (long long)group);
+  LQ_REQUIRE(n_bits >= 1 && n_bits <= 16, LQ_EINVAL, "n_bits %d out of range", n_bits);
+  LQ_REQUIRE(mode >= 0 && mode <= 2, LQ_EINVAL, "bad mode %d", mode);
+  if (rows == 0 || cols == 0) return LQ_OK;
+  LQ_REQUIRE(x, LQ_EINVAL, "x is NULL");
+  LQ_REQUIRE(mode == LQ_MODE_QPARAMS || out, LQ_EINVAL, "out is NULL");
+  LQ_REQUIRE((scale == nullptr) == (zero_point == nullptr), LQ_EINVAL, "scale and zero_point must both be given");
+  LQ_REQUIRE(mode != LQ_MODE_QPARAMS || scale, LQ_EINVAL, "QPARAMS mode needs scale/zero_point");
+  return lq::group_quant_remap(x, x_dtype, rows, cols, group, n_bits, symmetric, mode, out,
+                               out_dtype, scale, zero_point, stream, rows, rows, 0, rows, 0);
+}

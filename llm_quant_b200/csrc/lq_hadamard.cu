@@ -1,0 +1,344 @@
+// lq_hadamard.cu -- Walsh-Hadamard transform along the last dim, optionally
+// fused with per-row fake quantization.
+//
+// The reference computes x @ hadamard_matrix(d, x.dtype) as a dense d x d
+// matmul (core/rotation.py:130-147), O(d^2) per row.  Here it is the
+// O(d log d) butterfly of the same Sylvester matrix: for h = 1, 2, 4, ...
+// every index pair (i, i + h) with bit h clear becomes (a + b, a - b), then
+// the result is scaled by the matrix entry round_T(1 / sqrt(d))
+// (core/rotation.py:30-43), once, and rounded to T.
+//
+// Row mapping: a team of NT = d / E threads owns one row, thread t holding
+// elements [t*E, t*E + E) (contiguous 16/32-byte vector loads).  Stages
+// h < E run in registers, stages E <= h < 32E through warp shuffles, and the
+// remaining log2(NT/32) stages after one shared-memory transpose in which
+// every thread takes the NT/32 elements that differ only in the warp bits.
+#include "lq_common.cuh"
+
+namespace lq {
+namespace {
+
+struct FhtArgs {
+  int64_t rows;
+  int d, E, log2d;
+  float entry;  // round_T(1 / sqrt(d))
+  // fused quantization
+  float qmin, qmax, lo;
+  int sym;
+};
+
+template <typename T, int E>
+__device__ __forceinline__ void load_row_chunk(const T* __restrict__ src, float* v, bool vec) {
+  if (vec) {
+    constexpr int V = 16 / sizeof(T);
+#pragma unroll
+    for (int k = 0; k < E / V; ++k) {
+      Vec16<T> u;
+      u.u = ld_nc_v4(src + k * V);
+#pragma unroll
+      for (int i = 0; i < V; ++i) v[k * V + i] = Ty<T>::to_f(u.v[i]);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < E; ++i) v[i] = Ty<T>::to_f(src[i]);
+  }
+}
+
+template <typename T, int E>
+__device__ __forceinline__ void store_row_chunk(T* __restrict__ dst, const float* v, bool vec) {
+  if (vec) {
+    constexpr int V = 16 / sizeof(T);
+#pragma unroll
+    for (int k = 0; k < E / V; ++k) {
+      Vec16<T> u;
+#pragma unroll
+      for (int i = 0; i < V; ++i) u.v[i] = Ty<T>::from_f(v[k * V + i]);
+      st_v4(dst + k * V, u.u);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < E; ++i) dst[i] = Ty<T>::from_f(v[i]);
+  }
+}
+
+template <int E>
+__device__ __forceinline__ void butterfly_regs(float* v) {
+#pragma unroll
+  for (int h = 1; h < E; h <<= 1) {
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+      if ((i & h) == 0) {
+        float a = v[i], b = v[i + h];
+        v[i] = __fadd_rn(a, b);
+        v[i + h] = __fsub_rn(a, b);
+      }
+    }
+  }
+}
+
+// Shuffle stages over lane bits [0, log2(tps)).
+template <int E>
+__device__ __forceinline__ void butterfly_lanes(float* v, int tps, int lane_in_team) {
+  for (int m = 1; m < tps; m <<= 1) {
+    const bool upper = lane_in_team & m;
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+      float p = __shfl_xor_sync(0xffffffffu, v[i], m);
+      v[i] = upper ? __fsub_rn(p, v[i]) : __fadd_rn(v[i], p);
+    }
+  }
+}
+
+template <typename T, int E, bool QUANT>
+__device__ __forceinline__ void finish_and_quant(float* v, const FhtArgs& a, MinMax& r) {
+  // y = round_T(acc * entry)
+#pragma unroll
+  for (int i = 0; i < E; ++i) v[i] = Ty<T>::round(__fmul_rn(v[i], a.entry));
+  if constexpr (QUANT) {
+    r.init();
+#pragma unroll
+    for (int i = 0; i < E; ++i) r.add(a.sym ? fabsf(v[i]) : v[i]);
+  }
+}
+
+template <typename T, int E>
+__device__ __forceinline__ void fake_quant_vals(float* v, const FhtArgs& a, float scale, float zp) {
+#pragma unroll
+  for (int i = 0; i < E; ++i) {
+    float t = tadd<T>(tdiv<T>(v[i], scale), zp);
+    float q = tclamp(tste(t), a.qmin, a.qmax);
+    v[i] = tmul<T>(tsub<T>(q, zp), scale);
+  }
+}
+
+// Teams of tps = d/E <= 32 lanes; several rows per warp.
+template <typename T, int E, bool QUANT>
+__global__ void __launch_bounds__(256) fht_warp_kernel(const T* __restrict__ x, FhtArgs a,
+                                                       T* __restrict__ out,
+                                                       T* __restrict__ scale_out,
+                                                       T* __restrict__ zp_out, int vec) {
+  const int tps = a.d / E;
+  const int lane = threadIdx.x & 31;
+  const int t = lane & (tps - 1);
+  const int64_t team = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / tps;
+  const int64_t nteams = ((int64_t)gridDim.x * blockDim.x) / tps;
+  const int64_t team0 = team - lane / tps;
+  for (int64_t r0 = team0; r0 < a.rows; r0 += nteams) {
+    const int64_t row = r0 + lane / tps;
+    const bool live = row < a.rows;
+    float v[E];
+    if (live) load_row_chunk<T, E>(x + row * a.d + (int64_t)t * E, v, vec);
+    else {
+#pragma unroll
+      for (int i = 0; i < E; ++i) v[i] = 0.0f;
+    }
+    butterfly_regs<E>(v);
+    butterfly_lanes<E>(v, tps, t);
+    MinMax r;
+    finish_and_quant<T, E, QUANT>(v, a, r);
+    if constexpr (QUANT) {
+      for (int m = 1; m < tps; m <<= 1) r.shfl_xor_merge(m);
+      float scale, zp;
+      qparams_from<T>(r, a.sym, a.qmin, a.qmax, a.lo, scale, zp);
+      if (live && t == 0 && scale_out) {
+        scale_out[row] = Ty<T>::from_f(scale);
+        zp_out[row] = Ty<T>::from_f(zp);
+      }
+      fake_quant_vals<T, E>(v, a, scale, zp);
+    }
+    if (live) store_row_chunk<T, E>(out + row * a.d + (int64_t)t * E, v, vec);
+  }
+}
+
+// One block of NT = 32*W threads (d = NT*E, W <= E) per row.
+template <typename T, int E, int W, bool QUANT>
+__global__ void __launch_bounds__(1024) fht_block_kernel(const T* __restrict__ x, FhtArgs a,
+                                                         T* __restrict__ out,
+                                                         T* __restrict__ scale_out,
+                                                         T* __restrict__ zp_out, int vec) {
+  extern __shared__ float sm[];  // [d]
+  __shared__ MinMax red[32];
+  const int t = threadIdx.x, lane = t & 31;
+  constexpr int span = 32 * E;  // elements covered by one warp
+  constexpr int cpt = E / W;    // (lane, reg) combos per thread in phase 2
+  for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+    float v[E];
+    load_row_chunk<T, E>(x + row * a.d + (int64_t)t * E, v, vec);
+    butterfly_regs<E>(v);
+    butterfly_lanes<E>(v, 32, lane);
+    __syncthreads();  // previous row's readers are done with sm
+#pragma unroll
+    for (int i = 0; i < E; ++i) sm[t * E + i] = v[i];
+    __syncthreads();
+    // phase 2: thread owns combos c = t*cpt + m (c in [0, span)), each with W
+    // elements at c + w*span; butterfly over w in registers (reusing v).
+    float* u = v;
+#pragma unroll
+    for (int m = 0; m < cpt; ++m) {
+      const int c = t * cpt + m;
+#pragma unroll
+      for (int w = 0; w < W; ++w) u[m * W + w] = sm[c + w * span];
+    }
+#pragma unroll
+    for (int h = 1; h < W; h <<= 1) {
+#pragma unroll
+      for (int m = 0; m < cpt; ++m) {
+#pragma unroll
+        for (int w = 0; w < W; ++w) {
+          if ((w & h) == 0) {
+            float p = u[m * W + w], q = u[m * W + w + h];
+            u[m * W + w] = __fadd_rn(p, q);
+            u[m * W + w + h] = __fsub_rn(p, q);
+          }
+        }
+      }
+    }
+    MinMax r;
+    finish_and_quant<T, E, QUANT>(u, a, r);
+    __syncthreads();
+#pragma unroll
+    for (int m = 0; m < cpt; ++m) {
+      const int c = t * cpt + m;
+#pragma unroll
+      for (int w = 0; w < W; ++w) sm[c + w * span] = u[m * W + w];
+    }
+    float scale = 0.f, zp = 0.f;
+    if constexpr (QUANT) {
+      for (int mm = 16; mm >= 1; mm >>= 1) r.shfl_xor_merge(mm);
+      if (lane == 0) red[t >> 5] = r;
+    }
+    __syncthreads();
+    if constexpr (QUANT) {
+      MinMax tot = red[0];
+      for (int i = 1; i < W; ++i) tot.merge(red[i]);
+      qparams_from<T>(tot, a.sym, a.qmin, a.qmax, a.lo, scale, zp);
+      if (t == 0 && scale_out) {
+        scale_out[row] = Ty<T>::from_f(scale);
+        zp_out[row] = Ty<T>::from_f(zp);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < E; ++i) v[i] = sm[t * E + i];
+    if constexpr (QUANT) fake_quant_vals<T, E>(v, a, scale, zp);
+    store_row_chunk<T, E>(out + row * a.d + (int64_t)t * E, v, vec);
+  }
+}
+
+template <typename T> float entry_of(int d) {
+  float c = 1.0f / (float)sqrt((double)d);
+  if (Ty<T>::code == LQ_BF16) return __bfloat162float(__float2bfloat16_rn(c));
+  if (Ty<T>::code == LQ_F16) return __half2float(__float2half_rn(c));
+  return c;
+}
+
+template <typename T, bool QUANT>
+int fht_launch(const T* x, FhtArgs a, T* out, T* s, T* z, cudaStream_t st) {
+  constexpr int V = 16 / sizeof(T);
+  const int d = a.d;
+  auto vec_for = [&](int E) {
+    return (E % V == 0) && aligned16(x) && aligned16(out) && ((int64_t)d * sizeof(T)) % 16 == 0;
+  };
+  int E_warp = d <= 32 * V ? V : (d <= 32 * 16 ? 16 : 32);
+  if (d <= 32 * E_warp) {
+    int E = d < E_warp ? d : E_warp;
+    int tps = d / E;
+    int64_t threads_needed = a.rows * tps;
+    int grid = (int)((threads_needed + 255) / 256);
+    int cap = num_sms() * 16;
+    grid = grid < 1 ? 1 : (grid > cap ? cap : grid);
+    int vec = vec_for(E);
+    switch (E) {
+      case 1: fht_warp_kernel<T, 1, QUANT><<<grid, 256, 0, st>>>(x, a, out, s, z, 0); break;
+      case 2: fht_warp_kernel<T, 2, QUANT><<<grid, 256, 0, st>>>(x, a, out, s, z, 0); break;
+      case 4: fht_warp_kernel<T, 4, QUANT><<<grid, 256, 0, st>>>(x, a, out, s, z, vec); break;
+      case 8: fht_warp_kernel<T, 8, QUANT><<<grid, 256, 0, st>>>(x, a, out, s, z, vec); break;
+      case 16: fht_warp_kernel<T, 16, QUANT><<<grid, 256, 0, st>>>(x, a, out, s, z, vec); break;
+      case 32: fht_warp_kernel<T, 32, QUANT><<<grid, 256, 0, st>>>(x, a, out, s, z, vec); break;
+      default: set_error("internal: bad E %d", E); return LQ_EINVAL;
+    }
+    return launched("fht_warp_kernel");
+  }
+  int E = (d <= 8192) ? 16 : 32;
+  int NT = d / E;
+  LQ_REQUIRE(NT <= 1024 && NT / 32 <= E, LQ_ERANGE, "hadamard d=%d too large", d);
+  size_t smem = (size_t)d * sizeof(float);
+  int grid = (int)(a.rows < (int64_t)num_sms() * 4 ? a.rows : (int64_t)num_sms() * 4);
+  int vec = vec_for(E);
+  void (*k)(const T*, FhtArgs, T*, T*, T*, int) = nullptr;
+  const int W = NT / 32;
+  if (E == 16 && W == 4) k = fht_block_kernel<T, 16, 4, QUANT>;
+  else if (E == 16 && W == 8) k = fht_block_kernel<T, 16, 8, QUANT>;
+  else if (E == 16 && W == 16) k = fht_block_kernel<T, 16, 16, QUANT>;
+  else if (E == 32 && W == 16) k = fht_block_kernel<T, 32, 16, QUANT>;
+  else if (E == 32 && W == 32) k = fht_block_kernel<T, 32, 32, QUANT>;
+  LQ_REQUIRE(k != nullptr, LQ_EINVAL, "internal: no block shape for d=%d", d);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    LQ_REQUIRE(e == cudaSuccess, LQ_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  }
+  k<<<grid, NT, smem, st>>>(x, a, out, s, z, vec);
+  return launched("fht_block_kernel");
+}
+
+template <typename T, bool QUANT>
+int fht_t(const void* x, int64_t rows, int64_t d, int n_bits, int sym, void* out, void* s,
+          void* z, cudaStream_t st) {
+  FhtArgs a;
+  a.rows = rows;
+  a.d = (int)d;
+  a.E = 0;
+  a.log2d = 0;
+  while ((1 << a.log2d) < d) ++a.log2d;
+  a.entry = entry_of<T>((int)d);
+  a.qmin = (float)qmin_of(n_bits, sym);
+  a.qmax = (float)qmax_of(n_bits, sym);
+  a.lo = lo_clamp_value<T>();
+  a.sym = sym;
+  return fht_launch<T, QUANT>(static_cast<const T*>(x), a, static_cast<T*>(out),
+                              static_cast<T*>(s), static_cast<T*>(z), st);
+}
+
+}  // namespace
+}  // namespace lq
+
+using namespace lq;
+
+static int check_fht(int64_t rows, int64_t d) {
+  LQ_REQUIRE(rows >= 0, LQ_EINVAL, "bad rows");
+  LQ_REQUIRE(d >= 1 && (d & (d - 1)) == 0, LQ_EINVAL, "last dim must be power of 2 (got %lld)", (long long)d);
+  LQ_REQUIRE(d <= 32768, LQ_ERANGE, "d=%lld above 32768", (long long)d);
+  return LQ_OK;
+}
+
+extern "C" int lq_hadamard(const void* x, int dtype, int64_t rows, int64_t d, void* out,
+                           void* stream) {
+  int rc = check_fht(rows, d);
+  if (rc) return rc;
+  if (rows == 0) return LQ_OK;
+  LQ_REQUIRE(x && out, LQ_EINVAL, "NULL pointer");
+  cudaStream_t st = as_stream(stream);
+  switch (dtype) {
+    case LQ_F32: return fht_t<float, false>(x, rows, d, 8, 1, out, nullptr, nullptr, st);
+    case LQ_F16: return fht_t<__half, false>(x, rows, d, 8, 1, out, nullptr, nullptr, st);
+    case LQ_BF16: return fht_t<__nv_bfloat16, false>(x, rows, d, 8, 1, out, nullptr, nullptr, st);
+    default: set_error("unsupported dtype %d", dtype); return LQ_EDTYPE;
+  }
+}
+
+extern "C" int lq_hadamard_fake_quant(const void* x, int dtype, int64_t rows, int64_t d,
+                                      int n_bits, int symmetric, void* out, void* scale,
+                                      void* zero_point, void* stream) {
+  int rc = check_fht(rows, d);
+  if (rc) return rc;
+  LQ_REQUIRE(n_bits >= 1 && n_bits <= 16, LQ_EINVAL, "n_bits out of range");
+  LQ_REQUIRE((scale == nullptr) == (zero_point == nullptr), LQ_EINVAL, "scale and zero_point must both be given");
+  if (rows == 0) return LQ_OK;
+  LQ_REQUIRE(x && out, LQ_EINVAL, "NULL pointer");
+  cudaStream_t st = as_stream(stream);
+  switch (dtype) {
+    case LQ_F32: return fht_t<float, true>(x, rows, d, n_bits, symmetric, out, scale, zero_point, st);
+    case LQ_F16: return fht_t<__half, true>(x, rows, d, n_bits, symmetric, out, scale, zero_point, st);
+    case LQ_BF16: return fht_t<__nv_bfloat16, true>(x, rows, d, n_bits, symmetric, out, scale, zero_point, st);
+    default: set_error("unsupported dtype %d", dtype); return LQ_EDTYPE;
+  }
+}

@@ -1,0 +1,584 @@
+// lq_nf4.cu -- NF4 blockwise quantization (qlora.py).
+//
+// Encoding.  The reference picks code = first argmin_i |x_norm - NF4_TABLE[i]|
+// with the differences computed in fp32 (qlora.py:103-104).  For x_norm in
+// [-1, 1] the fp32 differences on either side of x_norm are monotone, so the
+// chosen code is a non-decreasing step function of x_norm: it equals the
+// number of thresholds kNF4Theta[i] <= x_norm, where kNF4Theta[i-1] is the
+// smallest fp32 value whose reference code is >= i (found by exhaustive
+// bisection over fp32 bit patterns and re-checked by the CPU tests).  A NaN
+// x_norm fails every comparison and gets code 0, as torch.argmin gives.
+//
+// Layout.  The tensor is flattened and cut into groups of G elements, the
+// last one zero-padded (qlora.py:84-93).  A warp team of G/V lanes (V
+// elements = 16 bytes per lane) owns one group; a block walks "super-groups"
+// of DG consecutive groups so the double quantization of their DG scales
+// (qlora.py:164-196) is done in shared memory in the same pass.
+#include "lq_common.cuh"
+
+namespace lq {
+namespace {
+
+// NF4_TABLE as float32 (qlora.py:50-55).
+__device__ __constant__ float kNF4[16] = {
+    -1.0f, -0.6962f, -0.5251f, -0.3949f, -0.2844f, -0.1848f, -0.0911f, 0.0f,
+    0.0796f, 0.1609f, 0.2461f, 0.3379f, 0.4407f, 0.5626f, 0.7230f, 1.0f};
+
+// Decision thresholds (exact fp32 values).
+__device__ __forceinline__ int nf4_code(float xn) {
+  int c = 0;
+  c += xn >= -0x1.b23a28p-1f;
+  c += xn >= -0x1.38a71cp-1f;
+  c += xn >= -0x1.d70a3cp-2f;
+  c += xn >= -0x1.5bcd34p-2f;
+  c += xn >= -0x1.e075f4p-3f;
+  c += xn >= -0x1.1a8586p-3f;
+  c += xn >= -0x1.752544p-5f;
+  c += xn >= 0x1.460aa8p-5f;
+  c += xn >= 0x1.ec8b44p-4f;
+  c += xn >= 0x1.a0c49cp-3f;
+  c += xn >= 0x1.2b020ep-2f;
+  c += xn >= 0x1.8ea4aap-2f;
+  c += xn >= 0x1.00d846p-1f;
+  c += xn >= 0x1.491d16p-1f;
+  c += xn >= 0x1.b91688p-1f;
+  return c;
+}
+
+// x_norm = (x / scale) rounded to T.  For bf16 operands the quotient of two
+// 8-bit significands is never within 2^-17 (relative) of a bf16 rounding
+// midpoint unless it equals one (impossible: a midpoint needs a 9-bit odd
+// significand), so bf16(x * rcp(scale)) with rcp correctly rounded equals
+// bf16(x / scale) whenever the product is a normal fp32 number.  Other
+// dtypes and edge cases use the IEEE division.
+template <typename T>
+__device__ __forceinline__ float xnorm(float x, float scale, float rcp, bool rcp_ok) {
+  if constexpr (sizeof(T) == 2 && Ty<T>::code == LQ_BF16) {
+    float p = __fmul_rn(x, rcp);
+    if (rcp_ok && (fabsf(p) >= 0x1p-126f || p == 0.0f)) return Ty<T>::round(p);
+  }
+  return tdiv<T>(x, scale);
+}
+
+template <typename T>
+__device__ __forceinline__ bool rcp_usable(float scale) {
+  return scale >= 0x1p-126f && scale <= 0x1p126f;  // finite, normal, not NaN
+}
+
+struct NfArgs {
+  int64_t n, G, DG, n_groups, n_super;
+  float lo;
+  int g_shift;  // log2(G) when G is a power of two, else -1
+};
+
+inline int log2_exact(int64_t v) {
+  if (v <= 0 || (v & (v - 1))) return -1;
+  int k = 0;
+  while ((int64_t(1) << k) < v) ++k;
+  return k;
+}
+
+// Write V (4 or 8) codes of elements e..e+V-1.
+template <int V, int CODE_DT>
+__device__ __forceinline__ void store_codes(void* codes, int64_t e, const int* c, int64_t n) {
+  if constexpr (CODE_DT == LQ_U4X2) {
+    uint8_t* p = static_cast<uint8_t*>(codes) + e / 2;
+    if (e + V <= n) {
+      uint32_t w = 0;
+#pragma unroll
+      for (int i = 0; i < V; ++i) w |= (uint32_t)c[i] << (4 * i);
+      if constexpr (V == 8) *reinterpret_cast<uint32_t*>(p) = w;
+      else *reinterpret_cast<uint16_t*>(p) = (uint16_t)w;
+    } else {
+      for (int i = 0; i < V; i += 2) {
+        if (e + i >= n) break;
+        int hi = (e + i + 1 < n) ? c[i + 1] : 0;
+        p[i / 2] = (uint8_t)(c[i] | (hi << 4));
+      }
+    }
+  } else if constexpr (CODE_DT == LQ_U8) {
+    uint8_t* p = static_cast<uint8_t*>(codes) + e;
+    for (int i = 0; i < V; ++i)
+      if (e + i < n) p[i] = (uint8_t)c[i];
+  } else {
+    int64_t* p = static_cast<int64_t*>(codes) + e;
+    if (e + V <= n) {
+#pragma unroll
+      for (int i = 0; i < V; i += 2)
+        *reinterpret_cast<longlong2*>(p + i) = make_longlong2(c[i], c[i + 1]);
+    } else {
+      for (int i = 0; i < V; ++i)
+        if (e + i < n) p[i] = c[i];
+    }
+  }
+}
+
+// Quantize kernel.  blockDim.x = 256; a warp team of `tps` lanes holds a
+// group of G = tps*NVT*V elements (vector path, G % V == 0) in registers.
+template <typename T, int NVT, int CODE_DT, bool DQ>
+__global__ void __launch_bounds__(256) nf4_quant_kernel(const T* __restrict__ x, NfArgs a,
+                                                        int tps, void* __restrict__ codes,
+                                                        T* __restrict__ scales,
+                                                        T* __restrict__ q_scales,
+                                                        T* __restrict__ dq_scales) {
+  constexpr int V = 16 / sizeof(T);
+  extern __shared__ float s_scale[];  // [DG] (double quant only)
+  __shared__ MinMax red[8];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int t = lane & (tps - 1);
+  const int teams_per_block = blockDim.x / tps;
+  const int team = threadIdx.x / tps;
+  for (int64_t sg = blockIdx.x; sg < a.n_super; sg += gridDim.x) {
+    const int64_t g_begin = sg * a.DG;
+    const int64_t g_end = min(g_begin + a.DG, a.n_groups);
+    // all warps iterate the same number of times
+    for (int64_t gb = g_begin; gb < g_end; gb += teams_per_block) {
+      const int64_t g = gb + team;
+      const bool live = g < g_end;
+      float v[NVT * V];
+      const int64_t e0 = g * a.G;
+      float am = 0.0f;
+      int nan = 0;
+#pragma unroll
+      for (int k = 0; k < NVT; ++k) {
+        const int64_t e = e0 + (int64_t)(k * tps + t) * V;
+        if (live && e + V <= a.n) {
+          Vec16<T> u;
+          u.u = ld_nc_v4(x + e);
+#pragma unroll
+          for (int i = 0; i < V; ++i) v[k * V + i] = Ty<T>::to_f(u.v[i]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < V; ++i) v[k * V + i] = (live && e + i < a.n) ? Ty<T>::to_f(x[e + i]) : 0.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+          am = fmaxf(am, fabsf(v[k * V + i]));
+          nan |= v[k * V + i] != v[k * V + i];
+        }
+      }
+      for (int m = 1; m < tps; m <<= 1) {
+        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, m));
+        nan |= __shfl_xor_sync(0xffffffffu, nan, m);
+      }
+      if (live) {
+        float s = nan ? __int_as_float(0x7fc00000) : am;
+        s = (s < a.lo) ? a.lo : s;  // clamp(min=1e-12) in T
+        const float sr = Ty<T>::round(s);  // absmax is already a T value
+        if (t == 0) {
+          scales[g] = Ty<T>::from_f(sr);
+          if constexpr (DQ) s_scale[g - g_begin] = sr;
+        }
+        const bool rok = rcp_usable<T>(sr);
+        const float rcp = rok ? __frcp_rn(sr) : 0.0f;
+#pragma unroll
+        for (int k = 0; k < NVT; ++k) {
+          const int64_t e = e0 + (int64_t)(k * tps + t) * V;
+          if (e >= a.n) continue;
+          int c[V];
+#pragma unroll
+          for (int i = 0; i < V; ++i) c[i] = nf4_code(xnorm<T>(v[k * V + i], sr, rcp, rok));
+          store_codes<V, CODE_DT>(codes, e, c, a.n);
+        }
+      }
+    }
+    if constexpr (DQ) {
+      __syncthreads();
+      // dq_scale = absmax over the DG scales (zero-padded), clamp(1e-12) in T
+      const int cnt = (int)(g_end - g_begin);
+      MinMax r;
+      r.init();
+      for (int j = threadIdx.x; j < cnt; j += blockDim.x) r.add(fabsf(s_scale[j]));
+      for (int m = 16; m >= 1; m >>= 1) r.shfl_xor_merge(m);
+      if (lane == 0) red[warp] = r;
+      __syncthreads();
+      MinMax tot = red[0];
+      for (int w = 1; w < (int)(blockDim.x >> 5); ++w) tot.merge(red[w]);
+      float dq = tot.nan ? __int_as_float(0x7fc00000) : fmaxf(tot.mx, 0.0f);
+      dq = (dq < a.lo) ? a.lo : dq;
+      if (threadIdx.x == 0) dq_scales[sg] = Ty<T>::from_f(dq);
+      for (int j = threadIdx.x; j < cnt; j += blockDim.x) {
+        float sn = tdiv<T>(s_scale[j], dq);
+        float q = tclamp(trint(tmul<T>(sn, 127.0f)), -127.0f, 127.0f);
+        q_scales[g_begin + j] = Ty<T>::from_f(q);
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// Generic scalar path (any G): pass 1 writes the group scales (one block per
+// group), pass 2 writes codes for pairs of flat elements, so packed bytes are
+// always written whole even when a pair straddles two groups.
+template <typename T>
+__global__ void __launch_bounds__(256) nf4_scales_kernel(const T* __restrict__ x, NfArgs a,
+                                                         T* __restrict__ scales) {
+  __shared__ MinMax red[8];
+  for (int64_t g = blockIdx.x; g < a.n_groups; g += gridDim.x) {
+    const int64_t e0 = g * a.G;
+    MinMax r;
+    r.init();
+    for (int64_t i = threadIdx.x; i < a.G; i += blockDim.x) {
+      float v = (e0 + i < a.n) ? Ty<T>::to_f(x[e0 + i]) : 0.0f;
+      r.add(fabsf(v));
+    }
+    for (int m = 16; m >= 1; m >>= 1) r.shfl_xor_merge(m);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = r;
+    __syncthreads();
+    MinMax tot = red[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) tot.merge(red[w]);
+    float s = tot.nan ? __int_as_float(0x7fc00000) : fmaxf(tot.mx, 0.0f);
+    s = (s < a.lo) ? a.lo : s;
+    if (threadIdx.x == 0) scales[g] = Ty<T>::from_f(s);
+  }
+}
+
+template <typename T, int CODE_DT>
+__global__ void __launch_bounds__(256) nf4_codes_kernel(const T* __restrict__ x, NfArgs a,
+                                                        const T* __restrict__ scales,
+                                                        void* __restrict__ codes) {
+  const int64_t npair = (a.n + 1) / 2;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < npair;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int c[2] = {0, 0};
+    for (int k = 0; k < 2; ++k) {
+      const int64_t e = 2 * i + k;
+      if (e < a.n) c[k] = nf4_code(tdiv<T>(Ty<T>::to_f(x[e]), Ty<T>::to_f(scales[e / a.G])));
+    }
+    if constexpr (CODE_DT == LQ_U4X2) {
+      static_cast<uint8_t*>(codes)[i] = (uint8_t)(c[0] | (c[1] << 4));
+    } else if constexpr (CODE_DT == LQ_U8) {
+      for (int k = 0; k < 2; ++k)
+        if (2 * i + k < a.n) static_cast<uint8_t*>(codes)[2 * i + k] = (uint8_t)c[k];
+    } else {
+      for (int k = 0; k < 2; ++k)
+        if (2 * i + k < a.n) static_cast<int64_t*>(codes)[2 * i + k] = c[k];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Dequantize: out[e] = table_T[code[e]] * scale[e / G] in T.  When q_scales
+// is given the scale is first restored as (q / 127) * dq (qlora.py:199-223).
+// Thread = 8 consecutive elements.
+// ---------------------------------------------------------------------------
+template <typename T, int CODE_DT>
+__global__ void __launch_bounds__(256) nf4_dequant_kernel(const void* __restrict__ codes, NfArgs a,
+                                                          const T* __restrict__ scales,
+                                                          const T* __restrict__ q_scales,
+                                                          const T* __restrict__ dq_scales,
+                                                          T* __restrict__ out, int vec) {
+  __shared__ float tab[16];
+  if (threadIdx.x < 16) tab[threadIdx.x] = Ty<T>::round(kNF4[threadIdx.x]);
+  __syncthreads();
+  const int64_t nthr = (a.n + 7) / 8;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nthr;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e0 = i * 8;
+    int c[8];
+    if (CODE_DT == LQ_U4X2 && vec && e0 + 8 <= a.n) {
+      uint32_t w = *reinterpret_cast<const uint32_t*>(static_cast<const uint8_t*>(codes) + e0 / 2);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) c[k] = (w >> (4 * k)) & 15;
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        int64_t e = e0 + k;
+        int cv = 0;
+        if (e < a.n) {
+          if constexpr (CODE_DT == LQ_U4X2) cv = (static_cast<const uint8_t*>(codes)[e / 2] >> (4 * (e & 1))) & 15;
+          else if constexpr (CODE_DT == LQ_U8) cv = static_cast<const uint8_t*>(codes)[e];
+          else cv = (int)static_cast<const int64_t*>(codes)[e];
+        }
+        c[k] = cv;
+      }
+    }
+    float o[8];
+    int64_t glast = -1;
+    float s = 0.0f;
+    const bool one_group = (a.G & 7) == 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int64_t g = one_group ? (k == 0 ? (a.g_shift >= 0 ? (e0 >> a.g_shift) : e0 / a.G) : glast)
+                                  : (e0 + k) / a.G;
+      if (g != glast && e0 + k < a.n) {
+        glast = g;
+        if (q_scales) {
+          s = tmul<T>(tdiv<T>(Ty<T>::to_f(q_scales[g]), 127.0f), Ty<T>::to_f(dq_scales[g / a.DG]));
+        } else {
+          s = Ty<T>::to_f(scales[g]);
+        }
+      }
+      // torch indexing of an out-of-range code would raise; codes are 0..15 here
+      o[k] = tmul<T>(tab[c[k] & 15], s);
+    }
+    if (vec && e0 + 8 <= a.n) {
+      if constexpr (sizeof(T) == 2) {
+        Vec16<T> u;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) u.v[k] = Ty<T>::from_f(o[k]);
+        st_v4(out + e0, u.u);
+      } else {
+        st_v4(out + e0, make_uint4(__float_as_uint(o[0]), __float_as_uint(o[1]), __float_as_uint(o[2]), __float_as_uint(o[3])));
+        st_v4(out + e0 + 4, make_uint4(__float_as_uint(o[4]), __float_as_uint(o[5]), __float_as_uint(o[6]), __float_as_uint(o[7])));
+      }
+    } else {
+      for (int k = 0; k < 8; ++k)
+        if (e0 + k < a.n) out[e0 + k] = Ty<T>::from_f(o[k]);
+    }
+  }
+}
+
+// Code container conversion (I64 / U8 / U4X2): pairs of elements per thread so
+// packed bytes are written whole.
+__device__ __forceinline__ int load_code(const void* p, int dt, int64_t e) {
+  if (dt == LQ_U4X2) return (static_cast<const uint8_t*>(p)[e >> 1] >> (4 * (e & 1))) & 15;
+  if (dt == LQ_U8) return static_cast<const uint8_t*>(p)[e];
+  return (int)static_cast<const int64_t*>(p)[e];
+}
+
+__global__ void __launch_bounds__(256) codes_convert_kernel(const void* __restrict__ src, int sdt,
+                                                            int64_t n, void* __restrict__ dst,
+                                                            int ddt) {
+  const int64_t npair = (n + 1) / 2;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < npair;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = 2 * i;
+    const int c0 = load_code(src, sdt, e);
+    const int c1 = (e + 1 < n) ? load_code(src, sdt, e + 1) : 0;
+    if (ddt == LQ_U4X2) {
+      static_cast<uint8_t*>(dst)[i] = (uint8_t)((c0 & 15) | ((c1 & 15) << 4));
+    } else if (ddt == LQ_U8) {
+      static_cast<uint8_t*>(dst)[e] = (uint8_t)c0;
+      if (e + 1 < n) static_cast<uint8_t*>(dst)[e + 1] = (uint8_t)c1;
+    } else {
+      static_cast<int64_t*>(dst)[e] = c0;
+      if (e + 1 < n) static_cast<int64_t*>(dst)[e + 1] = c1;
+    }
+  }
+}
+
+// double_quantize / double_dequantize on a scale vector (qlora.py:164-223).
+template <typename T>
+__global__ void __launch_bounds__(256) double_quant_kernel(const T* __restrict__ s, int64_t n,
+                                                           int64_t DG, float lo,
+                                                           T* __restrict__ q,
+                                                           T* __restrict__ dq) {
+  __shared__ MinMax red[8];
+  const int64_t nd = (n + DG - 1) / DG;
+  for (int64_t d = blockIdx.x; d < nd; d += gridDim.x) {
+    const int64_t b = d * DG, e = min(b + DG, n);
+    MinMax r;
+    r.init();
+    for (int64_t j = b + threadIdx.x; j < e; j += blockDim.x) r.add(fabsf(Ty<T>::to_f(s[j])));
+    for (int m = 16; m >= 1; m >>= 1) r.shfl_xor_merge(m);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = r;
+    __syncthreads();
+    MinMax tot = red[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) tot.merge(red[w]);
+    float m = tot.nan ? __int_as_float(0x7fc00000) : fmaxf(tot.mx, 0.0f);  // padding zeros
+    m = (m < lo) ? lo : m;
+    if (threadIdx.x == 0) dq[d] = Ty<T>::from_f(m);
+    for (int64_t j = b + threadIdx.x; j < e; j += blockDim.x) {
+      float sn = tdiv<T>(Ty<T>::to_f(s[j]), m);
+      q[j] = Ty<T>::from_f(tclamp(trint(tmul<T>(sn, 127.0f)), -127.0f, 127.0f));
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) double_dequant_kernel(const T* __restrict__ q,
+                                                             const T* __restrict__ dq, int64_t n,
+                                                             int64_t DG, T* __restrict__ out) {
+  for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n;
+       j += (int64_t)gridDim.x * blockDim.x)
+    out[j] = Ty<T>::from_f(tmul<T>(tdiv<T>(Ty<T>::to_f(q[j]), 127.0f), Ty<T>::to_f(dq[j / DG])));
+}
+
+int grid_cap(int64_t want, int per_sm = 8) {
+  int64_t cap = (int64_t)num_sms() * per_sm;
+  return (int)(want < 1 ? 1 : (want < cap ? want : cap));
+}
+
+template <typename T, int CODE_DT, bool DQ>
+int nf4_quant_launch(const T* x, NfArgs a, void* codes, T* scales, T* qs, T* dqs, cudaStream_t st) {
+  constexpr int V = 16 / sizeof(T);
+  const bool vec = (a.G % V == 0) && aligned16(x) && (a.G / V) <= 32 * 4 &&
+                   (CODE_DT != LQ_U4X2 || (a.G * 4) % 8 == 0) &&
+                   (reinterpret_cast<uintptr_t>(codes) % (CODE_DT == LQ_I64 ? 16 : 4) == 0);
+  if (!DQ && !vec) {
+    nf4_scales_kernel<T><<<grid_cap(a.n_groups, 16), 256, 0, st>>>(x, a, scales);
+    int rc = launched("nf4_scales_kernel");
+    if (rc != LQ_OK) return rc;
+    nf4_codes_kernel<T, CODE_DT><<<grid_cap((a.n + 511) / 512, 16), 256, 0, st>>>(x, a, scales, codes);
+    return launched("nf4_codes_kernel");
+  }
+  LQ_REQUIRE(vec, LQ_EALIGN, "fused NF4 packing needs group %% %d == 0 and 16-byte aligned input", V);
+  const int64_t nv = a.G / V;
+  int tps = 1, nvt = 1;
+  if (nv <= 32) {
+    while (tps < nv) tps <<= 1;
+    if (tps != nv) { set_error("group/%d must be a power of two <= 32 or a multiple of 32", V); return LQ_EINVAL; }
+  } else {
+    tps = 32;
+    nvt = (int)(nv / 32);
+    if (nv % 32 || (nvt != 2 && nvt != 4)) { set_error("unsupported NF4 group size %lld", (long long)a.G); return LQ_EINVAL; }
+  }
+  if (!DQ) {
+    a.DG = 256 / tps * 8;  // super-group = a few block iterations
+    a.n_super = (a.n_groups + a.DG - 1) / a.DG;
+  }
+  size_t smem = DQ ? (size_t)a.DG * sizeof(float) : 0;
+  int grid = grid_cap(a.n_super, 8);
+  if (nvt == 1) nf4_quant_kernel<T, 1, CODE_DT, DQ><<<grid, 256, smem, st>>>(x, a, tps, codes, scales, qs, dqs);
+  else if (nvt == 2) nf4_quant_kernel<T, 2, CODE_DT, DQ><<<grid, 256, smem, st>>>(x, a, tps, codes, scales, qs, dqs);
+  else nf4_quant_kernel<T, 4, CODE_DT, DQ><<<grid, 256, smem, st>>>(x, a, tps, codes, scales, qs, dqs);
+  return launched("nf4_quant_kernel");
+}
+
+template <typename T>
+int nf4_quant_t(const void* x, int64_t n, int64_t G, int64_t DG, void* codes, int cdt,
+                void* scales, void* qs, void* dqs, cudaStream_t st) {
+  NfArgs a;
+  a.n = n;
+  a.G = G;
+  a.n_groups = (n + G - 1) / G;
+  a.DG = DG > 0 ? DG : 1;
+  a.n_super = (a.n_groups + a.DG - 1) / a.DG;
+  a.lo = lo_clamp_value<T>();
+  a.g_shift = log2_exact(G);
+  const T* xp = static_cast<const T*>(x);
+  T* sp = static_cast<T*>(scales);
+  if (DG > 0) {
+    LQ_REQUIRE(DG <= 8192, LQ_ERANGE, "dq_group %lld above 8192", (long long)DG);
+    switch (cdt) {
+      case LQ_U4X2: return nf4_quant_launch<T, LQ_U4X2, true>(xp, a, codes, sp, (T*)qs, (T*)dqs, st);
+      case LQ_U8: return nf4_quant_launch<T, LQ_U8, true>(xp, a, codes, sp, (T*)qs, (T*)dqs, st);
+      case LQ_I64: return nf4_quant_launch<T, LQ_I64, true>(xp, a, codes, sp, (T*)qs, (T*)dqs, st);
+    }
+  } else {
+    switch (cdt) {
+      case LQ_U4X2: return nf4_quant_launch<T, LQ_U4X2, false>(xp, a, codes, sp, nullptr, nullptr, st);
+      case LQ_U8: return nf4_quant_launch<T, LQ_U8, false>(xp, a, codes, sp, nullptr, nullptr, st);
+      case LQ_I64: return nf4_quant_launch<T, LQ_I64, false>(xp, a, codes, sp, nullptr, nullptr, st);
+    }
+  }
+  set_error("unsupported code dtype %d", cdt);
+  return LQ_EDTYPE;
+}
+
+template <typename T>
+int nf4_dequant_t(const void* codes, int cdt, int64_t n, int64_t G, int64_t DG, const void* s,
+                  const void* qs, const void* dqs, void* out, cudaStream_t st) {
+  NfArgs a;
+  a.n = n;
+  a.G = G;
+  a.DG = DG > 0 ? DG : 1;
+  a.n_groups = (n + G - 1) / G;
+  a.n_super = 0;
+  a.lo = 0;
+  a.g_shift = log2_exact(G);
+  int vec = aligned16(out) && (reinterpret_cast<uintptr_t>(codes) % 4 == 0);
+  int grid = grid_cap((n + 8 * 256 - 1) / (8 * 256), 16);
+  const T* sp = static_cast<const T*>(s);
+  const T* q = static_cast<const T*>(qs);
+  const T* d = static_cast<const T*>(dqs);
+  T* o = static_cast<T*>(out);
+  switch (cdt) {
+    case LQ_U4X2: nf4_dequant_kernel<T, LQ_U4X2><<<grid, 256, 0, st>>>(codes, a, sp, q, d, o, vec); break;
+    case LQ_U8: nf4_dequant_kernel<T, LQ_U8><<<grid, 256, 0, st>>>(codes, a, sp, q, d, o, vec); break;
+    case LQ_I64: nf4_dequant_kernel<T, LQ_I64><<<grid, 256, 0, st>>>(codes, a, sp, q, d, o, vec); break;
+    default: set_error("unsupported code dtype %d", cdt); return LQ_EDTYPE;
+  }
+  return launched("nf4_dequant_kernel");
+}
+
+#define LQ_DISPATCH_FLOAT(dt, FN, ...)                                   \
+  switch (dt) {                                                          \
+    case LQ_F32: return FN<float>(__VA_ARGS__);                          \
+    case LQ_F16: return FN<__half>(__VA_ARGS__);                         \
+    case LQ_BF16: return FN<__nv_bfloat16>(__VA_ARGS__);                 \
+    default: ::lq::set_error("unsupported dtype %d", (int)(dt)); return LQ_EDTYPE; \
+  }
+
+template <typename T>
+int dq_t(const void* s, int64_t n, int64_t DG, void* q, void* dq, cudaStream_t st) {
+  const int64_t nd = (n + DG - 1) / DG;
+  double_quant_kernel<T><<<grid_cap(nd, 16), 256, 0, st>>>(static_cast<const T*>(s), n, DG, lo_clamp_value<T>(), static_cast<T*>(q), static_cast<T*>(dq));
+  return launched("double_quant_kernel");
+}
+template <typename T>
+int ddq_t(const void* q, const void* dq, int64_t n, int64_t DG, void* out, cudaStream_t st) {
+  double_dequant_kernel<T><<<grid_cap((n + 255) / 256, 16), 256, 0, st>>>(static_cast<const T*>(q), static_cast<const T*>(dq), n, DG, static_cast<T*>(out));
+  return launched("double_dequant_kernel");
+}
+
+}  // namespace
+}  // namespace lq
+
+using namespace lq;
+
+extern "C" int lq_nf4_quantize(const void* x, int x_dtype, int64_t n, int64_t group, void* codes,
+                               int code_dtype, void* scales, void* stream) {
+  LQ_REQUIRE(n >= 0 && group >= 1, LQ_EINVAL, "bad size n=%lld group=%lld", (long long)n, (long long)group);
+  if (n == 0) return LQ_OK;
+  LQ_REQUIRE(x && codes && scales, LQ_EINVAL, "NULL pointer");
+  LQ_DISPATCH_FLOAT(x_dtype, nf4_quant_t, x, n, group, 0, codes, code_dtype, scales, nullptr, nullptr, as_stream(stream));
+}
+
+extern "C" int lq_nf4_dequantize(const void* codes, int code_dtype, int64_t n, int64_t group,
+                                 const void* scales, int s_dtype, void* out, void* stream) {
+  LQ_REQUIRE(n >= 0 && group >= 1, LQ_EINVAL, "bad size");
+  if (n == 0) return LQ_OK;
+  LQ_REQUIRE(codes && scales && out, LQ_EINVAL, "NULL pointer");
+  LQ_DISPATCH_FLOAT(s_dtype, nf4_dequant_t, codes, code_dtype, n, group, 0, scales, nullptr, nullptr, out, as_stream(stream));
+}
+
+extern "C" int lq_double_quantize(const void* scales, int dtype, int64_t n, int64_t dq_group,
+                                  void* q_scales, void* dq_scales, void* stream) {
+  LQ_REQUIRE(n >= 0 && dq_group >= 1, LQ_EINVAL, "bad size");
+  if (n == 0) return LQ_OK;
+  LQ_REQUIRE(scales && q_scales && dq_scales, LQ_EINVAL, "NULL pointer");
+  LQ_DISPATCH_FLOAT(dtype, dq_t, scales, n, dq_group, q_scales, dq_scales, as_stream(stream));
+}
+
+extern "C" int lq_double_dequantize(const void* q_scales, const void* dq_scales, int dtype,
+                                    int64_t n, int64_t dq_group, void* out, void* stream) {
+  LQ_REQUIRE(n >= 0 && dq_group >= 1, LQ_EINVAL, "bad size");
+  if (n == 0) return LQ_OK;
+  LQ_REQUIRE(q_scales && dq_scales && out, LQ_EINVAL, "NULL pointer");
+  LQ_DISPATCH_FLOAT(dtype, ddq_t, q_scales, dq_scales, n, dq_group, out, as_stream(stream));
+}
+
+extern "C" int lq_nf4_pack(const void* x, int x_dtype, int64_t n, int64_t group, int64_t dq_group,
+                           uint8_t* packed_codes, void* scales, void* q_scales, void* dq_scales,
+                           void* stream) {
+  LQ_REQUIRE(n >= 0 && group >= 1 && dq_group >= 0, LQ_EINVAL, "bad size");
+  if (n == 0) return LQ_OK;
+  LQ_REQUIRE(x && packed_codes && scales, LQ_EINVAL, "NULL pointer");
+  LQ_REQUIRE(dq_group == 0 || (q_scales && dq_scales), LQ_EINVAL, "double quantization needs q_scales/dq_scales");
+  LQ_DISPATCH_FLOAT(x_dtype, nf4_quant_t, x, n, group, dq_group, packed_codes, LQ_U4X2, scales, q_scales, dq_scales, as_stream(stream));
+}
+
+extern "C" int lq_nf4_unpack(const uint8_t* packed_codes, int64_t n, int64_t group, int64_t dq_group,
+                             const void* scales, const void* q_scales, const void* dq_scales,
+                             int s_dtype, void* out, void* stream) {
+  LQ_REQUIRE(n >= 0 && group >= 1, LQ_EINVAL, "bad size");
+  if (n == 0) return LQ_OK;
+  LQ_REQUIRE(packed_codes && out && (scales || q_scales), LQ_EINVAL, "NULL pointer");
+  LQ_REQUIRE(!q_scales || (dq_scales && dq_group > 0), LQ_EINVAL, "double dequantization needs dq_scales and dq_group");
+  LQ_DISPATCH_FLOAT(s_dtype, nf4_dequant_t, packed_codes, LQ_U4X2, n, group, dq_group, scales, q_scales, dq_scales, out, as_stream(stream));
+}
+
+extern "C" int lq_codes_convert(const void* src, int src_dtype, int64_t n, void* dst, int dst_dtype,
+                                void* stream) {
+  LQ_REQUIRE(n >= 0, LQ_EINVAL, "bad size");
+  auto ok = [](int d) { return d == LQ_I64 || d == LQ_U8 || d == LQ_U4X2; };
+  LQ_REQUIRE(ok(src_dtype) && ok(dst_dtype), LQ_EDTYPE, "code containers are I64, U8 or U4X2");
+  if (n == 0) return LQ_OK;
+  LQ_REQUIRE(src && dst, LQ_EINVAL, "NULL pointer");
+  codes_convert_kernel<<<grid_cap(((n + 1) / 2 + 255) / 256, 16), 256, 0, as_stream(stream)>>>(src, src_dtype, n, dst, dst_dtype);
+  return launched("codes_convert_kernel");
+}

@@ -1,0 +1,191 @@
+"""CPU-side checks of the C-ABI library and the host logic (no GPU needed).
+
+* liblq_sm100.so builds for sm_100a and exports every function
+  include/lq_sm100.h declares;
+* the NF4 decision thresholds compiled into the kernel are exactly the
+  smallest fp32 values at which the reference's argmin code changes
+  (re-derived here from the oracle);
+* the Python layer fails loudly on CPU tensors (no fallback) and raises the
+  reference's exception types for bad arguments before touching a device.
+"""
+
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "lq_sm100.h")
+NF4_SRC = os.path.join(ROOT, "llm_quant_b200", "csrc", "lq_nf4.cu")
+
+
+@pytest.fixture(scope="module")
+def lib_path():
+    from llm_quant_b200 import build
+    return build.build()
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    names = re.findall(r"^\s*(?:const\s+)?[a-z_0-9]+\s*\*?\s*(lq_[a-z0-9_]+)\s*\(", src, flags=re.M)
+    return sorted(set(names))
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    for must in ("lq_group_quant", "lq_token_group_quant", "lq_kv_dequant", "lq_kv_append",
+                 "lq_tensor_qparams", "lq_affine", "lq_nf4_quantize", "lq_nf4_pack",
+                 "lq_nf4_unpack", "lq_hadamard", "lq_hadamard_fake_quant"):
+        assert must in names, must
+
+
+def test_library_exports_every_declared_symbol(lib_path):
+    lib = ctypes.CDLL(lib_path)
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, f"not exported: {missing}"
+
+
+def test_library_is_sm100a(lib_path):
+    # cuobjdump is not used (no reading of compiled code); the build flags
+    # are the evidence: every object is compiled with -gencode sm_100a.
+    from llm_quant_b200 import build
+    assert "arch=compute_100a,code=sm_100a" in " ".join(build.ARCH)
+
+
+def test_status_strings(lib_path):
+    lib = ctypes.CDLL(lib_path)
+    lib.lq_status_string.restype = ctypes.c_char_p
+    assert lib.lq_status_string(0) == b"ok"
+    assert lib.lq_status_string(-1) == b"invalid argument"
+    lib.lq_version.restype = ctypes.c_int
+    assert lib.lq_version() >= 100
+
+
+def test_argument_validation_without_gpu(lib_path):
+    """Bad arguments are rejected on the host before any launch."""
+    lib = ctypes.CDLL(lib_path)
+    lib.lq_last_error.restype = ctypes.c_char_p
+    V, I, L = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
+    lib.lq_hadamard.argtypes = [V, I, L, L, V, V]
+    assert lib.lq_hadamard(None, 2, 4, 12, None, None) == -1  # d not a power of two
+    assert b"power of 2" in lib.lq_last_error()
+    assert lib.lq_hadamard(None, 2, 4, 65536, None, None) == -6  # above maximum
+    lib.lq_group_quant.argtypes = [V, I, L, L, L, I, I, I, V, I, V, V, V]
+    assert lib.lq_group_quant(None, 0, 4, 8, 0, 4, 1, 1, None, 0, None, None, None) == -1
+    assert lib.lq_group_quant(None, 0, 4, 8, 4, 99, 1, 1, None, 0, None, None, None) == -1
+    # empty tensors are a no-op
+    assert lib.lq_group_quant(None, 0, 0, 8, 4, 4, 1, 1, None, 0, None, None, None) == 0
+
+
+def _oracle_thresholds():
+    from oracle.lq_oracle import nf4_encode
+
+    def code(v):
+        return int(nf4_encode(np.array([v], np.float32))[0])
+
+    def key(f):
+        u = int(np.array([f], np.float32).view(np.int32)[0])
+        return u if u >= 0 else -(u & 0x7FFFFFFF)
+
+    def unkey(k):
+        u = k if k >= 0 else ((-k) | -(2 ** 31))
+        return np.array([u], np.int32).view(np.float32)[0]
+
+    out = []
+    for i in range(1, 16):
+        lo, hi = key(np.float32(-1.0)), key(np.float32(1.0))
+        while hi - lo > 1:
+            mid = (lo + hi) // 2
+            if code(unkey(mid)) >= i:
+                hi = mid
+            else:
+                lo = mid
+        out.append(np.float32(unkey(hi)))
+    return out
+
+
+def test_nf4_kernel_thresholds_match_reference_rule():
+    src = open(NF4_SRC).read()
+    body = src[src.index("int nf4_code(float xn)"):]
+    body = body[:body.index("return c;")]
+    hexes = re.findall(r"xn >= (-?0x[0-9a-f.]+p-?\d+)f", body)
+    assert len(hexes) == 15
+    kernel = [np.float32(float.fromhex(h)) for h in hexes]
+    assert kernel == _oracle_thresholds()
+
+
+def test_nf4_threshold_count_equals_argmin_on_grids():
+    """The count-of-thresholds encoder equals the reference argmin on every
+    bf16 / fp16 value in [-1, 1] and near every boundary in fp32."""
+    from oracle.lq_oracle import nf4_encode
+    th = np.array(_oracle_thresholds(), np.float32)
+    u = (np.arange(0, 0x10000, dtype=np.uint32) << 16).view(np.float32)
+    v16 = np.arange(0, 0x10000, dtype=np.uint32).astype(np.uint16).view(np.float16).astype(np.float32)
+    rng = np.random.default_rng(0)
+    vals = np.concatenate([u, v16, rng.uniform(-1, 1, 200000).astype(np.float32),
+                           np.array([np.nan, -0.0, 0.0], np.float32)])
+    vals = vals[np.isnan(vals) | (np.abs(vals) <= 1)]
+    count = (vals[:, None] >= th[None, :]).sum(1)
+    assert np.array_equal(count, nf4_encode(vals))
+
+
+def test_host_rejects_cpu_tensors():
+    import llm_quant_b200 as L
+    x = torch.randn(4, 64)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        L.fake_quantize(x, 4, False, L.QScheme.PER_GROUP, 32)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        L.nf4_quantize(x)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        L.PerTokenKVCacheQuantizer(4).quantize(torch.randn(1, 2, 3, 8))
+
+
+def test_reference_error_types():
+    import llm_quant_b200 as L
+    with pytest.raises(AssertionError):
+        L.hadamard_matrix(3)
+    with pytest.raises(AssertionError):
+        L.fast_hadamard_transform(torch.randn(2, 12))
+    with pytest.raises(ValueError):
+        L.compute_qparams(torch.randn(2, 4), scheme="nope")
+    with pytest.raises(ValueError):
+        L.KVCacheQuantizer(granularity="bad")._compute_qparams(torch.randn(1, 1, 2, 4))
+
+
+def test_hadamard_matrix_matches_oracle():
+    import llm_quant_b200 as L
+    from oracle import lq_oracle as O
+    from golden_io import same_bits
+    for dt, odt in ((torch.float32, "float32"), (torch.bfloat16, "bfloat16"), (torch.float16, "float16")):
+        for n in (1, 2, 8, 64, 2048):
+            H = L.hadamard_matrix(n, dt).float().numpy()
+            assert same_bits(H, O.hadamard_matrix(n, odt)), (dt, n)
+
+
+def test_kv_memory_ratio_matches_reference_values():
+    import llm_quant_b200 as L
+    G = L.KVQuantGranularity
+    assert L.kv_cache_memory_ratio(4) == 4 / 16 + 32 / (128 * 4)
+    assert 0.4 < L.kv_cache_memory_ratio(8, head_dim=128) < 0.6
+    assert L.kv_cache_memory_ratio(4, granularity=G.PER_CHANNEL, seq_len=2048) < \
+        L.kv_cache_memory_ratio(4, granularity=G.PER_TOKEN)
+
+
+def test_install_as_llm_quant():
+    import sys
+    import llm_quant_b200 as L
+    saved = {k: v for k, v in sys.modules.items() if k == "llm_quant" or k.startswith("llm_quant.")}
+    try:
+        L.install_as_llm_quant()
+        from llm_quant.core.quantizer import fake_quantize  # noqa: F401
+        from llm_quant.qlora import nf4_quantize  # noqa: F401
+        import llm_quant
+        assert llm_quant.QuantizedKVCache is L.QuantizedKVCache
+    finally:
+        for k in [k for k in sys.modules if k == "llm_quant" or k.startswith("llm_quant.")]:
+            del sys.modules[k]
+        sys.modules.update(saved)
