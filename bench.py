@@ -321,6 +321,8 @@ class NF4Workload:
     def gather(self):
         """Final gather of every rank's packed codes + scales to rank 0."""
         torch = self.ctx.torch
+        if self.ctx.world == 1:
+            return 0.0, 0
         from llm_quant_b200.sharded import flatten_bytes, gather_to_rank0
         flat = flatten_bytes([t for m in self.mods for t in
                               (m.nf4_codes_packed, m.nf4_scales, m.dq_q_scales, m.dq_scales)])
@@ -537,7 +539,7 @@ class KVWorkload:
             self.k.append(k.to(torch.bfloat16))
             self.v.append(torch.randn(self.B, self.H, self.C, self.D, generator=g,
                                       device=ctx.dev).to(torch.bfloat16))
-        E = self.B * self.H * self.C * self.U
+        E = self.B * self.H * self.C * self.D * self.U  # elements of one tensor of one layer
         self.E = E
         self.n_local = len(self.layers)
         self.n_total = NUM_LAYERS
@@ -641,8 +643,106 @@ class KVWorkload:
                           f"tokens, head_dim 128 ({n} threads), median of 3"}
 
 
+class W4A16Workload:
+    """QuantizedLinear W4A16 forward: Linear(4096, 14336), int4 asym group 128
+    with fp16 scales / zeros, fp16 activations ~ N(0, 1).  A step is one
+    forward at M = 1024 tokens (the headline point); every M in
+    {1, 16, 128, 1024, 4096} is timed in `kernels`.  Weak scaling (replicas)."""
+    name = "w4a16"
+    workload = "quantized_linear_w4a16_K4096_N14336_g128_fp16_M1024"
+    Ms = (1, 16, 128, 1024, 4096)
+    K, N = 4096, 14336
+
+    def __init__(self, ctx):
+        torch = ctx.torch
+        import llm_quant_b200 as L
+        self.ctx, self.L = ctx, L
+        g = torch.Generator(device=ctx.dev).manual_seed(0)
+        lin = torch.nn.Linear(self.K, self.N, device=ctx.dev)
+        with torch.no_grad():
+            lin.weight.copy_(torch.randn(self.N, self.K, generator=g, device=ctx.dev) * 0.02)
+        lin = lin.half()
+        self.ql = L.QuantizedLinear.from_linear(lin, 4, False, 128)
+        self.x = {m: torch.randn(m, self.K, generator=g, device=ctx.dev).half() for m in self.Ms}
+        self.ql(self.x[1])  # builds the packed operand
+        self.n_local = 1
+        self.n_total = ctx.world
+        self.unit = "TFLOP/s"
+
+    def flops(self, m):
+        return 2.0 * m * self.K * self.N
+
+    def bytes_for(self, n):  # FLOPs: this workload's metric is TFLOP/s
+        return self.flops(1024) * n
+
+    def step(self):
+        self.ql(self.x[1024])
+
+    def kernels(self):
+        out = {}
+        for m in self.Ms:
+            x = self.x[m]
+            t = cuda_time_ms(self.ctx.torch, lambda: self.ql(x), 20)
+            wbytes = self.N * self.K / 2 + self.N * (self.K // 128) * 4
+            out[f"w4a16_kernel M={m}"] = (self.flops(m), t, m,
+                                          wbytes + 2 * m * self.K + 2 * m * self.N)
+        return out
+
+    def e2e(self, steps, graph):
+        """Forward through the public API (captured in a CUDA graph) with x
+        copied in from pinned host memory and y copied back, every step."""
+        torch = self.ctx.torch
+        host = self.x[1024].cpu().pin_memory()
+        out = torch.empty(1024, self.N, dtype=torch.float16).pin_memory()
+        dev = self.x[1024]
+        self.ql(dev)
+        torch.cuda.synchronize()
+        g2 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g2):
+            y = self.ql(dev)
+
+        def one():
+            dev.copy_(host, non_blocking=True)
+            g2.replay()
+            out.copy_(y, non_blocking=True)
+
+        one()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            one()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps, host.numel() * 2, out.numel() * 2
+
+    def gather(self):
+        return 0.0, 0
+
+    @staticmethod
+    def cpu_baseline():
+        """Oracle QuantizedLinear forward: exact fp32 dequantized weight (the
+        reference's w_float) times x in fp32 (numpy BLAS), M = 64 tokens."""
+        from oracle import lq_oracle as O
+        rng = np.random.default_rng(0)
+        K, N, M = 4096, 14336, 64
+        w = O.rnd((rng.standard_normal((N, K)) * 0.02).astype(np.float32), "float16")
+        wi, s, z = O.quantized_linear_quantize_weights(w, "float16", 4, False, 128)
+        x = O.rnd(rng.standard_normal((M, K)).astype(np.float32), "float16")
+        ts = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            wf = O.quantized_linear_dequant_weight(wi, s, "float16", z, "float16", 128, K)
+            _ = x @ wf.T
+            ts.append(time.perf_counter() - t0)
+        t = statistics.median(ts)
+        return {"value": 2.0 * M * K * N / t / 1e12, "unit": "TFLOP/s",
+                "cores": _threads(), "kind": "port",
+                "sample": f"oracle dequant + numpy fp32 matmul, M={M}, K={K}, N={N}, median of 3"}
+
+
 WORKLOADS = {"nf4": NF4Workload, "group": GroupWorkload, "rotquant": RotQuantWorkload,
-             "kv": KVWorkload}
+             "kv": KVWorkload, "w4a16": W4A16Workload}
 
 
 # ─────────────────────────────────────────────────────────────────────────────
@@ -664,7 +764,8 @@ def run_reference(args):
         vals.append(cb["value"])
     v = statistics.median(vals)
     cb["value"] = v
-    line = {"metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": args.gpus,
+    unit = cb["unit"]
+    line = {"metric": METRIC, "value": v, "unit": unit, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": 1e3 * statistics.median(ts), "higher_is_better": True,
             "scaling": "strong" if args.workload in ("nf4", "kv") else "weak",
@@ -672,7 +773,7 @@ def run_reference(args):
             "data": "synthetic (seeded)", "impl": "reference",
             "config": {"workload": W.workload, "sample": cb["sample"]},
             "cpu_baseline": cb,
-            "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
     return 0
 
@@ -705,27 +806,45 @@ def run_ours(args):
     ctx.barrier()
     ck = clocks.stop(set(range(ctx.world))) if ctx.local == 0 else None
     ms = ctx.max(e0.elapsed_time(e1) / args.steps)
+    unit = getattr(W, "unit", "GB/s")
+    scale = 1e12 if unit == "TFLOP/s" else 1e9
     total_bytes = W.bytes_for(W.n_total)
-    value = total_bytes / (ms * 1e-3) / 1e9
+    value = total_bytes / (ms * 1e-3) / scale
     launches = launches_per_step * args.steps
     launches_all = int(ctx.sum(float(launches)))
 
     # dominant kernel, timed alone
     kern = W.kernels()
-    name, (kb, kms, units, unit_name) = max(kern.items(), key=lambda kv: kv[1][1])
-    achieved = kb / (kms * 1e-3) / 1e9
     traffic = NCU_TRAFFIC.get(W.name)
-    roofline = {"bound": "hbm", "kernel": name, "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                "frac": achieved / hbm, "peak_kind": peak_kind,
-                "traffic": traffic if traffic is None else traffic * units,
-                "algorithmic_bytes_per_launch": kb, "launch_ms": kms,
-                "units_per_launch": f"{units} {unit_name}"}
-    kernels = {k: {"ms": v[1], "GB/s": v[0] / (v[1] * 1e-3) / 1e9,
-                   "frac_of_peak": v[0] / (v[1] * 1e-3) / 1e9 / hbm} for k, v in kern.items()}
+    if unit == "TFLOP/s":
+        name = "w4a16_kernel M=1024"
+        fl, kms, m, wb = kern[name]
+        achieved = fl / (kms * 1e-3) / 1e12
+        roofline = {"bound": "tensor", "kernel": name, "achieved": achieved, "peak": tflops,
+                    "unit": "TFLOP/s", "frac": achieved / tflops, "peak_kind": peak_kind,
+                    "traffic": traffic, "algorithmic_flops_per_launch": fl, "launch_ms": kms,
+                    "units_per_launch": f"{m} tokens x 4096 x 14336"}
+        kernels = {}
+        for k, (fl, t, m, wb) in kern.items():
+            tf = fl / (t * 1e-3) / 1e12
+            gbs = wb / (t * 1e-3) / 1e9
+            kernels[k] = {"ms": t, "TFLOP/s": tf, "frac_of_tensor_peak": tf / tflops,
+                          "GB/s": gbs, "frac_of_hbm_peak": gbs / hbm,
+                          "bound": "hbm" if m <= 16 else "tensor"}
+    else:
+        name, (kb, kms, units, unit_name) = max(kern.items(), key=lambda kv: kv[1][1])
+        achieved = kb / (kms * 1e-3) / 1e9
+        roofline = {"bound": "hbm", "kernel": name, "achieved": achieved, "peak": hbm,
+                    "unit": "GB/s", "frac": achieved / hbm, "peak_kind": peak_kind,
+                    "traffic": traffic if traffic is None else traffic * units,
+                    "algorithmic_bytes_per_launch": kb, "launch_ms": kms,
+                    "units_per_launch": f"{units} {unit_name}"}
+        kernels = {k: {"ms": v[1], "GB/s": v[0] / (v[1] * 1e-3) / 1e9,
+                       "frac_of_peak": v[0] / (v[1] * 1e-3) / 1e9 / hbm} for k, v in kern.items()}
 
     e2e_ms, h2d, d2h = W.e2e(max(1, args.e2e_steps), graph)
     e2e_ms = ctx.max(e2e_ms)
-    e2e = {"value": total_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
+    e2e = {"value": total_bytes / (e2e_ms * 1e-3) / scale, "unit": unit,
            "h2d_bytes_per_step": int(ctx.sum(h2d)), "d2h_bytes_per_step": int(ctx.sum(d2h)),
            "ms_per_step": e2e_ms}
     gather_ms, gather_bytes = W.gather()
@@ -736,12 +855,12 @@ def run_ours(args):
         cpu = W.cpu_baseline()
     if ctx.rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": ctx.world,
+            "metric": METRIC, "value": value, "unit": unit, "n_gpus": ctx.world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True,
             "scaling": "strong" if W.name in ("nf4", "kv") else "weak",
             "vs_baseline": None,
-            "dtype": "f32" if W.name == "group" else "bf16",
+            "dtype": {"group": "f32", "w4a16": "f16"}.get(W.name, "bf16"),
             "data": "synthetic (seeded torch.randn on the device)",
             "config": {"workload": W.workload, "parallelism": f"layer-shard x{ctx.world}"
                        if W.name in ("nf4", "kv") else f"independent x{ctx.world}",

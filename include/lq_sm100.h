@@ -84,6 +84,17 @@ int lq_group_quant(const void* x, int x_dtype, int64_t rows, int64_t cols, int64
                    int n_bits, int symmetric, int mode, void* out, int out_dtype,
                    void* scale, void* zero_point, void* stream);
 
+/* ---- fake_quantize backward ------------------------------------------------
+ * grad_x of fake_quantize under autograd (core/quantizer.py:143-185 with
+ * ste_round, core/quantizer.py:32-34): straight-through round, the clamp
+ * mask, and the gradient through the group's scale (min / max, or max |x|,
+ * distributed evenly over tied extrema; zero point has no gradient since it
+ * comes from round).  Groups as in lq_group_quant (rows x cols, groups of
+ * `group` columns, zero padding); PER_TENSOR is rows = 1, cols = group = n. */
+int lq_fake_quant_backward(const void* x, const void* grad_out, int dtype, int64_t rows,
+                           int64_t cols, int64_t group, int n_bits, int symmetric, void* grad_x,
+                           void* stream);
+
 /* ---- token-group (column) quantization --------------------------------------
  * x is [P, T, D] row-major; for every (p, d) the T tokens are cut into
  * ceil(T/tgroup) groups of `tgroup` tokens, zero-padded at the end
@@ -217,6 +228,27 @@ int lq_hadamard(const void* x, int dtype, int64_t rows, int64_t d, void* out, vo
 int lq_hadamard_fake_quant(const void* x, int dtype, int64_t rows, int64_t d, int n_bits,
                            int symmetric, void* out, void* scale, void* zero_point,
                            void* stream);
+
+/* ---- W4A16 QuantizedLinear forward (core/quantizer.py:262-280) ------------------------
+ * Weights: QuantizedLinear's int8 codes [N, K] (n_bits <= 4: asymmetric codes
+ * 0..15 or symmetric -8..7) with per-group scale / zero_point [N, K/group]
+ * (f32 / f16 / bf16).  lq_w4a16_pack builds the kernel's packed operand
+ * (lq_w4a16_packed_bytes() bytes, 16-byte aligned): 4-bit codes in 128-row x
+ * 64-column tiles followed by per-(row, group) (zero + magic, scale) pairs in
+ * the activation dtype.
+ * lq_w4a16_linear: y[M, N] = x[M, K] @ dequant(W)^T + bias, x / y in act_dtype
+ * (LQ_F16 or LQ_BF16), bias fp32 [N] or NULL, fp32 accumulation on the tensor
+ * cores (tcgen05.mma; A = weights dequantized into tensor memory, B =
+ * activations by TMA).  Requires N % 128 == 0, K % 64 == 0, group % 64 == 0.
+ * err (device int, may be NULL) receives a non-zero code if a bounded
+ * device-side wait ran out (the kernel then returns early). */
+size_t lq_w4a16_packed_bytes(int64_t N, int64_t K, int64_t group);
+int lq_w4a16_pack(const int8_t* weight_int, const void* scale, const void* zero_point,
+                  int s_dtype, int64_t N, int64_t K, int64_t group, int symmetric,
+                  int act_dtype, void* packed, void* stream);
+int lq_w4a16_linear(const void* x, int act_dtype, int64_t M, int64_t N, int64_t K,
+                    int64_t group, const void* packed, const float* bias, void* y, int* err,
+                    void* stream);
 
 #ifdef __cplusplus
 }

@@ -53,6 +53,7 @@ _SIGS = {
     "lq_channel_qparams": [_V, _I, _L, _L, _L, _I, _I, _V, _V, _V, ctypes.c_size_t, _V],
     "lq_affine": [_I, _I, _PL, _V, _I, _PL, _V, _I, _PL, _V, _I, _PL, _PI, _I, _I, _V, _I, _V],
     "lq_ste_round": [_V, _I, _L, _V, _V],
+    "lq_fake_quant_backward": [_V, _V, _I, _L, _L, _L, _I, _I, _V, _V],
     "lq_nf4_quantize": [_V, _I, _L, _L, _V, _I, _V, _V],
     "lq_nf4_dequantize": [_V, _I, _L, _L, _V, _I, _V, _V],
     "lq_double_quantize": [_V, _I, _L, _L, _V, _V, _V],
@@ -63,7 +64,7 @@ _SIGS = {
     "lq_hadamard": [_V, _I, _L, _L, _V, _V],
     "lq_hadamard_fake_quant": [_V, _I, _L, _L, _I, _I, _V, _V, _V, _V],
     "lq_w4a16_pack": [_V, _V, _V, _I, _L, _L, _L, _I, _I, _V, _V],
-    "lq_w4a16_linear": [_V, _I, _L, _L, _L, _L, _V, _V, _V, _V],
+    "lq_w4a16_linear": [_V, _I, _L, _L, _L, _L, _V, _V, _V, _V, _V],
 }
 _SIZE_SIGS = {
     "lq_tensor_qparams_workspace_size": [_L],

@@ -1,11 +1,79 @@
-"""W4A16 dispatch for QuantizedLinear.forward (filled in with the tensor-core kernel)."""
+"""W4A16 dispatch for QuantizedLinear.forward on the tensor cores.
+
+Used when the activations are float16 / bfloat16 and the layer holds
+group-quantized codes of at most 4 bits with a group size that is a multiple
+of 64, in_features % 64 == 0 and out_features % 128 == 0 (the Llama-style
+projection shapes).  The packed operand (4-bit codes in the kernel's tile
+order + per-group (zero, scale) pairs) is built once per activation dtype
+and cached on the module; it is dropped whenever the weights change.
+"""
+
+from __future__ import annotations
 
 import torch
 
+from .. import _C
+
+_ERR = {}
+
+
+def _err_flag(device) -> torch.Tensor:
+    t = _ERR.get(device)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=device)
+        _ERR[device] = t
+    return t
+
+
+def check_error_flag(device) -> int:
+    """Non-zero if a W4A16 launch on `device` hit a device-side wait timeout
+    (reads the flag: synchronizes the device)."""
+    t = _ERR.get(device)
+    return 0 if t is None else int(t.item())
+
 
 def eligible(ql, x: torch.Tensor) -> bool:
-    return False
+    return (x.is_cuda and x.dtype in (torch.float16, torch.bfloat16)
+            and ql.weight_int.is_cuda and ql.n_bits <= 4 and ql.group_size > 0
+            and ql.group_size % 64 == 0 and ql.in_features % ql.group_size == 0
+            and ql.in_features % 64 == 0 and ql.out_features % 128 == 0
+            and x.shape[-1] == ql.in_features
+            and ql.scale.dim() == 2 and ql.scale.shape[1] == ql.in_features // ql.group_size)
+
+
+def packed_operand(ql, act_dtype: torch.dtype) -> torch.Tensor:
+    """Build (or fetch the cached) packed weight operand for `act_dtype`."""
+    dev = ql.weight_int.device
+    cached = ql._w4
+    if cached is not None and cached[0] == act_dtype and cached[1] == dev:
+        return cached[2]
+    N, K, G = ql.out_features, ql.in_features, ql.group_size
+    nbytes = _C.lib().lq_w4a16_packed_bytes(N, K, G)
+    packed = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    wi = ql.weight_int.contiguous()
+    s = ql.scale.contiguous()
+    z = ql.zero_point.to(s.dtype).contiguous()
+    _C.call("lq_w4a16_pack", wi.data_ptr(), s.data_ptr(), z.data_ptr(), _C.dt(s), N, K, G,
+            int(ql.symmetric), _C.dt(act_dtype), packed.data_ptr(), _C.stream_ptr(wi))
+    ql._w4 = (act_dtype, dev, packed)
+    return packed
 
 
 def linear(ql, x: torch.Tensor) -> torch.Tensor:
-    raise NotImplementedError
+    """y = x @ dequant(W)^T + bias with the fused W4A16 kernel."""
+    packed = packed_operand(ql, x.dtype)
+    N, K = ql.out_features, ql.in_features
+    x2 = x.reshape(-1, K)
+    if not x2.is_contiguous() or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    M = x2.shape[0]
+    y = torch.empty(M, N, dtype=x.dtype, device=x.device)
+    bias = None
+    if ql.bias is not None:
+        bias = ql.bias.detach()
+        if bias.dtype != torch.float32 or not bias.is_contiguous():
+            bias = bias.float().contiguous()
+    _C.call("lq_w4a16_linear", x2.data_ptr(), _C.dt(x2), M, N, K, ql.group_size,
+            packed.data_ptr(), _C.ptr(bias), y.data_ptr(), _err_flag(x.device).data_ptr(),
+            _C.stream_ptr(x2))
+    return y.reshape(*x.shape[:-1], N)

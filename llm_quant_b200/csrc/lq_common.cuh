@@ -133,32 +133,41 @@ __device__ __forceinline__ int32_t tcast_i32(float v) {
   return static_cast<int32_t>(v);
 }
 
-// NaN-propagating min/max accumulators.
+// NaN-propagating min / max (PTX min.NaN / max.NaN: a NaN operand gives NaN),
+// the semantics of torch.amin / torch.amax.
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float fmin_nan(float a, float b) {
+  float r;
+  asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+// Min / max accumulator; NaN anywhere makes both NaN.  For symmetric
+// quantization only mx is used (fed |x|), so its shuffles skip mn.
 struct MinMax {
   float mn, mx;
-  int nan;
   __device__ __forceinline__ void init() {
     mn = __int_as_float(0x7f800000);
     mx = __int_as_float(0xff800000);
-    nan = 0;
   }
   __device__ __forceinline__ void add(float v) {
-    mn = fminf(mn, v);
-    mx = fmaxf(mx, v);
-    nan |= (v != v);
+    mn = fmin_nan(mn, v);
+    mx = fmax_nan(mx, v);
   }
+  __device__ __forceinline__ void add_max(float v) { mx = fmax_nan(mx, v); }
   __device__ __forceinline__ void merge(const MinMax& o) {
-    mn = fminf(mn, o.mn);
-    mx = fmaxf(mx, o.mx);
-    nan |= o.nan;
+    mn = fmin_nan(mn, o.mn);
+    mx = fmax_nan(mx, o.mx);
   }
-  __device__ __forceinline__ void shfl_xor_merge(int mask, unsigned active = 0xffffffffu) {
-    MinMax o;
-    o.mn = __shfl_xor_sync(active, mn, mask);
-    o.mx = __shfl_xor_sync(active, mx, mask);
-    o.nan = __shfl_xor_sync(active, nan, mask);
-    merge(o);
+  __device__ __forceinline__ void shfl_xor_merge(int mask, bool max_only = false) {
+    if (!max_only) mn = fmin_nan(mn, __shfl_xor_sync(0xffffffffu, mn, mask));
+    mx = fmax_nan(mx, __shfl_xor_sync(0xffffffffu, mx, mask));
   }
+  __device__ __forceinline__ bool has_nan() const { return (mn != mn) || (mx != mx); }
 };
 
 // Scale / zero point from a group's reduction (core/quantizer.py:64-104,
@@ -167,15 +176,13 @@ struct MinMax {
 template <typename T>
 __device__ __forceinline__ void qparams_from(const MinMax& r, bool sym, float qmin, float qmax,
                                              float lo_T, float& scale, float& zp) {
-  const float qnan = __int_as_float(0x7fc00000);
   if (sym) {
-    float amax = r.nan ? qnan : r.mx;
-    amax = (amax < lo_T) ? lo_T : amax;  // clamp(min=1e-12) in T
+    float amax = r.mx;
+    amax = (amax < lo_T) ? lo_T : amax;  // clamp(min=1e-12) in T; NaN passes
     scale = tdiv<T>(amax, qmax);
     zp = 0.0f;
   } else {
-    float mn = r.nan ? qnan : r.mn;
-    float mx = r.nan ? qnan : r.mx;
+    const float mn = r.mn, mx = r.mx;  // both NaN if the group holds a NaN
     float rng = tsub<T>(mx, mn);
     rng = (rng < lo_T) ? lo_T : rng;
     scale = tdiv<T>(rng, qmax - qmin);

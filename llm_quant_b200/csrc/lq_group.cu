@@ -122,7 +122,10 @@ struct Tile {
     for (int k = 0; k < NVT; ++k) {
       if (inb & (1u << k)) {
 #pragma unroll
-        for (int i = 0; i < V; ++i) r.add(sym ? fabsf(v[k * V + i]) : v[k * V + i]);
+        for (int i = 0; i < V; ++i) {
+          if (sym) r.add_max(fabsf(v[k * V + i]));
+          else r.add(v[k * V + i]);
+        }
       }
     }
   }
@@ -170,7 +173,7 @@ __global__ void __launch_bounds__(256) group_warp_kernel(const T* __restrict__ x
     else tile.inb = 0;
     MinMax r;
     tile.reduce_local(r, a.sym);
-    for (int m = 1; m < tps; m <<= 1) r.shfl_xor_merge(m);
+    for (int m = 1; m < tps; m <<= 1) r.shfl_xor_merge(m, a.sym);
     if (!live) continue;
     float scale, zp;
     qparams_from<T>(r, a.sym, a.qmin, a.qmax, a.lo, scale, zp);
@@ -184,8 +187,8 @@ __global__ void __launch_bounds__(256) group_warp_kernel(const T* __restrict__ x
 }
 
 // Block-wide NaN-aware min/max reduction; result broadcast to all threads.
-__device__ __forceinline__ MinMax block_reduce(MinMax r, MinMax* sm) {
-  for (int m = 16; m >= 1; m >>= 1) r.shfl_xor_merge(m);
+__device__ __forceinline__ MinMax block_reduce(MinMax r, MinMax* sm, bool sym) {
+  for (int m = 16; m >= 1; m >>= 1) r.shfl_xor_merge(m, sym);
   const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
   __syncthreads();  // sm may still be read from the previous group
   if ((threadIdx.x & 31) == 0) sm[w] = r;
@@ -210,7 +213,7 @@ __global__ void __launch_bounds__(1024) group_block_kernel(const T* __restrict__
     tile.load(x, row, gcol0, a, t, tps);
     MinMax r;
     tile.reduce_local(r, a.sym);
-    r = block_reduce(r, sm);
+    r = block_reduce(r, sm, a.sym);
     float scale, zp;
     qparams_from<T>(r, a.sym, a.qmin, a.qmax, a.lo, scale, zp);
     if (t == 0 && scale_out) {
@@ -238,9 +241,10 @@ __global__ void __launch_bounds__(1024) group_stream_kernel(const T* __restrict_
     r.init();
     for (int64_t e = threadIdx.x; e < a.G; e += blockDim.x) {
       float v = (gcol0 + e < a.cols) ? Ty<T>::to_f(base[e]) : 0.0f;
-      r.add(a.sym ? fabsf(v) : v);
+      if (a.sym) r.add_max(fabsf(v));
+      else r.add(v);
     }
-    r = block_reduce(r, sm);
+    r = block_reduce(r, sm, a.sym);
     float scale, zp;
     qparams_from<T>(r, a.sym, a.qmin, a.qmax, a.lo, scale, zp);
     if (threadIdx.x == 0 && scale_out) {
@@ -286,13 +290,24 @@ int dispatch(const T* x, const GroupArgs& a, OutT* out, T* s, T* z, bool vec_ok,
   const int64_t G = a.G;
   if (vec_ok) {
     const int64_t nv = G / V;  // vectors per group
-    if (nv <= 32) {
-      int tps = 1;
-      while (tps < nv) tps <<= 1;
-      return launch_warp<T, MODE, OutT, 1, true>(x, a, tps, out, s, z, st);
+    // up to 4 vectors (64 bytes) in flight per lane, teams of <= 32 lanes
+    int nvt = 1;
+    while (nvt < 4 && nvt * 2 <= nv) nvt *= 2;
+    int64_t need = (nv + nvt - 1) / nvt;
+    if (need > 32) {
+      nvt = 8;
+      need = (nv + 7) / 8;
     }
-    if (nv <= 64) return launch_warp<T, MODE, OutT, 2, true>(x, a, 32, out, s, z, st);
-    if (nv <= 128) return launch_warp<T, MODE, OutT, 4, true>(x, a, 32, out, s, z, st);
+    if (need <= 32) {
+      int tps = 1;
+      while (tps < need) tps <<= 1;
+      switch (nvt) {
+        case 1: return launch_warp<T, MODE, OutT, 1, true>(x, a, tps, out, s, z, st);
+        case 2: return launch_warp<T, MODE, OutT, 2, true>(x, a, tps, out, s, z, st);
+        case 4: return launch_warp<T, MODE, OutT, 4, true>(x, a, tps, out, s, z, st);
+        default: return launch_warp<T, MODE, OutT, 8, true>(x, a, tps, out, s, z, st);
+      }
+    }
     // block teams: up to 1024 threads x 2 vectors in registers
     for (int threads = 128; threads <= 1024; threads *= 2) {
       if (nv <= (int64_t)threads * 2) {
@@ -386,4 +401,156 @@ extern "C" int lq_group_quant(const void* x, int x_dtype, int64_t rows, int64_t 
   LQ_REQUIRE(mode != LQ_MODE_QPARAMS || scale, LQ_EINVAL, "QPARAMS mode needs scale/zero_point");
   return lq::group_quant_remap(x, x_dtype, rows, cols, group, n_bits, symmetric, mode, out,
                                out_dtype, scale, zero_point, stream, rows, rows, 0, rows, 0);
+}
+
+// ---------------------------------------------------------------------------
+// fake_quantize backward (core/quantizer.py:143-185 under autograd).
+// Per group (zero padding included in the reductions, its gradient dropped):
+//   y = (clamp(ste(x/s + zp)) - zp) * s,  s = clamp_min(mx - mn, lo) / (qmax - qmin)
+//   (symmetric: s = clamp_min(max|x|, lo) / qmax, zp = 0); zp has no gradient
+//   (it comes from round).  With m_i the clamp mask and c_i the clamped code:
+//   direct_i = (g_i * s) * m_i / s
+//   ds       = sum_i g_i * (c_i - zp)  +  sum_i -(g_i * s * m_i) * ((x_i / s) / s)
+//   d_rng    = ds / (qmax - qmin) if mx - mn >= lo else 0   (symmetric: / qmax)
+//   dx_i     = direct_i + [x_i == mx] d_rng / #max - [x_i == mn] d_rng / #min
+//              (symmetric: + sign(x_i) [|x_i| == max|x|] d_rng / #max)
+// Each elementwise op rounds to T as torch does; sums accumulate in fp32.
+// One block per group, three passes over the group (L2-resident).
+// ---------------------------------------------------------------------------
+namespace lq {
+namespace {
+
+template <typename T>
+__global__ void __launch_bounds__(256) fq_backward_kernel(const T* __restrict__ x,
+                                                          const T* __restrict__ g, GroupArgs a,
+                                                          T* __restrict__ dx) {
+  __shared__ MinMax sm[32];
+  __shared__ float red[3][32];
+  for (int64_t grp = blockIdx.x; grp < a.total_groups; grp += gridDim.x) {
+    const int64_t row = grp / a.groups_per_row;
+    const int64_t c0 = (grp % a.groups_per_row) * a.G;
+    const T* xb = x + row * a.cols + c0;
+    const T* gb = g + row * a.cols + c0;
+    T* db = dx + row * a.cols + c0;
+    const int64_t valid = min(a.G, a.cols - c0);
+    // pass 1: min / max (padding zeros included)
+    MinMax r;
+    r.init();
+    for (int64_t e = threadIdx.x; e < a.G; e += blockDim.x) {
+      const float v = e < valid ? Ty<T>::to_f(xb[e]) : 0.0f;
+      if (a.sym) r.add_max(fabsf(v));
+      else r.add(v);
+    }
+    r = block_reduce(r, sm, a.sym);
+    float s, zp;
+    qparams_from<T>(r, a.sym, a.qmin, a.qmax, a.lo, s, zp);
+    // pass 2: tie counts and the two sums of the scale gradient
+    float cmax = 0.f, cmin = 0.f, s1 = 0.f, s2 = 0.f;
+    for (int64_t e = threadIdx.x; e < a.G; e += blockDim.x) {
+      const bool in = e < valid;
+      const float v = in ? Ty<T>::to_f(xb[e]) : 0.0f;
+      const float gv = in ? Ty<T>::to_f(gb[e]) : 0.0f;
+      if (a.sym) {
+        cmax += (fabsf(v) == r.mx) ? 1.f : 0.f;
+      } else {
+        cmax += (v == r.mx) ? 1.f : 0.f;
+        cmin += (v == r.mn) ? 1.f : 0.f;
+      }
+      const float t = tadd<T>(tdiv<T>(v, s), zp);
+      const float q = tste(t);
+      const bool m = (q >= a.qmin) && (q <= a.qmax);
+      const float c = tclamp(q, a.qmin, a.qmax);
+      s1 += tmul<T>(gv, tsub<T>(c, zp));
+      const float du = m ? tmul<T>(gv, s) : 0.0f;
+      s2 += tmul<T>(-du, tdiv<T>(tdiv<T>(v, s), s));
+    }
+    float vals[3] = {cmax, cmin, __fadd_rn(s1, s2)};
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      for (int o = 16; o >= 1; o >>= 1) vals[k] += __shfl_xor_sync(0xffffffffu, vals[k], o);
+    }
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) {
+      red[0][threadIdx.x >> 5] = vals[0];
+      red[1][threadIdx.x >> 5] = vals[1];
+      red[2][threadIdx.x >> 5] = vals[2];
+    }
+    __syncthreads();
+    float tot[3] = {0.f, 0.f, 0.f};
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+      tot[0] += red[0][w];
+      tot[1] += red[1][w];
+      tot[2] += red[2][w];
+    }
+    const float ds = Ty<T>::round(tot[2]);
+    float drng;
+    if (a.sym) {
+      const bool pass = r.mx >= a.lo;  // clamp_min backward mask
+      drng = pass ? tdiv<T>(ds, a.qmax) : 0.0f;
+    } else {
+      const bool pass = tsub<T>(r.mx, r.mn) >= a.lo;
+      drng = pass ? tdiv<T>(ds, a.qmax - a.qmin) : 0.0f;
+    }
+    const float dmax = tdiv<T>(drng, tot[0]);
+    const float dmin = a.sym ? 0.0f : tdiv<T>(-drng, tot[1]);
+    // pass 3: the gradient of every real (non-padding) element
+    for (int64_t e = threadIdx.x; e < valid; e += blockDim.x) {
+      const float v = Ty<T>::to_f(xb[e]);
+      const float gv = Ty<T>::to_f(gb[e]);
+      const float t = tadd<T>(tdiv<T>(v, s), zp);
+      const float q = tste(t);
+      const bool m = (q >= a.qmin) && (q <= a.qmax);
+      float d = m ? tdiv<T>(tmul<T>(gv, s), s) : 0.0f;
+      if (a.sym) {
+        if (fabsf(v) == r.mx) d = tadd<T>(d, tmul<T>(dmax, v > 0.f ? 1.f : (v < 0.f ? -1.f : 0.f)));
+      } else {
+        if (v == r.mx) d = tadd<T>(d, dmax);
+        if (v == r.mn) d = tadd<T>(d, dmin);
+      }
+      db[e] = Ty<T>::from_f(d);
+    }
+    __syncthreads();
+  }
+}
+
+template <typename T>
+int fq_backward_t(const void* x, const void* g, int64_t rows, int64_t cols, int64_t G, int n_bits,
+                  int sym, void* dx, cudaStream_t st) {
+  GroupArgs a;
+  a.rows = rows;
+  a.cols = cols;
+  a.G = G;
+  a.groups_per_row = (cols + G - 1) / G;
+  a.total_groups = rows * a.groups_per_row;
+  a.qmin = (float)qmin_of(n_bits, sym);
+  a.qmax = (float)qmax_of(n_bits, sym);
+  a.lo = lo_clamp_value<T>();
+  a.sym = sym;
+  a.rpp = a.opitch = a.spitch = rows;
+  a.ooff = a.soff = 0;
+  int64_t want = a.total_groups;
+  int grid = (int)(want < (int64_t)num_sms() * 16 ? want : (int64_t)num_sms() * 16);
+  fq_backward_kernel<T><<<grid, 256, 0, st>>>(static_cast<const T*>(x), static_cast<const T*>(g),
+                                              a, static_cast<T*>(dx));
+  return launched("fq_backward_kernel");
+}
+
+}  // namespace
+}  // namespace lq
+
+extern "C" int lq_fake_quant_backward(const void* x, const void* grad_out, int dtype, int64_t rows,
+                                      int64_t cols, int64_t group, int n_bits, int symmetric,
+                                      void* grad_x, void* stream) {
+  using namespace lq;
+  LQ_REQUIRE(rows >= 0 && cols >= 0 && group >= 1, LQ_EINVAL, "bad shape");
+  LQ_REQUIRE(n_bits >= 1 && n_bits <= 16, LQ_EINVAL, "n_bits out of range");
+  if (rows == 0 || cols == 0) return LQ_OK;
+  LQ_REQUIRE(x && grad_out && grad_x, LQ_EINVAL, "NULL pointer");
+  cudaStream_t st = as_stream(stream);
+  switch (dtype) {
+    case LQ_F32: return fq_backward_t<float>(x, grad_out, rows, cols, group, n_bits, symmetric, grad_x, st);
+    case LQ_F16: return fq_backward_t<__half>(x, grad_out, rows, cols, group, n_bits, symmetric, grad_x, st);
+    case LQ_BF16: return fq_backward_t<__nv_bfloat16>(x, grad_out, rows, cols, group, n_bits, symmetric, grad_x, st);
+    default: set_error("unsupported dtype %d", dtype); return LQ_EDTYPE;
+  }
 }

@@ -97,7 +97,10 @@ __device__ __forceinline__ void finish_and_quant(float* v, const FhtArgs& a, Min
   if constexpr (QUANT) {
     r.init();
 #pragma unroll
-    for (int i = 0; i < E; ++i) r.add(a.sym ? fabsf(v[i]) : v[i]);
+    for (int i = 0; i < E; ++i) {
+      if (a.sym) r.add_max(fabsf(v[i]));
+      else r.add(v[i]);
+    }
   }
 }
 
@@ -137,7 +140,7 @@ __global__ void __launch_bounds__(256) fht_warp_kernel(const T* __restrict__ x, 
     MinMax r;
     finish_and_quant<T, E, QUANT>(v, a, r);
     if constexpr (QUANT) {
-      for (int m = 1; m < tps; m <<= 1) r.shfl_xor_merge(m);
+      for (int m = 1; m < tps; m <<= 1) r.shfl_xor_merge(m, a.sym);
       float scale, zp;
       qparams_from<T>(r, a.sym, a.qmin, a.qmax, a.lo, scale, zp);
       if (live && t == 0 && scale_out) {
@@ -204,7 +207,7 @@ __global__ void __launch_bounds__(1024) fht_block_kernel(const T* __restrict__ x
     }
     float scale = 0.f, zp = 0.f;
     if constexpr (QUANT) {
-      for (int mm = 16; mm >= 1; mm >>= 1) r.shfl_xor_merge(mm);
+      for (int mm = 16; mm >= 1; mm >>= 1) r.shfl_xor_merge(mm, a.sym);
       if (lane == 0) red[t >> 5] = r;
     }
     __syncthreads();

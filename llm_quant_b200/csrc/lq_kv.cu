@@ -87,11 +87,13 @@ __global__ void __launch_bounds__(256) token_group_kernel(const T* __restrict__ 
 #pragma unroll
           for (int i = 0; i < V; ++i) {
             float v = Ty<T>::to_f(u.v[i]);
-            r[i].add(a.sym ? fabsf(v) : v);
+            if (a.sym) r[i].add_max(fabsf(v));
+            else r[i].add(v);
           }
         } else {
           float v = Ty<T>::to_f(*src);
-          r[0].add(a.sym ? fabsf(v) : v);
+          if (a.sym) r[0].add_max(fabsf(v));
+          else r[0].add(v);
         }
       }
       // zero padding of the last token group takes part in min/max

@@ -138,7 +138,6 @@ __global__ void __launch_bounds__(256) nf4_quant_kernel(const T* __restrict__ x,
       float v[NVT * V];
       const int64_t e0 = g * a.G;
       float am = 0.0f;
-      int nan = 0;
 #pragma unroll
       for (int k = 0; k < NVT; ++k) {
         const int64_t e = e0 + (int64_t)(k * tps + t) * V;
@@ -152,17 +151,11 @@ __global__ void __launch_bounds__(256) nf4_quant_kernel(const T* __restrict__ x,
           for (int i = 0; i < V; ++i) v[k * V + i] = (live && e + i < a.n) ? Ty<T>::to_f(x[e + i]) : 0.0f;
         }
 #pragma unroll
-        for (int i = 0; i < V; ++i) {
-          am = fmaxf(am, fabsf(v[k * V + i]));
-          nan |= v[k * V + i] != v[k * V + i];
-        }
+        for (int i = 0; i < V; ++i) am = fmax_nan(am, fabsf(v[k * V + i]));
       }
-      for (int m = 1; m < tps; m <<= 1) {
-        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, m));
-        nan |= __shfl_xor_sync(0xffffffffu, nan, m);
-      }
+      for (int m = 1; m < tps; m <<= 1) am = fmax_nan(am, __shfl_xor_sync(0xffffffffu, am, m));
       if (live) {
-        float s = nan ? __int_as_float(0x7fc00000) : am;
+        float s = am;               // NaN if the group holds a NaN
         s = (s < a.lo) ? a.lo : s;  // clamp(min=1e-12) in T
         const float sr = Ty<T>::round(s);  // absmax is already a T value
         if (t == 0) {
@@ -194,7 +187,7 @@ __global__ void __launch_bounds__(256) nf4_quant_kernel(const T* __restrict__ x,
       __syncthreads();
       MinMax tot = red[0];
       for (int w = 1; w < (int)(blockDim.x >> 5); ++w) tot.merge(red[w]);
-      float dq = tot.nan ? __int_as_float(0x7fc00000) : fmaxf(tot.mx, 0.0f);
+      float dq = fmax_nan(tot.mx, 0.0f);  // zero padding of a partial super-group
       dq = (dq < a.lo) ? a.lo : dq;
       if (threadIdx.x == 0) dq_scales[sg] = Ty<T>::from_f(dq);
       for (int j = threadIdx.x; j < cnt; j += blockDim.x) {
@@ -228,7 +221,7 @@ __global__ void __launch_bounds__(256) nf4_scales_kernel(const T* __restrict__ x
     __syncthreads();
     MinMax tot = red[0];
     for (int w = 1; w < (int)(blockDim.x >> 5); ++w) tot.merge(red[w]);
-    float s = tot.nan ? __int_as_float(0x7fc00000) : fmaxf(tot.mx, 0.0f);
+    float s = fmax_nan(tot.mx, 0.0f);
     s = (s < a.lo) ? a.lo : s;
     if (threadIdx.x == 0) scales[g] = Ty<T>::from_f(s);
   }
@@ -378,7 +371,7 @@ __global__ void __launch_bounds__(256) double_quant_kernel(const T* __restrict__
     __syncthreads();
     MinMax tot = red[0];
     for (int w = 1; w < (int)(blockDim.x >> 5); ++w) tot.merge(red[w]);
-    float m = tot.nan ? __int_as_float(0x7fc00000) : fmaxf(tot.mx, 0.0f);  // padding zeros
+    float m = fmax_nan(tot.mx, 0.0f);  // padding zeros
     m = (m < lo) ? lo : m;
     if (threadIdx.x == 0) dq[d] = Ty<T>::from_f(m);
     for (int64_t j = b + threadIdx.x; j < e; j += blockDim.x) {

@@ -1,0 +1,563 @@
+// lq_w4a16.cu -- QuantizedLinear W4A16 forward on the 5th-generation tensor cores.
+//
+// y[M, N] = x[M, K] @ W^T + bias, W = (q - zero) * scale per group of the K
+// dim (core/quantizer.py:262-280 dequantizes the whole weight to fp32 and
+// calls F.linear; here the dequantization is fused into the GEMM).
+//
+// Tile = 128 weight rows x BT tokens ("swap AB"): the dequantized weights are
+// the MMA's A operand and live in tensor memory, the activations are the B
+// operand (TMA, 128-byte swizzle, K-major), the fp32 accumulator D[128, BT]
+// is in tensor memory.  Warp roles (192 threads):
+//   warp 0      TMA producer: activation tile + packed 4-bit weight tile +
+//               (zero, scale) pairs per stage, one mbarrier per stage each;
+//   warp 1      allocates tensor memory, one lane issues tcgen05.mma
+//               (4 x K=16 per 64-wide K step) and tcgen05.commit;
+//   warps 2..5  dequantize: thread = one weight row, 64 codes per stage ->
+//               32 packed fp16/bf16 pairs -> tcgen05.st into the A slot of
+//               the stage; afterwards they are the epilogue (tcgen05.ld of
+//               the accumulator, + bias, convert, store y).
+// Warp w may only touch tensor-memory lanes 32*(w%4)..+31, so warps 2,3,4,5
+// own weight rows 64..95, 96..127, 0..31, 32..63 of the tile.
+//
+// Every mbarrier wait is bounded; on timeout the kernel records an error
+// code in *err (when given), drains its outstanding copies (bounded), frees
+// its tensor memory and returns.
+#include "lq_common.cuh"
+
+namespace lq {
+namespace {
+
+constexpr int kBK = 64;           // K per stage (128 bytes of fp16)
+constexpr int kRows = 128;        // weight rows per tile (UMMA M)
+constexpr int kWStage = kRows * kBK / 2;  // packed codes per stage: 4 KB
+constexpr int kSStage = kRows * 4;        // (zero, scale) pairs per stage: 512 B
+constexpr int kAcol = 256;        // first TMEM column of the A slots
+constexpr uint32_t kTmemCols = 512;
+constexpr uint64_t kWaitNs = 2000000000ull;  // bounded waits give up after 2 s
+
+// ---- PTX wrappers ----------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count));
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait; false once kWaitNs of wall time has passed.
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity) {
+  if (mbar_try(b, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try(b, parity)) return true;
+    if ((i & 255) == 0 && global_ns() - t0 > kWaitNs) return false;
+  }
+}
+// Warp-uniform bounded wait (every lane polls; all agree on the outcome).
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* b, uint32_t parity) {
+  return __all_sync(0xffffffffu, mbar_wait(b, parity));
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t* b) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(b))
+               : "memory");
+}
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st32(uint32_t addr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
+      "%29, %30, %31, %32};" ::"r"(addr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+      "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
+      "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t addr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+      "%30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
+        "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
+        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(addr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory descriptor of a K-major, 128-byte-swizzled tile (rows of 128
+// bytes, 8-row groups 1024 bytes apart), sm100 format.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFF) >> 4);  // start address
+  d |= (uint64_t)1 << 16;                   // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;         // stride byte offset
+  d |= (uint64_t)1 << 46;                   // descriptor version (sm100)
+  d |= (uint64_t)2 << 61;                   // SWIZZLE_128B
+  return d;
+}
+
+// kind::f16 instruction descriptor: D fp32, A/B fp16 (fmt 0) or bf16 (fmt 1),
+// both K-major, M = 128, N = BT.
+__host__ __device__ constexpr uint32_t make_idesc(int fmt, int bt) {
+  return (1u << 4) | ((uint32_t)fmt << 7) | ((uint32_t)fmt << 10) | ((uint32_t)(bt >> 3) << 17) |
+         ((uint32_t)(kRows >> 4) << 24);
+}
+
+template <typename T> struct Act;
+template <> struct Act<__half> {
+  static constexpr int fmt = 0;
+  static constexpr uint32_t magic = 0x64006400u;  // fp16 1024.0 in both halves
+  __device__ __forceinline__ static uint32_t sub_mul(uint32_t v, uint32_t zb, uint32_t s) {
+    __half2 h = __hsub2(*reinterpret_cast<__half2*>(&v), *reinterpret_cast<__half2*>(&zb));
+    h = __hmul2(h, *reinterpret_cast<__half2*>(&s));
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+};
+template <> struct Act<__nv_bfloat16> {
+  static constexpr int fmt = 1;
+  static constexpr uint32_t magic = 0x43004300u;  // bf16 128.0 in both halves
+  __device__ __forceinline__ static uint32_t sub_mul(uint32_t v, uint32_t zb, uint32_t s) {
+    __nv_bfloat162 h = __hsub2(*reinterpret_cast<__nv_bfloat162*>(&v), *reinterpret_cast<__nv_bfloat162*>(&zb));
+    h = __hmul2(h, *reinterpret_cast<__nv_bfloat162*>(&s));
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+};
+
+struct W4Args {
+  int M, N, K, group, n_kb, n_groups;
+};
+
+template <typename T, int BT, int S>
+struct Smem {
+  static constexpr int kX = BT * kBK * 2;  // activation tile bytes per stage
+  static constexpr int off_x = 0;
+  static constexpr int off_w = off_x + S * kX;
+  static constexpr int off_s = off_w + S * kWStage;
+  static constexpr int off_bar = off_s + S * kSStage;
+  // barriers: full_x[S], full_w[S], a_full[S], empty[S], acc_full
+  static constexpr int n_bar = 4 * S + 1;
+  static constexpr int off_tmem = off_bar + n_bar * 8;
+  static constexpr int bytes = off_tmem + 16 + 1024;  // + alignment slack
+};
+
+template <typename T, int BT, int S>
+__global__ void __launch_bounds__(192, 1) w4a16_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                                                       const uint8_t* __restrict__ packed,
+                                                       const float* __restrict__ bias,
+                                                       T* __restrict__ y, W4Args a,
+                                                       int* __restrict__ err) {
+  using L = Smem<T, BT, S>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::off_bar);
+  uint64_t* full_x = bars;
+  uint64_t* full_w = bars + S;
+  uint64_t* a_full = bars + 2 * S;
+  uint64_t* empty = bars + 3 * S;
+  uint64_t* acc_full = bars + 4 * S;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::off_tmem);
+  __shared__ int s_err;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nt = blockIdx.x;       // weight-row tile
+  const int m0 = blockIdx.y * BT;  // first token of the tile
+  const uint8_t* wtile = packed + (size_t)nt * a.n_kb * kWStage;
+  const uint8_t* stile = packed + (size_t)(a.N / kRows) * a.n_kb * kWStage +
+                         (size_t)nt * a.n_groups * kSStage;
+
+  if (threadIdx.x == 0) {
+    s_err = 0;
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full_x[i], 1);
+      mbar_init(&full_w[i], 1);
+      mbar_init(&a_full[i], 128);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(acc_full, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_x)) : "memory");
+      int issued = 0;
+      for (int i = 0; i < a.n_kb; ++i) {
+        const int s = i % S;
+        if (i >= S && !mbar_wait(&empty[s], ((i / S) - 1) & 1)) { s_err = 1; break; }
+        if (s_err) break;
+        mbar_expect_tx(&full_x[s], L::kX);
+        tma_load_2d(smem + L::off_x + s * L::kX, &tmap_x, i * kBK, m0, &full_x[s]);
+        mbar_expect_tx(&full_w[s], kWStage + kSStage);
+        bulk_load(smem + L::off_w + s * kWStage, wtile + (size_t)i * kWStage, kWStage, &full_w[s]);
+        const int g = (i * kBK) / a.group;
+        bulk_load(smem + L::off_s + s * kSStage, stile + (size_t)g * kSStage, kSStage, &full_w[s]);
+        issued = i + 1;
+      }
+      if (s_err) {
+        // drain: wait (bounded) for every stage this thread may still have in flight
+        for (int i = (issued > S ? issued - S : 0); i < issued; ++i) {
+          mbar_wait(&full_x[i % S], (i / S) & 1);
+          mbar_wait(&full_w[i % S], (i / S) & 1);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    bool issued_any = false;
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc(Act<T>::fmt, BT);
+      for (int i = 0; i < a.n_kb; ++i) {
+        const int s = i % S;
+        const uint32_t ph = (i / S) & 1;
+        if (!mbar_wait(&full_x[s], ph) || !mbar_wait(&a_full[s], ph)) { s_err = 2; break; }
+        tc_fence_after();
+        const uint32_t xs = smem_u32(smem + L::off_x + s * L::kX);
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk) {
+          const uint64_t bdesc = sw128_desc(xs + kk * 32);
+          const uint32_t acol = tmem + kAcol + s * (kBK / 2) + kk * 8;
+          tc_mma(tmem, acol, bdesc, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc_commit(&empty[s]);  // frees the activation stage and the A slot
+        issued_any = true;
+      }
+      if (issued_any) tc_commit(acc_full);
+      if (s_err && issued_any) mbar_wait(acc_full, 0);  // MMAs in flight must finish before dealloc
+    }
+    __syncwarp();
+  } else {
+    // ---------------- dequantization (warps 2..5), then epilogue ----------------
+    const int q = warp & 3;          // tensor-memory lane quarter
+    const int row = q * 32 + lane;   // weight row within the tile
+    const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+    bool ok = true;
+    for (int i = 0; i < a.n_kb && ok; ++i) {
+      const int s = i % S;
+      const uint32_t ph = (i / S) & 1;
+      if (!mbar_wait_warp(&full_w[s], ph)) { ok = false; break; }
+      if (i >= S && !mbar_wait_warp(&empty[s], ph ^ 1)) { ok = false; break; }
+      const uint4* src = reinterpret_cast<const uint4*>(smem + L::off_w + s * kWStage + row * 32);
+      const uint4 c0 = src[0], c1 = src[1];
+      const uint32_t zs = *reinterpret_cast<const uint32_t*>(smem + L::off_s + s * kSStage + row * 4);
+      // zs = (zero_b, scale) as a T pair; broadcast each half to both halves
+      const uint32_t zb = __byte_perm(zs, zs, 0x1010);
+      const uint32_t sc = __byte_perm(zs, zs, 0x3232);
+      const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+      uint32_t r[32];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          // nibbles (4p, 16+4p) of word j are k = 8j+2p (low half), 8j+2p+1 (high half)
+          const uint32_t v = ((w[j] >> (4 * p)) & 0x000F000Fu) | Act<T>::magic;
+          r[j * 4 + p] = Act<T>::sub_mul(v, zb, sc);
+        }
+      }
+      tmem_st32(lane_base + kAcol + s * (kBK / 2), r);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&a_full[s]);
+    }
+    if (!ok) s_err = 3;
+    // epilogue: accumulator rows = weight rows (this thread's row), columns = tokens
+    if (ok && mbar_wait_warp(acc_full, 0)) {
+      tc_fence_after();
+      const int n = nt * kRows + row;
+      const float b = bias ? bias[n] : 0.0f;
+#pragma unroll 1
+      for (int c = 0; c < BT; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(lane_base + c, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int m = m0 + c + j;
+          if (m < a.M) y[(size_t)m * a.N + n] = Ty<T>::from_f(__fadd_rn(__uint_as_float(v[j]), b));
+        }
+      }
+    } else if (ok) {
+      s_err = 4;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
+  if (threadIdx.x == 0 && s_err && err) atomicExch(err, s_err);
+}
+
+// ---------------------------------------------------------------------------
+// Packing: QuantizedLinear int8 codes + (scale, zero) -> kernel operand.
+//   codes: [N/128][K/64][128 rows][8 words]; word j of a row holds
+//          k = 8j..8j+7 with k = 8j+2p at bits 4p and k = 8j+2p+1 at bits 16+4p;
+//          symmetric codes are stored biased by +8.
+//   pairs: [N/128][K/group][128 rows] (zero_b, scale) in the activation type,
+//          zero_b = magic + zero (+8 symmetric), magic = 1024 (fp16) / 128 (bf16).
+// ---------------------------------------------------------------------------
+template <typename ST>
+__device__ __forceinline__ float ld_s(const void* p, int64_t i) {
+  return Ty<ST>::to_f(static_cast<const ST*>(p)[i]);
+}
+
+template <typename T, typename ST>
+__global__ void __launch_bounds__(256) w4a16_pack_kernel(const int8_t* __restrict__ wi,
+                                                         const void* __restrict__ sc,
+                                                         const void* __restrict__ zp, int N, int K,
+                                                         int group, int sym,
+                                                         uint8_t* __restrict__ packed) {
+  const int n_kb = K / kBK, ng = K / group;
+  const int64_t words = (int64_t)N * K / 8;
+  uint32_t* out = reinterpret_cast<uint32_t*>(packed);
+  const int bias8 = sym ? 8 : 0;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < words;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int j = (int)(t & 7);
+    const int64_t r0 = t >> 3;  // (nt, kb, row)
+    const int row = (int)(r0 % kRows);
+    const int64_t r1 = r0 / kRows;
+    const int kb = (int)(r1 % n_kb);
+    const int nt = (int)(r1 / n_kb);
+    const int n = nt * kRows + row;
+    const int k0 = kb * kBK + j * 8;
+    const int8_t* src = wi + (int64_t)n * K + k0;
+    uint32_t w = 0;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      w |= (uint32_t)((src[2 * p] + bias8) & 15) << (4 * p);
+      w |= (uint32_t)((src[2 * p + 1] + bias8) & 15) << (16 + 4 * p);
+    }
+    out[t] = w;
+  }
+  const int64_t pairs = (int64_t)N * ng;
+  uint32_t* pout = reinterpret_cast<uint32_t*>(packed + (int64_t)N * K / 2);
+  const float magic = (Ty<T>::code == LQ_F16) ? 1024.0f : 128.0f;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < pairs;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int row = (int)(t % kRows);
+    const int64_t r1 = t / kRows;
+    const int g = (int)(r1 % ng);
+    const int nt = (int)(r1 / ng);
+    const int n = nt * kRows + row;
+    const float z = ld_s<ST>(zp, (int64_t)n * ng + g) + (float)bias8;
+    const float s = ld_s<ST>(sc, (int64_t)n * ng + g);
+    union {
+      T h[2];
+      uint32_t u;
+    } pr;
+    pr.h[0] = Ty<T>::from_f(magic + z);
+    pr.h[1] = Ty<T>::from_f(s);
+    pout[t] = pr.u;
+  }
+}
+
+// ---- host side ---------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return (EncodeTiledFn) nullptr;
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+template <typename T, int BT, int S>
+int launch_w4(const void* x, int M, int N, int K, int group, const void* packed, const float* bias,
+              void* y, int* err, cudaStream_t st) {
+  using L = Smem<T, BT, S>;
+  EncodeTiledFn enc = encode_fn();
+  LQ_REQUIRE(enc != nullptr, LQ_ECUDA, "cuTensorMapEncodeTiled unavailable");
+  CUtensorMap map;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
+  cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)BT};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(&map, Act<T>::fmt == 0 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                   2, const_cast<void*>(x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  LQ_REQUIRE(r == CUDA_SUCCESS, LQ_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  W4Args a;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.group = group;
+  a.n_kb = K / kBK;
+  a.n_groups = K / group;
+  auto kern = w4a16_kernel<T, BT, S>;
+  // every CTA allocates all 512 tensor-memory columns: request enough shared
+  // memory that only one CTA fits on an SM, so none waits in tcgen05.alloc
+  const int smem_bytes = L::bytes > 117 * 1024 ? L::bytes : 117 * 1024;
+  static std::atomic<uint64_t> attr_done{0};  // one bit per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(attr_done.load() & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+    LQ_REQUIRE(e == cudaSuccess, LQ_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    attr_done.fetch_or(bit);
+  }
+  dim3 grid(N / kRows, (M + BT - 1) / BT);
+  kern<<<grid, 192, smem_bytes, st>>>(map, static_cast<const uint8_t*>(packed), bias,
+                                    static_cast<T*>(y), a, err);
+  return launched("w4a16_kernel");
+}
+
+template <typename T>
+int w4_dispatch(const void* x, int M, int N, int K, int group, const void* packed,
+                const float* bias, void* y, int* err, cudaStream_t st) {
+  if (M <= 16) return launch_w4<T, 16, 8>(x, M, N, K, group, packed, bias, y, err, st);
+  if (M <= 32) return launch_w4<T, 32, 8>(x, M, N, K, group, packed, bias, y, err, st);
+  if (M <= 64) return launch_w4<T, 64, 8>(x, M, N, K, group, packed, bias, y, err, st);
+  if (M <= 128) return launch_w4<T, 128, 6>(x, M, N, K, group, packed, bias, y, err, st);
+  return launch_w4<T, 256, 4>(x, M, N, K, group, packed, bias, y, err, st);
+}
+
+template <typename T, typename ST>
+int pack_t(const int8_t* wi, const void* s, const void* z, int N, int K, int group, int sym,
+           void* packed, cudaStream_t st) {
+  int64_t work = (int64_t)N * K / 8;
+  int grid = (int)((work + 255) / 256);
+  if (grid > num_sms() * 16) grid = num_sms() * 16;
+  w4a16_pack_kernel<T, ST><<<grid, 256, 0, st>>>(wi, s, z, N, K, group, sym,
+                                                 static_cast<uint8_t*>(packed));
+  return launched("w4a16_pack_kernel");
+}
+
+template <typename T>
+int pack_s(const int8_t* wi, const void* s, const void* z, int sdt, int N, int K, int group,
+           int sym, void* packed, cudaStream_t st) {
+  switch (sdt) {
+    case LQ_F32: return pack_t<T, float>(wi, s, z, N, K, group, sym, packed, st);
+    case LQ_F16: return pack_t<T, __half>(wi, s, z, N, K, group, sym, packed, st);
+    case LQ_BF16: return pack_t<T, __nv_bfloat16>(wi, s, z, N, K, group, sym, packed, st);
+    default: set_error("unsupported scale dtype %d", sdt); return LQ_EDTYPE;
+  }
+}
+
+int check_shape(int64_t N, int64_t K, int64_t group) {
+  LQ_REQUIRE(N > 0 && K > 0 && group > 0, LQ_EINVAL, "bad shape");
+  LQ_REQUIRE(N % kRows == 0, LQ_EINVAL, "W4A16 needs out_features %% 128 == 0 (got %lld)", (long long)N);
+  LQ_REQUIRE(K % kBK == 0, LQ_EINVAL, "W4A16 needs in_features %% 64 == 0 (got %lld)", (long long)K);
+  LQ_REQUIRE(group % kBK == 0 && K % group == 0, LQ_EINVAL,
+             "W4A16 needs group_size %% 64 == 0 dividing in_features (got %lld)", (long long)group);
+  LQ_REQUIRE(N < (1LL << 31) && K < (1LL << 31), LQ_ERANGE, "shape too large");
+  return LQ_OK;
+}
+
+}  // namespace
+}  // namespace lq
+
+using namespace lq;
+
+extern "C" size_t lq_w4a16_packed_bytes(int64_t N, int64_t K, int64_t group) {
+  if (N <= 0 || K <= 0 || group <= 0) return 0;
+  return (size_t)(N * K / 2 + N * (K / group) * 4);
+}
+
+extern "C" int lq_w4a16_pack(const int8_t* weight_int, const void* scale, const void* zero_point,
+                             int s_dtype, int64_t N, int64_t K, int64_t group, int symmetric,
+                             int act_dtype, void* packed, void* stream) {
+  int rc = check_shape(N, K, group);
+  if (rc) return rc;
+  LQ_REQUIRE(weight_int && scale && zero_point && packed, LQ_EINVAL, "NULL pointer");
+  LQ_REQUIRE(aligned16(packed), LQ_EALIGN, "packed buffer must be 16-byte aligned");
+  cudaStream_t st = as_stream(stream);
+  if (act_dtype == LQ_F16) return pack_s<__half>(weight_int, scale, zero_point, s_dtype, (int)N, (int)K, (int)group, symmetric, packed, st);
+  if (act_dtype == LQ_BF16) return pack_s<__nv_bfloat16>(weight_int, scale, zero_point, s_dtype, (int)N, (int)K, (int)group, symmetric, packed, st);
+  set_error("W4A16 activations must be fp16 or bf16 (got dtype %d)", act_dtype);
+  return LQ_EDTYPE;
+}
+
+extern "C" int lq_w4a16_linear(const void* x, int act_dtype, int64_t M, int64_t N, int64_t K,
+                               int64_t group, const void* packed, const float* bias, void* y,
+                               int* err, void* stream) {
+  int rc = check_shape(N, K, group);
+  if (rc) return rc;
+  LQ_REQUIRE(M >= 0 && M < (1LL << 31), LQ_EINVAL, "bad M");
+  if (M == 0) return LQ_OK;
+  LQ_REQUIRE(x && packed && y, LQ_EINVAL, "NULL pointer");
+  LQ_REQUIRE(aligned16(x) && aligned16(packed), LQ_EALIGN, "x and packed must be 16-byte aligned");
+  cudaStream_t st = as_stream(stream);
+  if (act_dtype == LQ_F16) return w4_dispatch<__half>(x, (int)M, (int)N, (int)K, (int)group, packed, bias, y, err, st);
+  if (act_dtype == LQ_BF16) return w4_dispatch<__nv_bfloat16>(x, (int)M, (int)N, (int)K, (int)group, packed, bias, y, err, st);
+  set_error("W4A16 activations must be fp16 or bf16 (got dtype %d)", act_dtype);
+  return LQ_EDTYPE;
+}

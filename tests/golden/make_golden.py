@@ -167,7 +167,6 @@ def gen_quantizer(ref):
         lin = lin.to(DT[wdt])
         ql = QuantizedLinear.from_linear(lin, n_bits=bits, symmetric=sym, group_size=gs)
         x = torch.randn(5, inf_, generator=g)
-        ql32 = ql.float() if wdt != "float32" else ql
         # forward needs fp32 x and fp32 bias: the module dequantizes to fp32
         ql_f = QuantizedLinear(inf_, outf, bits, sym, gs)
         ql_f.weight_int.copy_(ql.weight_int)
@@ -180,7 +179,6 @@ def gen_quantizer(ref):
                                 symmetric=sym, group_size=gs, dtype=wdt),
                w=lin.weight.data, bias=lin.bias.data, weight_int=ql.weight_int, scale=ql.scale,
                zero_point=ql.zero_point, x=x, y=y)
-        del ql32
     st.save("quantizer.npz")
 
 
@@ -368,10 +366,34 @@ def gen_kv(ref):
     st.save("kv.npz")
 
 
+def gen_grad(ref):
+    """fake_quantize gradients under the reference's autograd."""
+    from llm_quant.core.quantizer import fake_quantize, QScheme
+    st = Store()
+    g = torch.Generator().manual_seed(77)
+    n = 0
+    for dtn in ("float32", "bfloat16", "float16"):
+        for scheme, shape, gs in (("per_group", (12, 256), 128), ("per_group", (5, 70), 32),
+                                  ("per_channel", (9, 48), 128), ("per_channel", (4, 3, 10), 128),
+                                  ("per_tensor", (6, 40), 128)):
+            for sym in (True, False):
+                bits = 4
+                x = torch.randn(shape, generator=g) * 0.5
+                x.view(-1)[7] = x.view(-1)[3]  # a tie
+                x = x.to(DT[dtn]).requires_grad_(True)
+                go = torch.randn(shape, generator=g).to(DT[dtn])
+                y = fake_quantize(x, bits, sym, QScheme(scheme), gs)
+                y.backward(go)
+                st.add(f"g{n:03d}", dict(fn="grad", dtype=dtn, scheme=scheme, shape=list(shape),
+                                         group_size=gs, symmetric=sym, n_bits=bits),
+                       x=x.detach(), go=go, y=y.detach(), gx=x.grad)
+                n += 1
+    st.save("grad.npz")
+
+
 if __name__ == "__main__":
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     ref = _import_reference()
-    gen_quantizer(ref)
-    gen_rotation(ref)
-    gen_nf4(ref)
-    gen_kv(ref)
+    which = sys.argv[1:] or ["quantizer", "rotation", "nf4", "kv", "grad"]
+    for name in which:
+        globals()[f"gen_{name}"](ref)

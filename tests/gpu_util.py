@@ -9,9 +9,11 @@ NAME = {v: k for k, v in TORCH_DT.items()}
 
 def to_dev(arr: np.ndarray, dtype: str, device="cuda") -> torch.Tensor:
     """float32-held values (or integer arrays) -> CUDA tensor of `dtype`."""
+    # np.array (not ascontiguousarray) keeps 0-dim arrays 0-dim: torch type
+    # promotion treats 0-dim tensors differently from [1]-shaped ones
     if dtype in TORCH_DT:
-        return torch.from_numpy(np.ascontiguousarray(arr, np.float32)).to(device).to(TORCH_DT[dtype])
-    return torch.from_numpy(np.ascontiguousarray(arr)).to(device)
+        return torch.from_numpy(np.array(arr, dtype=np.float32, copy=True)).to(device).to(TORCH_DT[dtype])
+    return torch.from_numpy(np.array(arr, copy=True)).to(device)
 
 
 def to_np(t: torch.Tensor) -> np.ndarray:

@@ -154,3 +154,27 @@ def test_quantized_linear_state_dict_roundtrip(L):
     ql2.load_state_dict(sd)
     x = torch.randn(3, 256, device="cuda")
     assert torch.equal(ql(x), ql2(x))
+
+
+@pytest.mark.parametrize("name,c", list(cases("grad.npz", "grad")), ids=_ids)
+def test_fake_quantize_gradient_golden(L, name, c):
+    """Forward bit-exact; gradient vs the reference's autograd within float
+    tolerance (1e-5 relative for fp32, 1e-2 for half types: sums of the scale
+    gradient are accumulated in a different order)."""
+    p = c["params"]
+    dt = p["dtype"]
+    x = to_dev(c["x"][0], dt).requires_grad_(True)
+    y = L.fake_quantize(x, p["n_bits"], p["symmetric"], L.QScheme(p["scheme"]), p["group_size"])
+    assert same_bits(to_np(y), c["y"][0])
+    y.backward(to_dev(c["go"][0], dt))
+    gx, ref = to_np(x.grad), c["gx"][0]
+    tol = 1e-5 if dt == "float32" else 1e-2
+    np.testing.assert_allclose(gx, ref, rtol=tol, atol=tol * max(1.0, np.abs(ref).max()))
+
+
+def test_fake_quantize_gradient_flows(L):
+    """The reference's own check (tests/test_quantizer.py:96-101)."""
+    x = torch.randn(8, 32, device="cuda", requires_grad=True)
+    y = L.fake_quantize(x, n_bits=8)
+    y.sum().backward()
+    assert x.grad is not None and x.grad.shape == x.shape
