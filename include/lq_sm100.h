@@ -151,6 +151,20 @@ int lq_tensor_qparams(const void* x, int x_dtype, int64_t n, int n_bits, int sym
                       void* scale, void* zero_point, void* workspace, size_t workspace_bytes,
                       void* stream);
 
+/* lq_tensor_qparams without a workspace argument -- no counterpart in the
+ * reference (which has no C interface); it exists for callers that cannot
+ * allocate device memory (an FFI host that is handed tensor pointers by
+ * another runtime and has no device allocator, or an application whose
+ * device memory is all reserved by a framework allocator).  Same results as
+ * lq_tensor_qparams.  Its partial results live in a fixed 128 KB array in
+ * this library's device memory (held by every GPU that loads the library),
+ * which limits n to 64 Mi elements (larger n: LQ_ERANGE).  All calls share
+ * that array: calls whose kernels overlap on the GPU race.  The first call on
+ * a device looks up the array's address (cudaGetSymbolAddress), so make it
+ * before any stream capture.  Allocates nothing. */
+int lq_tensor_qparams_noalloc(const void* x, int x_dtype, int64_t n, int n_bits, int symmetric,
+                              void* scale, void* zero_point, void* stream);
+
 /* ---- per-channel reduction along an inner axis ---------------------------------
  * compute_qparams PER_CHANNEL with channel_dim != 0 (core/quantizer.py:74-85):
  * x is [outer, C, inner]; scale/zp [C] reduce over outer and inner.

@@ -360,3 +360,89 @@ extern "C" int lq_ste_round(const void* x, int dtype, int64_t n, void* out, void
     default: set_error("unsupported dtype %d", dtype); return LQ_EDTYPE;
   }
 }
+
+// ---------------------------------------------------------------------------
+// Per-tensor qparams without a caller-provided workspace.
+//
+// For callers that cannot allocate device memory themselves -- a host
+// program that reaches this library only through its C ABI (an FFI binding
+// that is handed tensor pointers owned by another runtime and has no device
+// allocator of its own), or an application whose device memory is entirely
+// reserved by a framework allocator it cannot call into -- this variant keeps
+// its per-block partial results in a fixed array in this library's own
+// device memory instead of a workspace argument.
+//
+// Limits and behaviour:
+//   * the array holds kNoAllocParts partials of one 4096-element block each,
+//     so n is limited to kNoAllocParts * 4096 = 64 Mi elements (every GPU
+//     that loads the library holds the 128 KB array until the process exits);
+//   * every call on a device shares the array: calls whose kernels overlap on
+//     the GPU (different streams without ordering) race and give wrong
+//     results; calls ordered on one stream are safe.  Each call writes every
+//     partial it later reads, so nothing has to be cleared between calls;
+//   * the first call on a device looks up the array's device address with
+//     cudaGetSymbolAddress (once per device, with that device current), so
+//     make that first call before any stream capture;
+//   * the call allocates nothing: no cudaMalloc, no cudaFree, no library
+//     routine that allocates.
+// ---------------------------------------------------------------------------
+namespace lq {
+namespace {
+
+constexpr int64_t kNoAllocParts = 16384;
+constexpr int64_t kNoAllocBlockElems = 256 * 16;
+
+static __device__ __align__(256) MinMax g_noalloc_partials[kNoAllocParts];
+
+MinMax* noalloc_partials_for_current_device() {
+  static std::atomic<MinMax*> slots[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  MinMax* p = slots[dev].load(std::memory_order_acquire);
+  if (p) return p;
+  void* addr = nullptr;
+  // the host-side name of the array is only a stand-in: ask the runtime for
+  // its address on this device
+  if (cudaGetSymbolAddress(&addr, g_noalloc_partials) != cudaSuccess || addr == nullptr) return nullptr;
+  p = static_cast<MinMax*>(addr);
+  slots[dev].store(p, std::memory_order_release);
+  return p;
+}
+
+template <typename T>
+int tensor_qparams_noalloc_t(const void* x, int64_t n, int n_bits, int sym, void* scale, void* zp,
+                             MinMax* part, cudaStream_t st) {
+  const int nb = (int)((n + kNoAllocBlockElems - 1) / kNoAllocBlockElems);
+  tensor_minmax_kernel<T><<<nb, 256, 0, st>>>(static_cast<const T*>(x), n, part);
+  int rc = launched("tensor_minmax_kernel");
+  if (rc) return rc;
+  tensor_qparams_kernel<T><<<1, 256, 0, st>>>(part, nb, sym, (float)qmin_of(n_bits, sym),
+                                              (float)qmax_of(n_bits, sym), lo_clamp_value<T>(),
+                                              static_cast<T*>(scale), static_cast<T*>(zp));
+  return launched("tensor_qparams_kernel");
+}
+
+}  // namespace
+}  // namespace lq
+
+extern "C" int lq_tensor_qparams_noalloc(const void* x, int x_dtype, int64_t n, int n_bits,
+                                         int symmetric, void* scale, void* zero_point,
+                                         void* stream) {
+  using namespace lq;
+  LQ_REQUIRE(n >= 1, LQ_EINVAL, "per-tensor qparams of an empty tensor");
+  LQ_REQUIRE(n <= kNoAllocParts * kNoAllocBlockElems, LQ_ERANGE,
+             "lq_tensor_qparams_noalloc: n = %lld is above its maximum of %lld elements "
+             "(use lq_tensor_qparams with a workspace)",
+             (long long)n, (long long)(kNoAllocParts * kNoAllocBlockElems));
+  LQ_REQUIRE(n_bits >= 1 && n_bits <= 16, LQ_EINVAL, "n_bits out of range");
+  LQ_REQUIRE(x && scale && zero_point, LQ_EINVAL, "NULL pointer");
+  MinMax* part = noalloc_partials_for_current_device();
+  LQ_REQUIRE(part != nullptr, LQ_ECUDA, "cudaGetSymbolAddress of the scratch array failed");
+  cudaStream_t st = as_stream(stream);
+  switch (x_dtype) {
+    case LQ_F32: return tensor_qparams_noalloc_t<float>(x, n, n_bits, symmetric, scale, zero_point, part, st);
+    case LQ_F16: return tensor_qparams_noalloc_t<__half>(x, n, n_bits, symmetric, scale, zero_point, part, st);
+    case LQ_BF16: return tensor_qparams_noalloc_t<__nv_bfloat16>(x, n, n_bits, symmetric, scale, zero_point, part, st);
+    default: set_error("unsupported dtype %d", x_dtype); return LQ_EDTYPE;
+  }
+}
