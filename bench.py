@@ -741,6 +741,42 @@ class W4A16Workload:
                 "sample": f"oracle dequant + numpy fp32 matmul, M={M}, K={K}, N={N}, median of 3"}
 
 
+def profile_case(name, ctx):
+    """A small case of each workload's dominant kernel for ncu captures:
+    inputs larger than L2 (126 MB) but a few hundred MB at most, 3 launches."""
+    torch = ctx.torch
+    import llm_quant_b200 as L
+    g = torch.Generator(device=ctx.dev).manual_seed(0)
+    if name == "nf4":
+        w = (torch.randn(28672, 4096, generator=g, device=ctx.dev) * 0.02).to(torch.bfloat16)
+        m = L.QLoRALinear(4096, 28672, rank=16, group_size=64).to(ctx.dev)
+        for _ in range(3):
+            m.pack_base(w)
+            m._dequantize_base()
+    elif name == "group":
+        w = torch.randn(8192, 4096, generator=g, device=ctx.dev) * 0.02
+        for _ in range(3):
+            L.fake_quantize(w, 4, False, L.QScheme.PER_GROUP, 128)
+    elif name == "rotquant":
+        a = torch.randn(16384, 4096, generator=g, device=ctx.dev).to(torch.bfloat16)
+        for _ in range(3):
+            L.hadamard_fake_quantize(a, 4, True)
+    elif name == "kv":
+        cache = L.QuantizedKVCache(1, L.PerChannelKVCacheQuantizer(8),
+                                   value_quantizer=L.PerTokenKVCacheQuantizer(4), max_seq_len=8192)
+        for _ in range(16):
+            k = torch.randn(8, 8, 512, 128, generator=g, device=ctx.dev).to(torch.bfloat16)
+            cache.update(0, k, k)
+    elif name == "w4a16":
+        lin = torch.nn.Linear(4096, 14336, device=ctx.dev).half()
+        ql = L.QuantizedLinear.from_linear(lin, 4, False, 128)
+        x = torch.randn(1024, 4096, generator=g, device=ctx.dev).half()
+        for _ in range(3):
+            ql(x)
+    torch.cuda.synchronize()
+    print(f"profile case {name} done")
+
+
 WORKLOADS = {"nf4": NF4Workload, "group": GroupWorkload, "rotquant": RotQuantWorkload,
              "kv": KVWorkload, "w4a16": W4A16Workload}
 
@@ -889,10 +925,15 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="nf4")
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--profile", action="store_true",
+                    help="only run a small case of the workload's dominant kernel (for ncu)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)  # at least 3 warm-up steps
     if args.impl == "reference":
         return run_reference(args)
+    if args.profile:
+        profile_case(args.workload, Ctx(args.gpus))
+        return 0
     return run_ours(args)
 
 

@@ -79,12 +79,16 @@ template <> struct Ty<__half> {
   __device__ __forceinline__ static __half from_f(float v) { return __float2half_rn(v); }
   __device__ __forceinline__ static float round(float v) { return __half2float(__float2half_rn(v)); }
 };
+// bf16 -> fp32 is a 16-bit shift (exact, one ALU op); fp32 -> bf16 rounding
+// uses the hardware round-to-nearest-even conversion.
 template <> struct Ty<__nv_bfloat16> {
   static constexpr int code = LQ_BF16;
-  __device__ __forceinline__ static float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  __device__ __forceinline__ static float to_f(__nv_bfloat16 v) {
+    return __uint_as_float((uint32_t)__bfloat16_as_ushort(v) << 16);
+  }
   __device__ __forceinline__ static __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
   __device__ __forceinline__ static float round(float v) {
-    return __bfloat162float(__float2bfloat16_rn(v));
+    return __uint_as_float((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v)) << 16);
   }
 };
 
@@ -158,7 +162,12 @@ struct MinMax {
     mn = fmin_nan(mn, v);
     mx = fmax_nan(mx, v);
   }
-  __device__ __forceinline__ void add_max(float v) { mx = fmax_nan(mx, v); }
+  // v must be >= 0 or NaN with a clear sign bit (callers pass fabsf(x)):
+  // then the integer order of the bit patterns is the float order and any
+  // NaN is above +inf, so an integer max propagates NaN like torch.amax.
+  __device__ __forceinline__ void add_max(float v) {
+    mx = __int_as_float(max(__float_as_int(mx), __float_as_int(v)));
+  }
   __device__ __forceinline__ void merge(const MinMax& o) {
     mn = fmin_nan(mn, o.mn);
     mx = fmax_nan(mx, o.mx);

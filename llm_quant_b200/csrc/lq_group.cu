@@ -10,6 +10,8 @@
 //   * a streaming block path (two passes, the second from L2) beyond that.
 // The vector path moves 16 bytes per load/store (ld.global.nc.v4); it needs
 // G*sizeof(T) % 16 == 0, cols % G == 0 and 16-byte aligned pointers.
+#include <type_traits>
+
 #include "lq_common.cuh"
 
 namespace lq {
@@ -70,16 +72,27 @@ struct GroupArgs {
   }
 };
 
-// Per-element output of the fused modes.
+// Per-element output of the fused modes.  A zero point of +0.0 (symmetric
+// quantization) is skipped: t + 0 only turns a -0.0 into +0.0, which ste_round
+// and the code casts treat alike, and q - 0 is exact for integer q.
 template <typename T, int MODE>
-__device__ __forceinline__ float apply_q(float v, float scale, float zp, float qmin, float qmax) {
-  float t = tadd<T>(tdiv<T>(v, scale), zp);
+__device__ __forceinline__ float apply_q(float v, float scale, float zp, float qmin, float qmax,
+                                         bool zp0) {
+  float t = tdiv<T>(v, scale);
+  if (!zp0) t = tadd<T>(t, zp);
   if constexpr (MODE == MODE_FAKE) {
     float q = tclamp(tste(t), qmin, qmax);
-    return tmul<T>(tsub<T>(q, zp), scale);
+    return tmul<T>(zp0 ? q : tsub<T>(q, zp), scale);
   } else {
     return tclamp(trint(t), qmin, qmax);
   }
+}
+
+// The symmetric skip is exact for fake quantization and integer codes; a
+// float code output keeps the +0.0 add (it can turn a -0.0 code into +0.0).
+template <int MODE, typename OutT, typename T>
+__device__ __forceinline__ bool zp0_ok(const GroupArgs& a) {
+  return a.sym && (MODE == MODE_FAKE || !std::is_same<OutT, T>::value);
 }
 
 // ---------------------------------------------------------------------------
@@ -141,7 +154,7 @@ struct Tile {
       int64_t e = (int64_t)(k * tps + t) * V;
       float o[V];
 #pragma unroll
-      for (int i = 0; i < V; ++i) o[i] = apply_q<T, MODE>(v[k * V + i], scale, zp, a.qmin, a.qmax);
+      for (int i = 0; i < V; ++i) o[i] = apply_q<T, MODE>(v[k * V + i], scale, zp, a.qmin, a.qmax, zp0_ok<MODE, OutT, T>(a));
       if constexpr (VEC) {
         store_vec<OutT, T, V>(base + e, o);
       } else {
@@ -255,7 +268,7 @@ __global__ void __launch_bounds__(1024) group_stream_kernel(const T* __restrict_
     if constexpr (MODE != MODE_QPARAMS) {
       OutT* ob = out + a.out_row(row) * a.cols + gcol0;
       for (int64_t e = threadIdx.x; e < a.G && gcol0 + e < a.cols; e += blockDim.x)
-        ob[e] = Store<OutT, T>::cv(apply_q<T, MODE>(Ty<T>::to_f(base[e]), scale, zp, a.qmin, a.qmax));
+        ob[e] = Store<OutT, T>::cv(apply_q<T, MODE>(Ty<T>::to_f(base[e]), scale, zp, a.qmin, a.qmax, zp0_ok<MODE, OutT, T>(a)));
     }
   }
 }

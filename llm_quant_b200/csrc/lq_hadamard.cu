@@ -76,15 +76,16 @@ __device__ __forceinline__ void butterfly_regs(float* v) {
   }
 }
 
-// Shuffle stages over lane bits [0, log2(tps)).
+// Shuffle stages over lane bits [0, log2(tps)): the lower lane of a pair
+// keeps a + b, the upper one a - b, both as one exact fma(v, +-1, partner).
 template <int E>
 __device__ __forceinline__ void butterfly_lanes(float* v, int tps, int lane_in_team) {
   for (int m = 1; m < tps; m <<= 1) {
-    const bool upper = lane_in_team & m;
+    const float sgn = (lane_in_team & m) ? -1.0f : 1.0f;
 #pragma unroll
     for (int i = 0; i < E; ++i) {
-      float p = __shfl_xor_sync(0xffffffffu, v[i], m);
-      v[i] = upper ? __fsub_rn(p, v[i]) : __fadd_rn(v[i], p);
+      const float p = __shfl_xor_sync(0xffffffffu, v[i], m);
+      v[i] = fmaf(v[i], sgn, p);
     }
   }
 }
@@ -104,13 +105,30 @@ __device__ __forceinline__ void finish_and_quant(float* v, const FhtArgs& a, Min
   }
 }
 
+// fake_quantize of T-rounded values with the row's scale / zero point.  For
+// bf16, round_T(v / scale) is computed as round_T(v * rcp_rn(scale)): a
+// quotient of two 8-bit significands is either exact or at least 2^-17
+// (relative) away from every bf16 rounding midpoint, while v * rcp is within
+// 2^-23 of it, so both round to the same bf16 value when the product is a
+// normal number (otherwise the IEEE division is used).
 template <typename T, int E>
 __device__ __forceinline__ void fake_quant_vals(float* v, const FhtArgs& a, float scale, float zp) {
+  constexpr bool kBf16 = Ty<T>::code == LQ_BF16;
+  const float rcp = __frcp_rn(scale);
+  const bool rcp_ok = kBf16 && scale >= 0x1p-126f && scale <= 0x1p126f;
 #pragma unroll
   for (int i = 0; i < E; ++i) {
-    float t = tadd<T>(tdiv<T>(v[i], scale), zp);
-    float q = tclamp(tste(t), a.qmin, a.qmax);
-    v[i] = tmul<T>(tsub<T>(q, zp), scale);
+    float qv;
+    if (kBf16) {
+      const float pr = __fmul_rn(v[i], rcp);
+      qv = (rcp_ok && (fabsf(pr) >= 0x1p-126f || pr == 0.0f)) ? Ty<T>::round(pr) : tdiv<T>(v[i], scale);
+    } else {
+      qv = tdiv<T>(v[i], scale);
+    }
+    // symmetric: zp is +0.0 and both zero-point ops are exact no-ops here
+    const float t = a.sym ? qv : tadd<T>(qv, zp);
+    const float q = tclamp(tste(t), a.qmin, a.qmax);
+    v[i] = tmul<T>(a.sym ? q : tsub<T>(q, zp), scale);
   }
 }
 

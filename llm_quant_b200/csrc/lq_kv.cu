@@ -294,9 +294,74 @@ __global__ void __launch_bounds__(256) kv_dequant_kernel(const CT* __restrict__ 
   }
 }
 
+// Vector path: thread = 16 consecutive elements of one token row (16 codes
+// in one load, 64 bytes of fp32 out); needs D % 16 == 0 and aligned buffers.
+// float(q) is formed exactly as (1.5 * 2^23 + q) - 1.5 * 2^23.
+template <typename CT, typename ST>
+__global__ void __launch_bounds__(256) kv_dequant16_kernel(const CT* __restrict__ codes, DqArgs a,
+                                                           const ST* __restrict__ scale,
+                                                           const ST* __restrict__ zp,
+                                                           float* __restrict__ out) {
+  const int64_t per_row = a.D / 16;
+  const int64_t total = a.P * a.T * per_row;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / per_row;  // (p, t)
+    const int c = (int)(i - r * per_row) * 16;
+    const int64_t p = r / a.T, t = r - p * a.T;
+    const CT* q = codes + (p * a.cpitch + t) * a.D + c;
+    int qv[16];
+    if constexpr (sizeof(CT) == 1) {
+      const uint4 w = *reinterpret_cast<const uint4*>(q);
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int k = 0; k < 16; ++k) qv[k] = (int)(int8_t)(ws[k >> 2] >> (8 * (k & 3)));
+    } else {
+      const uint4 w0 = reinterpret_cast<const uint4*>(q)[0], w1 = reinterpret_cast<const uint4*>(q)[1];
+      const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+      for (int k = 0; k < 16; ++k) qv[k] = (int)(int16_t)(ws[k >> 1] >> (16 * (k & 1)));
+    }
+    float sv[16], zv[16];
+    if (a.gran == 0) {
+      const int64_t si = p * a.szpitch + t;
+      const float s0 = Ty<ST>::to_f(scale[si]), z0 = Ty<ST>::to_f(zp[si]);
+#pragma unroll
+      for (int k = 0; k < 16; ++k) { sv[k] = s0; zv[k] = z0; }
+    } else {
+      const int64_t base = (a.gran == 1) ? p * a.D + c : (p * a.szpitch + t / a.S) * a.D + c;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        sv[k] = Ty<ST>::to_f(scale[base + k]);
+        zv[k] = Ty<ST>::to_f(zp[base + k]);
+      }
+    }
+    float o[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const float qf = __fsub_rn(__int_as_float(0x4B400000 + qv[k]), 12582912.0f);
+      o[k] = __fmul_rn(__fsub_rn(qf, zv[k]), sv[k]);
+    }
+    float* dst = out + r * a.D + c;
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      st_v4(dst + 4 * k, make_uint4(__float_as_uint(o[4 * k]), __float_as_uint(o[4 * k + 1]),
+                                    __float_as_uint(o[4 * k + 2]), __float_as_uint(o[4 * k + 3])));
+  }
+}
+
 template <typename CT, typename ST>
 int kv_dequant_t(const void* codes, const DqArgs& a, const void* s, const void* z, float* out,
                  cudaStream_t st) {
+  if (a.D % 16 == 0 && aligned16(out) && aligned16(codes)) {
+    const int64_t total = a.P * a.T * (a.D / 16);
+    int64_t want = (total + 255) / 256;
+    int grid = (int)(want < (int64_t)num_sms() * 16 ? (want > 0 ? want : 1) : (int64_t)num_sms() * 16);
+    kv_dequant16_kernel<CT, ST><<<grid, 256, 0, st>>>(static_cast<const CT*>(codes), a,
+                                                      static_cast<const ST*>(s),
+                                                      static_cast<const ST*>(z), out);
+    return launched("kv_dequant16_kernel");
+  }
   int vec4 = (a.D % 4 == 0) && aligned16(out) &&
              (reinterpret_cast<uintptr_t>(codes) % (4 * sizeof(CT)) == 0);
   const int64_t per_row = vec4 ? a.D / 4 : a.D;

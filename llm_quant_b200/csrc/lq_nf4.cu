@@ -1,19 +1,26 @@
 // lq_nf4.cu -- NF4 blockwise quantization (qlora.py).
 //
 // Encoding.  The reference picks code = first argmin_i |x_norm - NF4_TABLE[i]|
-// with the differences computed in fp32 (qlora.py:103-104).  For x_norm in
-// [-1, 1] the fp32 differences on either side of x_norm are monotone, so the
-// chosen code is a non-decreasing step function of x_norm: it equals the
-// number of thresholds kNF4Theta[i] <= x_norm, where kNF4Theta[i-1] is the
-// smallest fp32 value whose reference code is >= i (found by exhaustive
-// bisection over fp32 bit patterns and re-checked by the CPU tests).  A NaN
-// x_norm fails every comparison and gets code 0, as torch.argmin gives.
+// with the differences computed in fp32 (qlora.py:103-104), where
+// x_norm = round_T(x / scale).  For x_norm in [-1, 1] the fp32 differences on
+// either side of x_norm are monotone, so the code is a non-decreasing step
+// function of x_norm, and since round_T is monotone too, of the unrounded
+// quotient p = x / scale: code = #{i : p >= kTheta[T][i]}, where kTheta[T][i]
+// is the smallest fp32 value whose reference code is > i (found by exhaustive
+// bisection over fp32 bit patterns; the CPU tests re-derive the fp32 set).
+// The thresholds are >= 0.08 apart, so a 65-bucket table over [-1, 1]
+// (bucket width 1/32, at most one threshold per bucket) turns the count into
+// one FFMA (bucket index), one shared-memory load and one compare.  A NaN
+// quotient gets code 0, as torch.argmin gives for an all-NaN row.
 //
 // Layout.  The tensor is flattened and cut into groups of G elements, the
-// last one zero-padded (qlora.py:84-93).  A warp team of G/V lanes (V
-// elements = 16 bytes per lane) owns one group; a block walks "super-groups"
-// of DG consecutive groups so the double quantization of their DG scales
-// (qlora.py:164-196) is done in shared memory in the same pass.
+// last one zero-padded (qlora.py:84-93).  A team of G/(V*NVT) lanes owns one
+// group (V elements = 16 bytes per vector, NVT vectors per lane) and keeps
+// four groups in flight; a block walks "super-groups" of DG consecutive
+// groups so the double quantization of their DG scales (qlora.py:164-196) is
+// done in shared memory in the same pass.
+#include <type_traits>
+
 #include "lq_common.cuh"
 
 namespace lq {
@@ -24,45 +31,63 @@ __device__ __constant__ float kNF4[16] = {
     -1.0f, -0.6962f, -0.5251f, -0.3949f, -0.2844f, -0.1848f, -0.0911f, 0.0f,
     0.0796f, 0.1609f, 0.2461f, 0.3379f, 0.4407f, 0.5626f, 0.7230f, 1.0f};
 
-// Decision thresholds (exact fp32 values).
-__device__ __forceinline__ int nf4_code(float xn) {
-  int c = 0;
-  c += xn >= -0x1.b23a28p-1f;
-  c += xn >= -0x1.38a71cp-1f;
-  c += xn >= -0x1.d70a3cp-2f;
-  c += xn >= -0x1.5bcd34p-2f;
-  c += xn >= -0x1.e075f4p-3f;
-  c += xn >= -0x1.1a8586p-3f;
-  c += xn >= -0x1.752544p-5f;
-  c += xn >= 0x1.460aa8p-5f;
-  c += xn >= 0x1.ec8b44p-4f;
-  c += xn >= 0x1.a0c49cp-3f;
-  c += xn >= 0x1.2b020ep-2f;
-  c += xn >= 0x1.8ea4aap-2f;
-  c += xn >= 0x1.00d846p-1f;
-  c += xn >= 0x1.491d16p-1f;
-  c += xn >= 0x1.b91688p-1f;
-  return c;
-}
+// Decision thresholds on the unrounded quotient, per input dtype
+// (row 0: fp32, 1: fp16, 2: bf16).
+__device__ __constant__ float kTheta[3][15] = {
+    {-0x1.b23a28p-1f, -0x1.38a71cp-1f, -0x1.d70a3cp-2f, -0x1.5bcd34p-2f, -0x1.e075f4p-3f,
+     -0x1.1a8586p-3f, -0x1.752544p-5f, 0x1.460aa8p-5f, 0x1.ec8b44p-4f, 0x1.a0c49cp-3f,
+     0x1.2b020ep-2f, 0x1.8ea4aap-2f, 0x1.00d846p-1f, 0x1.491d16p-1f, 0x1.b91688p-1f},
+    {-0x1.b22p-1f, -0x1.38ap-1f, -0x1.d72p-2f, -0x1.5bdffep-2f, -0x1.e05ffep-3f,
+     -0x1.1aap-3f, -0x1.752p-5f, 0x1.462002p-5f, 0x1.eca002p-4f, 0x1.a0ep-3f,
+     0x1.2b2002p-2f, 0x1.8ea002p-2f, 0x1.00ep-1f, 0x1.492002p-1f, 0x1.b92002p-1f},
+    {-0x1.b2fffep-1f, -0x1.39p-1f, -0x1.d6fffep-2f, -0x1.5afffep-2f, -0x1.e1p-3f,
+     -0x1.1afffep-3f, -0x1.75p-5f, 0x1.47p-5f, 0x1.ed0002p-4f, 0x1.a10002p-3f,
+     0x1.2bp-2f, 0x1.8fp-2f, 0x1.010002p-1f, 0x1.490002p-1f, 0x1.b90002p-1f}};
 
-// x_norm = (x / scale) rounded to T.  For bf16 operands the quotient of two
-// 8-bit significands is never within 2^-17 (relative) of a bf16 rounding
-// midpoint unless it equals one (impossible: a midpoint needs a 9-bit odd
-// significand), so bf16(x * rcp(scale)) with rcp correctly rounded equals
-// bf16(x / scale) whenever the product is a normal fp32 number.  Other
-// dtypes and edge cases use the IEEE division.
+template <typename T> struct ThetaRow;
+template <> struct ThetaRow<float> { static constexpr int row = 0; };
+template <> struct ThetaRow<__half> { static constexpr int row = 1; };
+template <> struct ThetaRow<__nv_bfloat16> { static constexpr int row = 2; };
+
+constexpr int kLut = 128;  // 65 buckets used; the rest catch NaN bucket indices
+
+// lut[b] = (bits of the threshold inside bucket b or +inf, code at the bucket's
+// left edge); bucket b covers quotients p with rint(32 p) = b - 32.
 template <typename T>
-__device__ __forceinline__ float xnorm(float x, float scale, float rcp, bool rcp_ok) {
-  if constexpr (sizeof(T) == 2 && Ty<T>::code == LQ_BF16) {
-    float p = __fmul_rn(x, rcp);
-    if (rcp_ok && (fabsf(p) >= 0x1p-126f || p == 0.0f)) return Ty<T>::round(p);
+__device__ __forceinline__ void build_lut(int2* lut) {
+  for (int b = threadIdx.x; b < kLut; b += blockDim.x) {
+    int code = 0;
+    float th = __int_as_float(0x7f800000);
+    if (b <= 64) {
+      const float left = (float)(2 * b - 65) / 64.0f, right = (float)(2 * b - 63) / 64.0f;
+      for (int i = 0; i < 15; ++i) {
+        const float t = kTheta[ThetaRow<T>::row][i];
+        code += (t <= left);
+        if (t > left && t <= right) th = t;
+      }
+    }
+    lut[b] = make_int2(__float_as_int(th), code);
   }
-  return tdiv<T>(x, scale);
 }
 
+__device__ __forceinline__ int nf4_encode(float p, const int2* lut) {
+  const float f = fmaf(p, 32.0f, 12582944.0f);  // 1.5 * 2^23 + 32: rint(32 p) + 32 in the low bits
+  const int2 e = lut[__float_as_int(f) & (kLut - 1)];
+  const int c = e.y + (p >= __int_as_float(e.x) ? 1 : 0);
+  return (p == p) ? c : 0;
+}
+
+// The unrounded quotient p compared against kTheta[T].  For bf16 operands
+// x * rcp_rn(scale) rounds to the same bf16 value as x / scale whenever the
+// product is a normal number: a quotient of two 8-bit significands is either
+// exact or at least 2^-17 (relative) away from every bf16 rounding midpoint
+// (a midpoint needs a 9-bit odd significand), while x * rcp is within 2^-23
+// of the quotient; tiny (subnormal) products lie far inside the code-7
+// interval either way.  Other dtypes divide.
 template <typename T>
-__device__ __forceinline__ bool rcp_usable(float scale) {
-  return scale >= 0x1p-126f && scale <= 0x1p126f;  // finite, normal, not NaN
+__device__ __forceinline__ float nf4_quotient(float x, float scale, float rcp) {
+  if constexpr (sizeof(T) == 2 && Ty<T>::code == LQ_BF16) return __fmul_rn(x, rcp);
+  return __fdiv_rn(x, scale);
 }
 
 struct NfArgs {
@@ -113,8 +138,9 @@ __device__ __forceinline__ void store_codes(void* codes, int64_t e, const int* c
   }
 }
 
-// Quantize kernel.  blockDim.x = 256; a warp team of `tps` lanes holds a
-// group of G = tps*NVT*V elements (vector path, G % V == 0) in registers.
+// Quantize kernel.  blockDim.x = 256; a team of `tps` lanes holds a group of
+// G = tps*NVT*V elements (vector path, G % V == 0) in registers; every team
+// keeps U groups in flight (loads of all U issued before any reduction).
 template <typename T, int NVT, int CODE_DT, bool DQ>
 __global__ void __launch_bounds__(256) nf4_quant_kernel(const T* __restrict__ x, NfArgs a,
                                                         int tps, void* __restrict__ codes,
@@ -122,8 +148,12 @@ __global__ void __launch_bounds__(256) nf4_quant_kernel(const T* __restrict__ x,
                                                         T* __restrict__ q_scales,
                                                         T* __restrict__ dq_scales) {
   constexpr int V = 16 / sizeof(T);
+  constexpr int U = 4;
   extern __shared__ float s_scale[];  // [DG] (double quant only)
   __shared__ MinMax red[8];
+  __shared__ int2 lut[kLut];
+  build_lut<T>(lut);
+  __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int t = lane & (tps - 1);
   const int teams_per_block = blockDim.x / tps;
@@ -132,45 +162,53 @@ __global__ void __launch_bounds__(256) nf4_quant_kernel(const T* __restrict__ x,
     const int64_t g_begin = sg * a.DG;
     const int64_t g_end = min(g_begin + a.DG, a.n_groups);
     // all warps iterate the same number of times
-    for (int64_t gb = g_begin; gb < g_end; gb += teams_per_block) {
-      const int64_t g = gb + team;
-      const bool live = g < g_end;
-      float v[NVT * V];
-      const int64_t e0 = g * a.G;
-      float am = 0.0f;
+    for (int64_t gb = g_begin; gb < g_end; gb += (int64_t)teams_per_block * U) {
+      float v[U][NVT * V];
 #pragma unroll
-      for (int k = 0; k < NVT; ++k) {
-        const int64_t e = e0 + (int64_t)(k * tps + t) * V;
-        if (live && e + V <= a.n) {
-          Vec16<T> u;
-          u.u = ld_nc_v4(x + e);
+      for (int u = 0; u < U; ++u) {
+        const int64_t g = gb + team + (int64_t)u * teams_per_block;
+        const bool live = g < g_end;
+        const int64_t e0 = g * a.G;
 #pragma unroll
-          for (int i = 0; i < V; ++i) v[k * V + i] = Ty<T>::to_f(u.v[i]);
-        } else {
+        for (int k = 0; k < NVT; ++k) {
+          const int64_t e = e0 + (int64_t)(k * tps + t) * V;
+          if (live && e + V <= a.n) {
+            Vec16<T> w;
+            w.u = ld_nc_v4(x + e);
 #pragma unroll
-          for (int i = 0; i < V; ++i) v[k * V + i] = (live && e + i < a.n) ? Ty<T>::to_f(x[e + i]) : 0.0f;
+            for (int i = 0; i < V; ++i) v[u][k * V + i] = Ty<T>::to_f(w.v[i]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < V; ++i)
+              v[u][k * V + i] = (live && e + i < a.n) ? Ty<T>::to_f(x[e + i]) : 0.0f;
+          }
         }
-#pragma unroll
-        for (int i = 0; i < V; ++i) am = fmax_nan(am, fabsf(v[k * V + i]));
       }
-      for (int m = 1; m < tps; m <<= 1) am = fmax_nan(am, __shfl_xor_sync(0xffffffffu, am, m));
-      if (live) {
-        float s = am;               // NaN if the group holds a NaN
-        s = (s < a.lo) ? a.lo : s;  // clamp(min=1e-12) in T
-        const float sr = Ty<T>::round(s);  // absmax is already a T value
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t g = gb + team + (int64_t)u * teams_per_block;
+        const bool live = g < g_end;
+        // absmax as an integer max of |x| bit patterns (NaN bits exceed +inf)
+        int amb = 0;
+#pragma unroll
+        for (int i = 0; i < NVT * V; ++i) amb = max(amb, __float_as_int(v[u][i]) & 0x7FFFFFFF);
+        for (int m = 1; m < tps; m <<= 1) amb = max(amb, __shfl_xor_sync(0xffffffffu, amb, m));
+        const float am = __int_as_float(amb);
+        if (!live) continue;
+        const float s = (am < a.lo) ? a.lo : am;  // clamp(min=1e-12) in T; NaN passes
         if (t == 0) {
-          scales[g] = Ty<T>::from_f(sr);
-          if constexpr (DQ) s_scale[g - g_begin] = sr;
+          scales[g] = Ty<T>::from_f(s);
+          if constexpr (DQ) s_scale[g - g_begin] = s;
         }
-        const bool rok = rcp_usable<T>(sr);
-        const float rcp = rok ? __frcp_rn(sr) : 0.0f;
+        const float rcp = __frcp_rn(s);
+        const int64_t e0 = g * a.G;
 #pragma unroll
         for (int k = 0; k < NVT; ++k) {
           const int64_t e = e0 + (int64_t)(k * tps + t) * V;
           if (e >= a.n) continue;
           int c[V];
 #pragma unroll
-          for (int i = 0; i < V; ++i) c[i] = nf4_code(xnorm<T>(v[k * V + i], sr, rcp, rok));
+          for (int i = 0; i < V; ++i) c[i] = nf4_encode(nf4_quotient<T>(v[u][k * V + i], s, rcp), lut);
           store_codes<V, CODE_DT>(codes, e, c, a.n);
         }
       }
@@ -181,8 +219,8 @@ __global__ void __launch_bounds__(256) nf4_quant_kernel(const T* __restrict__ x,
       const int cnt = (int)(g_end - g_begin);
       MinMax r;
       r.init();
-      for (int j = threadIdx.x; j < cnt; j += blockDim.x) r.add(fabsf(s_scale[j]));
-      for (int m = 16; m >= 1; m >>= 1) r.shfl_xor_merge(m);
+      for (int j = threadIdx.x; j < cnt; j += blockDim.x) r.add_max(fabsf(s_scale[j]));
+      for (int m = 16; m >= 1; m >>= 1) r.shfl_xor_merge(m, true);
       if (lane == 0) red[warp] = r;
       __syncthreads();
       MinMax tot = red[0];
@@ -194,6 +232,146 @@ __global__ void __launch_bounds__(256) nf4_quant_kernel(const T* __restrict__ x,
         float sn = tdiv<T>(s_scale[j], dq);
         float q = tclamp(trint(tmul<T>(sn, 127.0f)), -127.0f, 127.0f);
         q_scales[g_begin + j] = Ty<T>::from_f(q);
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// bf16 input, packed 4-bit codes (QLoRALinear.pack_base): the same algorithm
+// as nf4_quant_kernel on raw 32-bit words (two bf16 each).
+//   absmax: |w| = w & 0x7FFF7FFF and an unsigned 16-bit-pair max; for
+//           non-negative bf16 bit patterns the integer order is the float
+//           order and NaN patterns lie above +inf, so NaN propagates;
+//   quotient: x * rcp_rn(scale) (see nf4_quotient), one shift per element to
+//           widen bf16 to fp32;
+//   NaN: a quotient can only be NaN when the scale is not finite, so the
+//           per-element NaN test runs only for such groups;
+//   packing: codes folded into nibbles with integer multiply-adds.
+__device__ __forceinline__ int nf4_encode_finite(float p, const int2* lut) {
+  const float f = fmaf(p, 32.0f, 12582944.0f);
+  const int2 e = lut[__float_as_int(f) & (kLut - 1)];
+  return e.y + (p >= __int_as_float(e.x) ? 1 : 0);
+}
+
+__device__ __forceinline__ uint32_t nf4_pack8_bf16(const uint4& w, float rcp, bool finite,
+                                                   const int2* lut) {
+  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+  int c[8];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float lo = __uint_as_float(ws[j] << 16), hi = __uint_as_float(ws[j] & 0xFFFF0000u);
+    const float plo = __fmul_rn(lo, rcp), phi = __fmul_rn(hi, rcp);
+    c[2 * j] = nf4_encode_finite(plo, lut);
+    c[2 * j + 1] = nf4_encode_finite(phi, lut);
+    if (!finite) {
+      c[2 * j] = (plo == plo) ? c[2 * j] : 0;
+      c[2 * j + 1] = (phi == phi) ? c[2 * j + 1] : 0;
+    }
+  }
+  uint32_t acc = (uint32_t)c[7];
+#pragma unroll
+  for (int i = 6; i >= 0; --i) acc = acc * 16u + (uint32_t)c[i];
+  return acc;
+}
+
+template <int NVT, bool DQ>
+__global__ void __launch_bounds__(256) nf4_pack_bf16_kernel(const __nv_bfloat16* __restrict__ x,
+                                                            NfArgs a, int tps,
+                                                            uint8_t* __restrict__ codes,
+                                                            __nv_bfloat16* __restrict__ scales,
+                                                            __nv_bfloat16* __restrict__ q_scales,
+                                                            __nv_bfloat16* __restrict__ dq_scales) {
+  using T = __nv_bfloat16;
+  constexpr int V = 8;
+  constexpr int U = 4;
+  extern __shared__ float s_scale[];  // [DG] (double quant only)
+  __shared__ MinMax red[8];
+  __shared__ int2 lut[kLut];
+  build_lut<T>(lut);
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int t = lane & (tps - 1);
+  const int teams_per_block = blockDim.x / tps;
+  const int team = threadIdx.x / tps;
+  for (int64_t sg = blockIdx.x; sg < a.n_super; sg += gridDim.x) {
+    const int64_t g_begin = sg * a.DG;
+    const int64_t g_end = min(g_begin + a.DG, a.n_groups);
+    for (int64_t gb = g_begin; gb < g_end; gb += (int64_t)teams_per_block * U) {
+      uint4 w[U][NVT];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t g = gb + team + (int64_t)u * teams_per_block;
+        const bool live = g < g_end;
+#pragma unroll
+        for (int k = 0; k < NVT; ++k) {
+          const int64_t e = g * a.G + (int64_t)(k * tps + t) * V;
+          if (live && e + V <= a.n) {
+            w[u][k] = ld_nc_v4(x + e);
+          } else {
+            uint16_t hv[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) hv[i] = (live && e + i < a.n) ? __bfloat16_as_ushort(x[e + i]) : 0;
+            w[u][k] = make_uint4(hv[0] | (uint32_t)hv[1] << 16, hv[2] | (uint32_t)hv[3] << 16,
+                                 hv[4] | (uint32_t)hv[5] << 16, hv[6] | (uint32_t)hv[7] << 16);
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t g = gb + team + (int64_t)u * teams_per_block;
+        const bool live = g < g_end;
+        uint32_t m2 = 0;
+#pragma unroll
+        for (int k = 0; k < NVT; ++k) {
+          m2 = __vmaxu2(m2, w[u][k].x & 0x7FFF7FFFu);
+          m2 = __vmaxu2(m2, w[u][k].y & 0x7FFF7FFFu);
+          m2 = __vmaxu2(m2, w[u][k].z & 0x7FFF7FFFu);
+          m2 = __vmaxu2(m2, w[u][k].w & 0x7FFF7FFFu);
+        }
+        uint32_t m16 = max(m2 & 0xFFFFu, m2 >> 16);
+        for (int m = 1; m < tps; m <<= 1) m16 = max(m16, __shfl_xor_sync(0xffffffffu, m16, m));
+        if (!live) continue;
+        const float am = __uint_as_float(m16 << 16);
+        const float s = (am < a.lo) ? a.lo : am;  // clamp(min=1e-12) in bf16; NaN passes
+        if (t == 0) {
+          scales[g] = __float2bfloat16_rn(s);
+          if constexpr (DQ) s_scale[g - g_begin] = s;
+        }
+        const float rcp = __frcp_rn(s);
+        const bool finite = s <= 3.40282347e38f;
+#pragma unroll
+        for (int k = 0; k < NVT; ++k) {
+          const int64_t e = g * a.G + (int64_t)(k * tps + t) * V;
+          if (e >= a.n) continue;
+          const uint32_t pk = nf4_pack8_bf16(w[u][k], rcp, finite, lut);
+          if (e + V <= a.n) {
+            *reinterpret_cast<uint32_t*>(codes + e / 2) = pk;
+          } else {
+            for (int i = 0; i < V; i += 2)
+              if (e + i < a.n) codes[(e + i) / 2] = (uint8_t)((pk >> (4 * i)) & (e + i + 1 < a.n ? 0xFF : 0x0F));
+          }
+        }
+      }
+    }
+    if constexpr (DQ) {
+      __syncthreads();
+      const int cnt = (int)(g_end - g_begin);
+      MinMax r;
+      r.init();
+      for (int j = threadIdx.x; j < cnt; j += blockDim.x) r.add_max(fabsf(s_scale[j]));
+      for (int m = 16; m >= 1; m >>= 1) r.shfl_xor_merge(m, true);
+      if (lane == 0) red[warp] = r;
+      __syncthreads();
+      MinMax tot = red[0];
+      for (int w2 = 1; w2 < (int)(blockDim.x >> 5); ++w2) tot.merge(red[w2]);
+      float dq = fmax_nan(tot.mx, 0.0f);
+      dq = (dq < a.lo) ? a.lo : dq;
+      if (threadIdx.x == 0) dq_scales[sg] = __float2bfloat16_rn(dq);
+      for (int j = threadIdx.x; j < cnt; j += blockDim.x) {
+        float sn = tdiv<T>(s_scale[j], dq);
+        float q = tclamp(trint(tmul<T>(sn, 127.0f)), -127.0f, 127.0f);
+        q_scales[g_begin + j] = __float2bfloat16_rn(q);
       }
       __syncthreads();
     }
@@ -231,13 +409,16 @@ template <typename T, int CODE_DT>
 __global__ void __launch_bounds__(256) nf4_codes_kernel(const T* __restrict__ x, NfArgs a,
                                                         const T* __restrict__ scales,
                                                         void* __restrict__ codes) {
+  __shared__ int2 lut[kLut];
+  build_lut<T>(lut);
+  __syncthreads();
   const int64_t npair = (a.n + 1) / 2;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < npair;
        i += (int64_t)gridDim.x * blockDim.x) {
     int c[2] = {0, 0};
     for (int k = 0; k < 2; ++k) {
       const int64_t e = 2 * i + k;
-      if (e < a.n) c[k] = nf4_code(tdiv<T>(Ty<T>::to_f(x[e]), Ty<T>::to_f(scales[e / a.G])));
+      if (e < a.n) c[k] = nf4_encode(__fdiv_rn(Ty<T>::to_f(x[e]), Ty<T>::to_f(scales[e / a.G])), lut);
     }
     if constexpr (CODE_DT == LQ_U4X2) {
       static_cast<uint8_t*>(codes)[i] = (uint8_t)(c[0] | (c[1] << 4));
@@ -261,16 +442,17 @@ __global__ void __launch_bounds__(256) nf4_dequant_kernel(const void* __restrict
                                                           const T* __restrict__ scales,
                                                           const T* __restrict__ q_scales,
                                                           const T* __restrict__ dq_scales,
-                                                          T* __restrict__ out, int vec) {
+                                                          T* __restrict__ out, int vec,
+                                                          int64_t e_begin) {
   __shared__ float tab[16];
   if (threadIdx.x < 16) tab[threadIdx.x] = Ty<T>::round(kNF4[threadIdx.x]);
   __syncthreads();
-  const int64_t nthr = (a.n + 7) / 8;
+  const int64_t nthr = (a.n - e_begin + 7) / 8;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nthr;
        i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t e0 = i * 8;
+    const int64_t e0 = e_begin + i * 8;
     int c[8];
-    if (CODE_DT == LQ_U4X2 && vec && e0 + 8 <= a.n) {
+    if (CODE_DT == LQ_U4X2 && vec && e0 + 8 <= a.n && (e0 & 7) == 0) {
       uint32_t w = *reinterpret_cast<const uint32_t*>(static_cast<const uint8_t*>(codes) + e0 / 2);
 #pragma unroll
       for (int k = 0; k < 8; ++k) c[k] = (w >> (4 * k)) & 15;
@@ -320,6 +502,66 @@ __global__ void __launch_bounds__(256) nf4_dequant_kernel(const void* __restrict
       for (int k = 0; k < 8; ++k)
         if (e0 + k < a.n) out[e0 + k] = Ty<T>::from_f(o[k]);
     }
+  }
+}
+
+// Vectorized dequantize of packed codes for 2-byte T: thread = 32 elements
+// (16 bytes of codes, 64 bytes of output), all in one group (G % 32 == 0).
+// pair[b] holds round_T(NF4_TABLE) of both nibbles of code byte b; the
+// product with the scale is __hmul2, whose correctly rounded result equals
+// round_T(fp32 product) because the product of two 8- or 11-bit significands
+// is exact in fp32.
+template <typename T>
+__global__ void __launch_bounds__(256) nf4_unpack_vec_kernel(const uint4* __restrict__ codes,
+                                                             NfArgs a,
+                                                             const T* __restrict__ scales,
+                                                             const T* __restrict__ q_scales,
+                                                             const T* __restrict__ dq_scales,
+                                                             T* __restrict__ out, int64_t nchunk) {
+  __shared__ uint32_t pair[256];
+  for (int b = threadIdx.x; b < 256; b += blockDim.x) {
+    union {
+      T h[2];
+      uint32_t u;
+    } pr;
+    pr.h[0] = Ty<T>::from_f(Ty<T>::round(kNF4[b & 15]));
+    pr.h[1] = Ty<T>::from_f(Ty<T>::round(kNF4[b >> 4]));
+    pair[b] = pr.u;
+  }
+  __syncthreads();
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nchunk;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e0 = i * 32;
+    const int64_t g = a.g_shift >= 0 ? (e0 >> a.g_shift) : e0 / a.G;
+    float s;
+    if (q_scales) s = tmul<T>(tdiv<T>(Ty<T>::to_f(q_scales[g]), 127.0f), Ty<T>::to_f(dq_scales[g / a.DG]));
+    else s = Ty<T>::to_f(scales[g]);
+    union {
+      T h[2];
+      uint32_t u;
+    } s2;
+    s2.h[0] = s2.h[1] = Ty<T>::from_f(s);
+    const uint4 c = codes[i];
+    const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+    uint32_t o[16];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        uint32_t pv = pair[(w[j] >> (8 * b)) & 255];
+        if constexpr (Ty<T>::code == LQ_BF16) {
+          __nv_bfloat162 r = __hmul2(*reinterpret_cast<__nv_bfloat162*>(&pv),
+                                     *reinterpret_cast<__nv_bfloat162*>(&s2.u));
+          o[j * 4 + b] = *reinterpret_cast<uint32_t*>(&r);
+        } else {
+          __half2 r = __hmul2(*reinterpret_cast<__half2*>(&pv), *reinterpret_cast<__half2*>(&s2.u));
+          o[j * 4 + b] = *reinterpret_cast<uint32_t*>(&r);
+        }
+      }
+    }
+    uint4* dst = reinterpret_cast<uint4*>(out + e0);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) st_v4(dst + k, make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]));
   }
 }
 
@@ -425,6 +667,13 @@ int nf4_quant_launch(const T* x, NfArgs a, void* codes, T* scales, T* qs, T* dqs
   }
   size_t smem = DQ ? (size_t)a.DG * sizeof(float) : 0;
   int grid = grid_cap(a.n_super, 8);
+  if constexpr (std::is_same<T, __nv_bfloat16>::value && CODE_DT == LQ_U4X2) {
+    uint8_t* cp = static_cast<uint8_t*>(codes);
+    if (nvt == 1) nf4_pack_bf16_kernel<1, DQ><<<grid, 256, smem, st>>>(x, a, tps, cp, scales, qs, dqs);
+    else if (nvt == 2) nf4_pack_bf16_kernel<2, DQ><<<grid, 256, smem, st>>>(x, a, tps, cp, scales, qs, dqs);
+    else nf4_pack_bf16_kernel<4, DQ><<<grid, 256, smem, st>>>(x, a, tps, cp, scales, qs, dqs);
+    return launched("nf4_pack_bf16_kernel");
+  }
   if (nvt == 1) nf4_quant_kernel<T, 1, CODE_DT, DQ><<<grid, 256, smem, st>>>(x, a, tps, codes, scales, qs, dqs);
   else if (nvt == 2) nf4_quant_kernel<T, 2, CODE_DT, DQ><<<grid, 256, smem, st>>>(x, a, tps, codes, scales, qs, dqs);
   else nf4_quant_kernel<T, 4, CODE_DT, DQ><<<grid, 256, smem, st>>>(x, a, tps, codes, scales, qs, dqs);
@@ -473,16 +722,28 @@ int nf4_dequant_t(const void* codes, int cdt, int64_t n, int64_t G, int64_t DG, 
   a.n_super = 0;
   a.lo = 0;
   a.g_shift = log2_exact(G);
-  int vec = aligned16(out) && (reinterpret_cast<uintptr_t>(codes) % 4 == 0);
-  int grid = grid_cap((n + 8 * 256 - 1) / (8 * 256), 16);
   const T* sp = static_cast<const T*>(s);
   const T* q = static_cast<const T*>(qs);
   const T* d = static_cast<const T*>(dqs);
   T* o = static_cast<T*>(out);
+  int64_t done = 0;
+  if (sizeof(T) == 2 && cdt == LQ_U4X2 && G % 32 == 0 && aligned16(codes) && aligned16(out)) {
+    const int64_t nchunk = n / 32;
+    if (nchunk > 0) {
+      nf4_unpack_vec_kernel<T><<<grid_cap((nchunk + 255) / 256, 16), 256, 0, st>>>(
+          static_cast<const uint4*>(codes), a, sp, q, d, o, nchunk);
+      int rc = launched("nf4_unpack_vec_kernel");
+      if (rc) return rc;
+      done = nchunk * 32;
+    }
+    if (done == n) return LQ_OK;
+  }
+  int vec = aligned16(out) && (reinterpret_cast<uintptr_t>(codes) % 4 == 0);
+  int grid = grid_cap((n - done + 8 * 256 - 1) / (8 * 256), 16);
   switch (cdt) {
-    case LQ_U4X2: nf4_dequant_kernel<T, LQ_U4X2><<<grid, 256, 0, st>>>(codes, a, sp, q, d, o, vec); break;
-    case LQ_U8: nf4_dequant_kernel<T, LQ_U8><<<grid, 256, 0, st>>>(codes, a, sp, q, d, o, vec); break;
-    case LQ_I64: nf4_dequant_kernel<T, LQ_I64><<<grid, 256, 0, st>>>(codes, a, sp, q, d, o, vec); break;
+    case LQ_U4X2: nf4_dequant_kernel<T, LQ_U4X2><<<grid, 256, 0, st>>>(codes, a, sp, q, d, o, vec, done); break;
+    case LQ_U8: nf4_dequant_kernel<T, LQ_U8><<<grid, 256, 0, st>>>(codes, a, sp, q, d, o, vec, done); break;
+    case LQ_I64: nf4_dequant_kernel<T, LQ_I64><<<grid, 256, 0, st>>>(codes, a, sp, q, d, o, vec, done); break;
     default: set_error("unsupported code dtype %d", cdt); return LQ_EDTYPE;
   }
   return launched("nf4_dequant_kernel");

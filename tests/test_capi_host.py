@@ -81,11 +81,13 @@ def test_argument_validation_without_gpu(lib_path):
     assert lib.lq_group_quant(None, 0, 0, 8, 4, 4, 1, 1, None, 0, None, None, None) == 0
 
 
-def _oracle_thresholds():
-    from oracle.lq_oracle import nf4_encode
+def _oracle_thresholds(dtype="float32"):
+    """Smallest fp32 quotient p at which the reference's code of round_dtype(p)
+    reaches i, for i = 1..15 (bisection over fp32 bit patterns)."""
+    from oracle.lq_oracle import nf4_encode, rnd
 
     def code(v):
-        return int(nf4_encode(np.array([v], np.float32))[0])
+        return int(nf4_encode(rnd(np.array([v], np.float32), dtype))[0])
 
     def key(f):
         u = int(np.array([f], np.float32).view(np.int32)[0])
@@ -108,29 +110,48 @@ def _oracle_thresholds():
     return out
 
 
-def test_nf4_kernel_thresholds_match_reference_rule():
+def _kernel_theta_rows():
     src = open(NF4_SRC).read()
-    body = src[src.index("int nf4_code(float xn)"):]
-    body = body[:body.index("return c;")]
-    hexes = re.findall(r"xn >= (-?0x[0-9a-f.]+p-?\d+)f", body)
-    assert len(hexes) == 15
-    kernel = [np.float32(float.fromhex(h)) for h in hexes]
-    assert kernel == _oracle_thresholds()
+    body = src[src.index("kTheta[3][15] = {"):]
+    body = body[:body.index("}};") + 3]
+    hexes = re.findall(r"(-?0x[0-9a-f.]+p-?\d+)f", body)
+    assert len(hexes) == 45
+    vals = [np.float32(float.fromhex(h)) for h in hexes]
+    return {"float32": vals[0:15], "float16": vals[15:30], "bfloat16": vals[30:45]}
 
 
-def test_nf4_threshold_count_equals_argmin_on_grids():
-    """The count-of-thresholds encoder equals the reference argmin on every
-    bf16 / fp16 value in [-1, 1] and near every boundary in fp32."""
-    from oracle.lq_oracle import nf4_encode
-    th = np.array(_oracle_thresholds(), np.float32)
+@pytest.mark.parametrize("dtype", ["float32", "float16", "bfloat16"])
+def test_nf4_kernel_thresholds_match_reference_rule(dtype):
+    assert _kernel_theta_rows()[dtype] == _oracle_thresholds(dtype)
+
+
+@pytest.mark.parametrize("dtype", ["float32", "float16", "bfloat16"])
+def test_nf4_bucket_table_encoder_equals_argmin(dtype):
+    """The kernel's encoder -- bucket b = rint(32 p) + 32 of [-1, 1], code =
+    (code at the bucket's left edge) + (p >= threshold inside the bucket) --
+    equals the reference argmin of round_dtype(p), on dense samples, every
+    bf16 / fp16 value in [-1, 1], the thresholds and their fp32 neighbours."""
+    from oracle.lq_oracle import nf4_encode, rnd
+    th = np.array(_kernel_theta_rows()[dtype], np.float32)
+    left = ((2 * np.arange(65) - 65) / 64).astype(np.float32)
+    right = ((2 * np.arange(65) - 63) / 64).astype(np.float32)
+    code_lo = (th[None, :] <= left[:, None]).sum(1)
+    inside = (th[None, :] > left[:, None]) & (th[None, :] <= right[:, None])
+    assert inside.sum(1).max() <= 1
+    theta = np.where(inside.any(1), (th[None, :] * inside).sum(1), np.inf).astype(np.float32)
     u = (np.arange(0, 0x10000, dtype=np.uint32) << 16).view(np.float32)
     v16 = np.arange(0, 0x10000, dtype=np.uint32).astype(np.uint16).view(np.float16).astype(np.float32)
-    rng = np.random.default_rng(0)
-    vals = np.concatenate([u, v16, rng.uniform(-1, 1, 200000).astype(np.float32),
-                           np.array([np.nan, -0.0, 0.0], np.float32)])
-    vals = vals[np.isnan(vals) | (np.abs(vals) <= 1)]
-    count = (vals[:, None] >= th[None, :]).sum(1)
-    assert np.array_equal(count, nf4_encode(vals))
+    rng = np.random.default_rng(1)
+    p = np.concatenate([u, v16, rng.uniform(-1, 1, 500000).astype(np.float32), th,
+                        np.nextafter(th, np.float32(-2)), np.nextafter(th, np.float32(2)),
+                        left, right, np.array([-0.0, 0.0, np.nan], np.float32)])
+    p = p[np.isnan(p) | (np.abs(p) <= 1)]
+    with np.errstate(invalid="ignore"):
+        b = (np.rint(p.astype(np.float64) * 32) + 32)
+    b = np.where(np.isnan(b), 0, b).astype(np.int64)
+    code = code_lo[b] + (p >= theta[b])
+    code = np.where(np.isnan(p), 0, code)
+    assert np.array_equal(code, nf4_encode(rnd(p, dtype)))
 
 
 def test_host_rejects_cpu_tensors():
