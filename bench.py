@@ -268,15 +268,26 @@ class NF4Workload:
         return 2 * len(self.weights)
 
     def kernels(self):
-        """Time pack and unpack alone on the largest weight of the rank."""
+        """Time pack and unpack alone on weights of the largest shape of the
+        rank, cycling through up to 4 of them (470 MB of bf16, more than L2)."""
         torch = self.ctx.torch
-        i = max(range(len(self.weights)), key=lambda j: self.weights[j].numel())
-        w, m = self.weights[i], self.mods[i]
-        n = w.numel()
+        n = max(w.numel() for w in self.weights)
+        idx = [j for j, w in enumerate(self.weights) if w.numel() == n][:4]
         ng, nd = n / 64, n / 64 / 256
-        m.pack_base(w)
-        t_pack = cuda_time_ms(torch, lambda: m.pack_base(w), 20)
-        t_unpack = cuda_time_ms(torch, lambda: m._dequantize_base(), 20)
+        c = [0, 0]
+
+        def pack():
+            j = idx[c[0] % len(idx)]
+            self.mods[j].pack_base(self.weights[j])
+            c[0] += 1
+
+        def unpack():
+            self.mods[idx[c[1] % len(idx)]]._dequantize_base()
+            c[1] += 1
+        for j in idx:
+            self.mods[j].pack_base(self.weights[j])
+        t_pack = cuda_time_ms(torch, pack, 8 * len(idx))
+        t_unpack = cuda_time_ms(torch, unpack, 8 * len(idx))
         b_pack = 2 * n + n / 2 + 4 * ng + 2 * nd
         b_unpack = n / 2 + 2 * ng + 2 * nd + 2 * n
         return {
@@ -381,10 +392,16 @@ class GroupWorkload:
         return len(self.ws)
 
     def kernels(self):
-        w = self.ws[0]
-        t = cuda_time_ms(self.ctx.torch, lambda: self.L.fake_quantize(
-            w, 4, False, self.L.QScheme.PER_GROUP, 128), 50)
-        return {"group_warp_kernel (fake_quantize)": (8.0 * w.numel(), t, w.numel(), "elements")}
+        """fake_quantize timed alone, cycling through the 8 matrices (512 MB of
+        input, more than L2)."""
+        c = [0]
+
+        def f():
+            self.L.fake_quantize(self.ws[c[0] % len(self.ws)], 4, False, self.L.QScheme.PER_GROUP, 128)
+            c[0] += 1
+        t = cuda_time_ms(self.ctx.torch, f, 48)
+        n = self.ws[0].numel()
+        return {"group_warp_kernel (fake_quantize)": (8.0 * n, t, n, "elements")}
 
     def e2e(self, steps, graph):
         """fake_quantize through the public API on matrices copied in from
@@ -430,10 +447,10 @@ class GroupWorkload:
 class RotQuantWorkload:
     """QuaRot activation path: Hadamard (d = 4096) + per-token INT4 sym fake
     quant of bf16 [8192, 4096] activations with 1% outlier channels x50,
-    fused in one kernel; 4 distinct batches rotate so inputs exceed L2
-    (weak scaling: each rank its own activations)."""
+    fused in one kernel; a step processes 4 distinct batches (512 MB in and
+    out, more than L2; weak scaling: each rank its own activations)."""
     name = "rotquant"
-    workload = "quarot_fht4096_pertoken_int4_bf16_8192x4096"
+    workload = "quarot_fht4096_pertoken_int4_bf16_8192x4096_x4"
 
     def __init__(self, ctx):
         torch = ctx.torch
@@ -446,20 +463,19 @@ class RotQuantWorkload:
             idx = torch.randperm(4096, generator=g, device=ctx.dev)[:41]
             a[:, idx] *= 50
             self.xs.append(a.to(torch.bfloat16))
-        self.n_local = self.xs[0].numel()
+        self.n_local = sum(a.numel() for a in self.xs)
         self.n_total = self.n_local * ctx.world
-        self.i = 0
 
     @staticmethod
     def bytes_for(n):
         return 4.0 * n
 
     def step(self):
-        self.L.hadamard_fake_quantize(self.xs[self.i % 4], 4, True)
-        self.i += 1
+        for a in self.xs:
+            self.L.hadamard_fake_quantize(a, 4, True)
 
     def launches_per_step(self):
-        return 1
+        return len(self.xs)
 
     def kernels(self):
         c = [0]
@@ -479,8 +495,9 @@ class RotQuantWorkload:
         dev = torch.empty_like(self.xs[0])
 
         def one():
-            dev.copy_(host, non_blocking=True)
-            out.copy_(self.L.hadamard_fake_quantize(dev, 4, True), non_blocking=True)
+            for _ in self.xs:
+                dev.copy_(host, non_blocking=True)
+                out.copy_(self.L.hadamard_fake_quantize(dev, 4, True), non_blocking=True)
 
         one()
         torch.cuda.synchronize()
@@ -490,7 +507,7 @@ class RotQuantWorkload:
             one()
         e1.record()
         torch.cuda.synchronize()
-        nb = host.numel() * 2
+        nb = host.numel() * 2 * len(self.xs)
         return e0.elapsed_time(e1) / steps, nb, nb
 
     def gather(self):
@@ -645,28 +662,35 @@ class KVWorkload:
 
 class W4A16Workload:
     """QuantizedLinear W4A16 forward: Linear(4096, 14336), int4 asym group 128
-    with fp16 scales / zeros, fp16 activations ~ N(0, 1).  A step is one
-    forward at M = 1024 tokens (the headline point); every M in
-    {1, 16, 128, 1024, 4096} is timed in `kernels`.  Weak scaling (replicas)."""
+    with fp16 scales / zeros, fp16 activations ~ N(0, 1).  Six such layers
+    with distinct weights (6 x 29 MB packed, more than L2, like consecutive
+    layers of a model); a step is the forward of all six at M = 1024 tokens
+    (the headline point); every M in {1, 16, 128, 1024, 4096} is timed in
+    `kernels`, cycling through the layers.  Weak scaling (replicas)."""
     name = "w4a16"
-    workload = "quantized_linear_w4a16_K4096_N14336_g128_fp16_M1024"
+    workload = "quantized_linear_w4a16_K4096_N14336_g128_fp16_M1024_x6_layers"
     Ms = (1, 16, 128, 1024, 4096)
     K, N = 4096, 14336
+    LAYERS = 6
 
     def __init__(self, ctx):
         torch = ctx.torch
         import llm_quant_b200 as L
         self.ctx, self.L = ctx, L
         g = torch.Generator(device=ctx.dev).manual_seed(0)
-        lin = torch.nn.Linear(self.K, self.N, device=ctx.dev)
-        with torch.no_grad():
-            lin.weight.copy_(torch.randn(self.N, self.K, generator=g, device=ctx.dev) * 0.02)
-        lin = lin.half()
-        self.ql = L.QuantizedLinear.from_linear(lin, 4, False, 128)
+        self.qls = []
+        for _ in range(self.LAYERS):
+            lin = torch.nn.Linear(self.K, self.N, device=ctx.dev)
+            with torch.no_grad():
+                lin.weight.copy_(torch.randn(self.N, self.K, generator=g, device=ctx.dev) * 0.02)
+            self.qls.append(L.QuantizedLinear.from_linear(lin.half(), 4, False, 128))
+            del lin
+        self.ql = self.qls[0]
         self.x = {m: torch.randn(m, self.K, generator=g, device=ctx.dev).half() for m in self.Ms}
-        self.ql(self.x[1])  # builds the packed operand
-        self.n_local = 1
-        self.n_total = ctx.world
+        for ql in self.qls:
+            ql(self.x[1])  # builds the packed operand
+        self.n_local = self.LAYERS
+        self.n_total = self.LAYERS * ctx.world
         self.unit = "TFLOP/s"
 
     def flops(self, m):
@@ -676,13 +700,22 @@ class W4A16Workload:
         return self.flops(1024) * n
 
     def step(self):
-        self.ql(self.x[1024])
+        for ql in self.qls:
+            ql(self.x[1024])
+
+    def launches_per_step(self):
+        return self.LAYERS
 
     def kernels(self):
         out = {}
         for m in self.Ms:
             x = self.x[m]
-            t = cuda_time_ms(self.ctx.torch, lambda: self.ql(x), 20)
+            c = [0]
+
+            def f():
+                self.qls[c[0] % self.LAYERS](x)
+                c[0] += 1
+            t = cuda_time_ms(self.ctx.torch, f, 4 * self.LAYERS)
             wbytes = self.N * self.K / 2 + self.N * (self.K // 128) * 4
             out[f"w4a16_kernel M={m}"] = (self.flops(m), t, m,
                                           wbytes + 2 * m * self.K + 2 * m * self.N)
@@ -695,16 +728,20 @@ class W4A16Workload:
         host = self.x[1024].cpu().pin_memory()
         out = torch.empty(1024, self.N, dtype=torch.float16).pin_memory()
         dev = self.x[1024]
-        self.ql(dev)
         torch.cuda.synchronize()
-        g2 = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g2):
-            y = self.ql(dev)
+        graphs, ys = [], []
+        for ql in self.qls:
+            ql(dev)
+            g2 = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g2):
+                ys.append(ql(dev))
+            graphs.append(g2)
 
         def one():
-            dev.copy_(host, non_blocking=True)
-            g2.replay()
-            out.copy_(y, non_blocking=True)
+            for g2, y in zip(graphs, ys):
+                dev.copy_(host, non_blocking=True)
+                g2.replay()
+                out.copy_(y, non_blocking=True)
 
         one()
         torch.cuda.synchronize()
@@ -714,7 +751,8 @@ class W4A16Workload:
             one()
         e1.record()
         torch.cuda.synchronize()
-        return e0.elapsed_time(e1) / steps, host.numel() * 2, out.numel() * 2
+        return (e0.elapsed_time(e1) / steps, host.numel() * 2 * self.LAYERS,
+                out.numel() * 2 * self.LAYERS)
 
     def gather(self):
         return 0.0, 0

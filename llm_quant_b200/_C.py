@@ -147,6 +147,18 @@ def require_cuda(*tensors: torch.Tensor, what: str = "llm_quant_b200") -> None:
                 "(llm_quant_b200 has no CPU implementation)")
 
 
+def check_clamp_bounds(dtype: torch.dtype, n_bits: int, symmetric: bool) -> None:
+    """torch.clamp converts its scalar bounds to the tensor's dtype and raises
+    when a bound overflows it, which for the code range means an fp16 tensor
+    with qmax = 2^16 - 1 (asymmetric 16-bit); the reference fails there, so
+    this layer does too, with torch's message."""
+    if dtype != torch.float16:
+        return
+    qmin, qmax = (-(2 ** (n_bits - 1)), 2 ** (n_bits - 1) - 1) if symmetric else (0, 2 ** n_bits - 1)
+    if max(abs(qmin), abs(qmax)) > 65519:
+        raise RuntimeError("value cannot be converted to type c10::Half without overflow")
+
+
 def require_float(t: torch.Tensor, what: str) -> None:
     if t.dtype not in FLOAT_TYPES:
         raise TypeError(f"{what}: unsupported dtype {t.dtype} (float32, float16, bfloat16)")

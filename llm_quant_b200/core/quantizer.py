@@ -119,6 +119,8 @@ def compute_qparams(
     sch = _scheme(scheme)
     _C.require_cuda(x, what="compute_qparams")
     _C.require_float(x, "compute_qparams")
+    if not symmetric:  # the zero point is clamped to the code range
+        _C.check_clamp_bounds(x.dtype, n_bits, symmetric)
     xc = x.detach().contiguous()
     if sch == "per_tensor":
         return _tensor_qparams(xc, n_bits, symmetric)
@@ -220,6 +222,7 @@ def quantize_tensor(
     for d in (d0, d1):
         if d not in _C.FLOAT_TYPES:
             raise TypeError(f"quantize_tensor: unsupported result dtype {d}")
+    _C.check_clamp_bounds(d1, n_bits, symmetric)
     return _affine(_C.AFFINE_QUANT, x, scale, zero_point, d0, d1, n_bits, symmetric, d1)
 
 
@@ -294,6 +297,7 @@ def fake_quantize(
     sch = _scheme(scheme)
     _C.require_cuda(x, what="fake_quantize")
     _C.require_float(x, "fake_quantize")
+    _C.check_clamp_bounds(x.dtype, n_bits, symmetric)
     if x.requires_grad and torch.is_grad_enabled():
         return _FakeQuantFn.apply(x, n_bits, symmetric, sch, group_size)
     return _fake_quant_forward(x, n_bits, symmetric, sch, group_size)

@@ -45,6 +45,7 @@ def _fht(x: torch.Tensor, n_bits=None, symmetric=True, want_qparams=False):
     if n_bits is None:
         _C.call("lq_hadamard", xc.data_ptr(), _C.dt(xc), rows, d, out.data_ptr(), _C.stream_ptr(xc))
         return out
+    _C.check_clamp_bounds(xc.dtype, n_bits, symmetric)
     s = z = None
     if want_qparams:
         s = torch.empty(rows, 1, dtype=xc.dtype, device=xc.device)

@@ -79,9 +79,10 @@ __global__ void __launch_bounds__(256) affine_kernel(const void* __restrict__ x,
     } else {
       const float t = round_to(a.d1, __fadd_rn(round_to(a.d0, __fdiv_rn(xv, sv)), zv));
       if constexpr (OP == LQ_AFFINE_QUANT) {
-        o = tclamp(trint(t), a.qmin, a.qmax);
+        // the clamp bounds act in the result dtype (4095 -> 4096 in bf16)
+        o = tclamp(trint(t), round_to(a.d1, a.qmin), round_to(a.d1, a.qmax));
       } else {
-        const float q = tclamp(tste(t), a.qmin, a.qmax);
+        const float q = tclamp(tste(t), round_to(a.d1, a.qmin), round_to(a.d1, a.qmax));
         o = round_to(a.d1, __fmul_rn(round_to(a.d1, __fsub_rn(q, zv)), sv));
       }
     }

@@ -119,6 +119,14 @@ __device__ __forceinline__ float tclamp(float v, float lo, float hi) {
   return (v > hi) ? hi : v;
 }
 
+// torch.clamp(t, lo, hi) on a tensor of dtype T: the scalar bounds are
+// converted to T first, so a bound T cannot hold acts as its rounded value
+// (qmax = 4095 clamps to 4096 in bf16).
+template <typename T>
+__device__ __forceinline__ float tclamp_t(float v, float lo, float hi) {
+  return tclamp(v, Ty<T>::round(lo), Ty<T>::round(hi));
+}
+
 // torch.round: half to even, sign of zero kept.
 __device__ __forceinline__ float trint(float v) { return rintf(v); }
 
@@ -195,7 +203,7 @@ __device__ __forceinline__ void qparams_from(const MinMax& r, bool sym, float qm
     float rng = tsub<T>(mx, mn);
     rng = (rng < lo_T) ? lo_T : rng;
     scale = tdiv<T>(rng, qmax - qmin);
-    zp = tclamp(trint(tdiv<T>(-mn, scale)), qmin, qmax);
+    zp = tclamp_t<T>(trint(tdiv<T>(-mn, scale)), qmin, qmax);
   }
 }
 

@@ -81,10 +81,10 @@ __device__ __forceinline__ float apply_q(float v, float scale, float zp, float q
   float t = tdiv<T>(v, scale);
   if (!zp0) t = tadd<T>(t, zp);
   if constexpr (MODE == MODE_FAKE) {
-    float q = tclamp(tste(t), qmin, qmax);
+    float q = tclamp_t<T>(tste(t), qmin, qmax);
     return tmul<T>(zp0 ? q : tsub<T>(q, zp), scale);
   } else {
-    return tclamp(trint(t), qmin, qmax);
+    return tclamp_t<T>(trint(t), qmin, qmax);
   }
 }
 
@@ -471,8 +471,8 @@ __global__ void __launch_bounds__(256) fq_backward_kernel(const T* __restrict__ 
       }
       const float t = tadd<T>(tdiv<T>(v, s), zp);
       const float q = tste(t);
-      const bool m = (q >= a.qmin) && (q <= a.qmax);
-      const float c = tclamp(q, a.qmin, a.qmax);
+      const bool m = (q >= Ty<T>::round(a.qmin)) && (q <= Ty<T>::round(a.qmax));
+      const float c = tclamp_t<T>(q, a.qmin, a.qmax);
       s1 += tmul<T>(gv, tsub<T>(c, zp));
       const float du = m ? tmul<T>(gv, s) : 0.0f;
       s2 += tmul<T>(-du, tdiv<T>(tdiv<T>(v, s), s));
@@ -512,7 +512,7 @@ __global__ void __launch_bounds__(256) fq_backward_kernel(const T* __restrict__ 
       const float gv = Ty<T>::to_f(gb[e]);
       const float t = tadd<T>(tdiv<T>(v, s), zp);
       const float q = tste(t);
-      const bool m = (q >= a.qmin) && (q <= a.qmax);
+      const bool m = (q >= Ty<T>::round(a.qmin)) && (q <= Ty<T>::round(a.qmax));
       float d = m ? tdiv<T>(tmul<T>(gv, s), s) : 0.0f;
       if (a.sym) {
         if (fabsf(v) == r.mx) d = tadd<T>(d, tmul<T>(dmax, v > 0.f ? 1.f : (v < 0.f ? -1.f : 0.f)));

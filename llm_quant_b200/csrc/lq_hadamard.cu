@@ -127,7 +127,7 @@ __device__ __forceinline__ void fake_quant_vals(float* v, const FhtArgs& a, floa
     }
     // symmetric: zp is +0.0 and both zero-point ops are exact no-ops here
     const float t = a.sym ? qv : tadd<T>(qv, zp);
-    const float q = tclamp(tste(t), a.qmin, a.qmax);
+    const float q = tclamp_t<T>(tste(t), a.qmin, a.qmax);
     v[i] = tmul<T>(a.sym ? q : tsub<T>(q, zp), scale);
   }
 }
@@ -245,6 +245,247 @@ __global__ void __launch_bounds__(1024) fht_block_kernel(const T* __restrict__ x
   }
 }
 
+// ---------------------------------------------------------------------------
+// d = 2^L, L in {11, 12, 13}: one block of NT = d/32 threads per row, 32
+// elements per thread held as 16 float2 (elements 2j, 2j+1 = "pair" j), in
+// three register phases joined by two shared-memory transposes:
+//   phase 1  thread t holds pairs 16t..16t+15 (elements 32t..32t+31, read
+//            from global memory): stage of element bit 0 inside each float2,
+//            then pair bits 0..3;
+//   phase 2  thread t holds pairs (t % 16) + 16k + 256(t / 16), k = 0..15:
+//            pair bits 4..7;
+//   phase 3  thread t holds pairs f + NF t + 256 k3 (NF = 2^(13-L) "filler"
+//            values f, k3 over the remaining pair bits 8..L-2): those bits,
+//            then the row is finished in registers and stored, NF pairs
+//            (2 NF contiguous elements) per store.
+// Stages run in the order of the element bits (0, 1, ..., L-1) like the
+// other kernels; between float2 registers they are packed f32x2 operations
+// (a + b, and a - b as the exact fma(b, -1, a)).  Shared-memory layout: pair
+// j at float2 slot j + j/16 (one pad slot per 16), which keeps the 16 lanes
+// of every 64-bit access of all three phases on distinct banks.
+//
+// Fused fake quantization, bf16: the row's values y = round_bf16(acc *
+// entry) are kept as bf16x2 words.  When the scale lies in [2^-126, 2^126]
+// and every |t| (quotient plus zero point) is below 63, each pair is
+//   t = round_bf16(y * rcp_rn(scale)) (+ zp),  q = (t + 192) - 192,
+//   q = clamp(q, qmin, qmax) (- zp),  out = round_bf16(q * scale)
+// in bf16x2 arithmetic: t + 192 lands in [128, 256) where the bf16 spacing
+// is 1, so the pair of adds is round-half-even to an integer with a zero
+// result of +0, which is what ste_round gives for finite t; the sums,
+// differences and products of these small integers and bf16 values are exact
+// before their one rounding.  Other rows, and fp16 / fp32, use the scalar
+// fake_quant_vals.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void bfly2(float2& a, float2& b) {
+  const float2 s = __fadd2_rn(a, b);
+  b = __ffma2_rn(b, make_float2(-1.0f, -1.0f), a);
+  a = s;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ __nv_bfloat162 as_bf2(uint32_t u) { return *reinterpret_cast<__nv_bfloat162*>(&u); }
+__device__ __forceinline__ uint32_t as_u32(__nv_bfloat162 h) { return *reinterpret_cast<uint32_t*>(&h); }
+
+// Store NW 32-bit words (NW in {1, 2, 4}) at dst (aligned to 4 NW bytes).
+template <int NW>
+__device__ __forceinline__ void store_words(void* dst, const uint32_t* w) {
+  if constexpr (NW == 1) *reinterpret_cast<uint32_t*>(dst) = w[0];
+  else if constexpr (NW == 2) *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+  else st_v4(dst, make_uint4(w[0], w[1], w[2], w[3]));
+}
+
+// Store NF consecutive float2 (2 NF elements, rounded to T) at dst.
+template <typename T, int NF>
+__device__ __forceinline__ void store_pairs(T* dst, const float2* v) {
+  if constexpr (sizeof(T) == 4) {
+    if constexpr (NF == 1) {
+      *reinterpret_cast<float2*>(dst) = v[0];
+    } else {
+#pragma unroll
+      for (int f = 0; f < NF; f += 2)
+        st_v4(dst + 2 * f, make_uint4(__float_as_uint(v[f].x), __float_as_uint(v[f].y),
+                                      __float_as_uint(v[f + 1].x), __float_as_uint(v[f + 1].y)));
+    }
+  } else {
+    uint32_t w[NF];
+#pragma unroll
+    for (int f = 0; f < NF; ++f)
+      w[f] = Ty<T>::code == LQ_BF16 ? pack_bf16x2(v[f].x, v[f].y) : pack_f16x2(v[f].x, v[f].y);
+    store_words<NF>(dst, w);
+  }
+}
+
+template <typename T, int L, bool QUANT>
+__global__ void __launch_bounds__((1 << L) / 32) fht3_kernel(const T* __restrict__ x, FhtArgs a,
+                                                            T* __restrict__ out,
+                                                            T* __restrict__ scale_out,
+                                                            T* __restrict__ zp_out) {
+  constexpr int D = 1 << L, NT = D / 32, C3 = L - 9, NF = 1 << (4 - C3), NK3 = 1 << C3;
+  constexpr bool kBf16 = Ty<T>::code == LQ_BF16;
+  __shared__ float2 sm[(D / 2) + (D / 32)];
+  __shared__ MinMax red[NT / 32];
+  const int t = threadIdx.x, lane = t & 31;
+  const int base2 = (t & 15) + 272 * (t >> 4);
+  const int base3 = NF * t + ((NF * t) >> 4);
+  for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+    float2 v[16];
+    {  // phase 1
+      const T* src = x + row * D + (int64_t)t * 32;
+      constexpr int V = 16 / sizeof(T);
+#pragma unroll
+      for (int k = 0; k < 32 / V; ++k) {
+        Vec16<T> u;
+        u.u = ld_nc_v4(src + k * V);
+#pragma unroll
+        for (int i = 0; i < V; i += 2)
+          v[(k * V + i) / 2] = make_float2(Ty<T>::to_f(u.v[i]), Ty<T>::to_f(u.v[i + 1]));
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < 16; ++m) {
+      const float p = v[m].x, q = v[m].y;
+      v[m] = make_float2(__fadd_rn(p, q), __fsub_rn(p, q));
+    }
+#pragma unroll
+    for (int h = 1; h < 16; h <<= 1)
+#pragma unroll
+      for (int m = 0; m < 16; ++m)
+        if ((m & h) == 0) bfly2(v[m], v[m + h]);
+    __syncthreads();  // the previous row's phase-3 reads are done
+#pragma unroll
+    for (int m = 0; m < 16; ++m) sm[17 * t + m] = v[m];
+    __syncthreads();
+    // phase 2
+#pragma unroll
+    for (int k = 0; k < 16; ++k) v[k] = sm[base2 + 17 * k];
+#pragma unroll
+    for (int h = 1; h < 16; h <<= 1)
+#pragma unroll
+      for (int k = 0; k < 16; ++k)
+        if ((k & h) == 0) bfly2(v[k], v[k + h]);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) sm[base2 + 17 * k] = v[k];
+    __syncthreads();
+    // phase 3: register r = f + NF * k3
+#pragma unroll
+    for (int k3 = 0; k3 < NK3; ++k3)
+#pragma unroll
+      for (int f = 0; f < NF; ++f) v[f + NF * k3] = sm[base3 + f + 272 * k3];
+#pragma unroll
+    for (int h = NF; h < 16; h <<= 1)
+#pragma unroll
+      for (int r = 0; r < 16; ++r)
+        if ((r & h) == 0) bfly2(v[r], v[r + h]);
+    // finish: y = round_T(acc * entry)
+    const float2 e2 = make_float2(a.entry, a.entry);
+#pragma unroll
+    for (int r = 0; r < 16; ++r) v[r] = __fmul2_rn(v[r], e2);
+    T* dst = out + row * D + 2 * NF * (int64_t)t;
+    if constexpr (!QUANT) {
+#pragma unroll
+      for (int k3 = 0; k3 < NK3; ++k3) store_pairs<T, NF>(dst + 512 * k3, v + NF * k3);
+    } else if constexpr (kBf16) {
+      uint32_t y[16];
+#pragma unroll
+      for (int r = 0; r < 16; ++r) y[r] = pack_bf16x2(v[r].x, v[r].y);
+      MinMax mm;
+      mm.init();
+      if (a.sym) {
+        uint32_t m2 = 0;
+#pragma unroll
+        for (int r = 0; r < 16; r += 2) m2 = __vimax3_u16x2(m2, y[r] & 0x7FFF7FFFu, y[r + 1] & 0x7FFF7FFFu);
+        mm.mx = __uint_as_float(max(m2 & 0xFFFFu, m2 >> 16) << 16);
+      } else {
+        __nv_bfloat162 lo2 = as_bf2(y[0]), hi2 = lo2;
+#pragma unroll
+        for (int r = 1; r < 16; ++r) {
+          lo2 = __hmin2_nan(lo2, as_bf2(y[r]));
+          hi2 = __hmax2_nan(hi2, as_bf2(y[r]));
+        }
+        mm.mn = fmin_nan(__low2float(lo2), __high2float(lo2));
+        mm.mx = fmax_nan(__low2float(hi2), __high2float(hi2));
+      }
+      for (int s = 16; s >= 1; s >>= 1) mm.shfl_xor_merge(s, a.sym);
+      if (lane == 0) red[t >> 5] = mm;
+      __syncthreads();
+      MinMax tot = red[0];
+#pragma unroll
+      for (int i = 1; i < NT / 32; ++i) tot.merge(red[i]);
+      float scale, zp;
+      qparams_from<T>(tot, a.sym, a.qmin, a.qmax, a.lo, scale, zp);
+      if (t == 0 && scale_out) {
+        scale_out[row] = Ty<T>::from_f(scale);
+        zp_out[row] = Ty<T>::from_f(zp);
+      }
+      const float rcp = __frcp_rn(scale);
+      const float bound = a.sym ? tot.mx * rcp : fmaxf(fabsf(tot.mn), fabsf(tot.mx)) * rcp + fabsf(zp);
+      const bool fast = scale >= 0x1p-126f && scale <= 0x1p126f && bound < 63.0f;
+      uint32_t o[16];
+      if (fast) {
+        const float2 r2 = make_float2(rcp, rcp);
+        const __nv_bfloat162 magic = __float2bfloat162_rn(192.0f);
+        const __nv_bfloat162 qlo = __float2bfloat162_rn(a.qmin), qhi = __float2bfloat162_rn(a.qmax);
+        const __nv_bfloat162 z2 = __float2bfloat162_rn(zp), s2 = __float2bfloat162_rn(scale);
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+          const float2 p = __fmul2_rn(make_float2(__uint_as_float(y[r] << 16), __uint_as_float(y[r] & 0xFFFF0000u)), r2);
+          __nv_bfloat162 q = as_bf2(pack_bf16x2(p.x, p.y));
+          if (!a.sym) q = __hadd2(q, z2);
+          q = __hsub2(__hadd2(q, magic), magic);
+          q = __hmin2(__hmax2(q, qlo), qhi);
+          if (!a.sym) q = __hsub2(q, z2);
+          o[r] = as_u32(__hmul2(q, s2));
+        }
+      } else {
+        float f[32];
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+          f[2 * r] = __uint_as_float(y[r] << 16);
+          f[2 * r + 1] = __uint_as_float(y[r] & 0xFFFF0000u);
+        }
+        fake_quant_vals<T, 32>(f, a, scale, zp);
+#pragma unroll
+        for (int r = 0; r < 16; ++r) o[r] = pack_bf16x2(f[2 * r], f[2 * r + 1]);
+      }
+#pragma unroll
+      for (int k3 = 0; k3 < NK3; ++k3) store_words<NF>(dst + 512 * k3, o + NF * k3);
+    } else {
+      float* f = reinterpret_cast<float*>(v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) f[i] = Ty<T>::round(f[i]);
+      MinMax mm;
+      mm.init();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        if (a.sym) mm.add_max(fabsf(f[i]));
+        else mm.add(f[i]);
+      }
+      for (int s = 16; s >= 1; s >>= 1) mm.shfl_xor_merge(s, a.sym);
+      if (lane == 0) red[t >> 5] = mm;
+      __syncthreads();
+      MinMax tot = red[0];
+#pragma unroll
+      for (int i = 1; i < NT / 32; ++i) tot.merge(red[i]);
+      float scale, zp;
+      qparams_from<T>(tot, a.sym, a.qmin, a.qmax, a.lo, scale, zp);
+      if (t == 0 && scale_out) {
+        scale_out[row] = Ty<T>::from_f(scale);
+        zp_out[row] = Ty<T>::from_f(zp);
+      }
+      fake_quant_vals<T, 32>(f, a, scale, zp);
+#pragma unroll
+      for (int k3 = 0; k3 < NK3; ++k3) store_pairs<T, NF>(dst + 512 * k3, v + NF * k3);
+    }
+  }
+}
+
 template <typename T> float entry_of(int d) {
   float c = 1.0f / (float)sqrt((double)d);
   if (Ty<T>::code == LQ_BF16) return __bfloat162float(__float2bfloat16_rn(c));
@@ -278,6 +519,17 @@ int fht_launch(const T* x, FhtArgs a, T* out, T* s, T* z, cudaStream_t st) {
       default: set_error("internal: bad E %d", E); return LQ_EINVAL;
     }
     return launched("fht_warp_kernel");
+  }
+  if ((d == 2048 || d == 4096 || d == 8192) && aligned16(x) && aligned16(out)) {
+    void (*k3)(const T*, FhtArgs, T*, T*, T*) =
+        d == 2048 ? fht3_kernel<T, 11, QUANT> : (d == 4096 ? fht3_kernel<T, 12, QUANT> : fht3_kernel<T, 13, QUANT>);
+    int per_sm = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k3, d / 32, 0);
+    LQ_REQUIRE(e == cudaSuccess && per_sm > 0, LQ_ECUDA, "occupancy query: %s", cudaGetErrorString(e));
+    const int64_t cap = (int64_t)num_sms() * per_sm;
+    const int grid = (int)(a.rows < cap ? a.rows : cap);
+    k3<<<grid, d / 32, 0, st>>>(x, a, out, s, z);
+    return launched("fht3_kernel");
   }
   int E = (d <= 8192) ? 16 : 32;
   int NT = d / E;

@@ -158,7 +158,7 @@ __global__ void __launch_bounds__(256) token_group_kernel(const T* __restrict__ 
           } ov;
 #pragma unroll
           for (int i = 0; i < V; ++i) {
-            float q = tclamp(trint(tadd<T>(tdiv<T>(v[i], sc[i]), zz[i])), a.qmin, a.qmax);
+            float q = tclamp_t<T>(trint(tadd<T>(tdiv<T>(v[i], sc[i]), zz[i])), a.qmin, a.qmax);
             if constexpr (MODE == 1) {
               // KVCacheQuantizer.fake_quantize: codes are cast to intN first
               // (NaN -> 0), then (q.float() - zp) * scale in fp32.
@@ -294,73 +294,96 @@ __global__ void __launch_bounds__(256) kv_dequant_kernel(const CT* __restrict__ 
   }
 }
 
-// Vector path: thread = 16 consecutive elements of one token row (16 codes
-// in one load, 64 bytes of fp32 out); needs D % 16 == 0 and aligned buffers.
-// float(q) is formed exactly as (1.5 * 2^23 + q) - 1.5 * 2^23.
+// Segment path (D % 4 == 0): a warp takes 512 consecutive elements of one
+// (p) slice -- T*D elements, contiguous in the output and in the code buffer
+// -- and lane l the 4-element chunks 4l + 128k, k = 0..3, so every load and
+// store instruction of the warp covers one contiguous span (128 or 256 bytes
+// of codes, 512 bytes of fp32).  float(q) is formed exactly as
+// (1.5 * 2^23 + q) - 1.5 * 2^23.
+template <typename CT> struct Codes4;
+template <> struct Codes4<int8_t> {
+  using W = uint32_t;
+  __device__ __forceinline__ static int get(W w, int i) { return (int)(int8_t)(w >> (8 * i)); }
+};
+template <> struct Codes4<int16_t> {
+  using W = uint2;
+  __device__ __forceinline__ static int get(W w, int i) {
+    return (int)(int16_t)((i < 2 ? w.x : w.y) >> (16 * (i & 1)));
+  }
+};
+
 template <typename CT, typename ST>
-__global__ void __launch_bounds__(256) kv_dequant16_kernel(const CT* __restrict__ codes, DqArgs a,
-                                                           const ST* __restrict__ scale,
-                                                           const ST* __restrict__ zp,
-                                                           float* __restrict__ out) {
-  const int64_t per_row = a.D / 16;
-  const int64_t total = a.P * a.T * per_row;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / per_row;  // (p, t)
-    const int c = (int)(i - r * per_row) * 16;
-    const int64_t p = r / a.T, t = r - p * a.T;
-    const CT* q = codes + (p * a.cpitch + t) * a.D + c;
-    int qv[16];
-    if constexpr (sizeof(CT) == 1) {
-      const uint4 w = *reinterpret_cast<const uint4*>(q);
-      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+__global__ void __launch_bounds__(256) kv_dequant_seg_kernel(const CT* __restrict__ codes, DqArgs a,
+                                                             const ST* __restrict__ scale,
+                                                             const ST* __restrict__ zp,
+                                                             float* __restrict__ out,
+                                                             int64_t segs_per_p, int d_shift) {
+  using W = typename Codes4<CT>::W;
+  const int lane = threadIdx.x & 31;
+  const int64_t slice = a.T * a.D;
+  const int64_t nseg = a.P * segs_per_p;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t g = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; g < nseg; g += warps) {
+    const int64_t p = g / segs_per_p;
+    const int64_t e0 = (g - p * segs_per_p) * 512 + 4 * lane;
+    const CT* qp = codes + p * a.cpitch * a.D;
+    float* op = out + p * slice;
+    W w[4];
 #pragma unroll
-      for (int k = 0; k < 16; ++k) qv[k] = (int)(int8_t)(ws[k >> 2] >> (8 * (k & 3)));
-    } else {
-      const uint4 w0 = reinterpret_cast<const uint4*>(q)[0], w1 = reinterpret_cast<const uint4*>(q)[1];
-      const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-#pragma unroll
-      for (int k = 0; k < 16; ++k) qv[k] = (int)(int16_t)(ws[k >> 1] >> (16 * (k & 1)));
+    for (int k = 0; k < 4; ++k) {
+      const int64_t e = e0 + 128 * k;
+      if (e < slice) w[k] = *reinterpret_cast<const W*>(qp + e);
     }
-    float sv[16], zv[16];
-    if (a.gran == 0) {
-      const int64_t si = p * a.szpitch + t;
-      const float s0 = Ty<ST>::to_f(scale[si]), z0 = Ty<ST>::to_f(zp[si]);
 #pragma unroll
-      for (int k = 0; k < 16; ++k) { sv[k] = s0; zv[k] = z0; }
-    } else {
-      const int64_t base = (a.gran == 1) ? p * a.D + c : (p * a.szpitch + t / a.S) * a.D + c;
+    for (int k = 0; k < 4; ++k) {
+      const int64_t e = e0 + 128 * k;
+      if (e >= slice) break;
+      const int64_t t = d_shift >= 0 ? (e >> d_shift) : e / a.D;
+      const int64_t c = e - t * a.D;
+      float sv[4], zv[4];
+      if (a.gran == 0) {
+        const int64_t si = p * a.szpitch + t;
+        const float s0 = Ty<ST>::to_f(scale[si]), z0 = Ty<ST>::to_f(zp[si]);
 #pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        sv[k] = Ty<ST>::to_f(scale[base + k]);
-        zv[k] = Ty<ST>::to_f(zp[base + k]);
+        for (int i = 0; i < 4; ++i) { sv[i] = s0; zv[i] = z0; }
+      } else {
+        const int64_t base = (a.gran == 1) ? p * a.D + c : (p * a.szpitch + t / a.S) * a.D + c;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          sv[i] = Ty<ST>::to_f(scale[base + i]);
+          zv[i] = Ty<ST>::to_f(zp[base + i]);
+        }
       }
-    }
-    float o[16];
+      float o[4];
 #pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      const float qf = __fsub_rn(__int_as_float(0x4B400000 + qv[k]), 12582912.0f);
-      o[k] = __fmul_rn(__fsub_rn(qf, zv[k]), sv[k]);
+      for (int i = 0; i < 4; ++i) {
+        const float qf = __fsub_rn(__int_as_float(0x4B400000 + Codes4<CT>::get(w[k], i)), 12582912.0f);
+        o[i] = __fmul_rn(__fsub_rn(qf, zv[i]), sv[i]);
+      }
+      st_v4(op + e, make_uint4(__float_as_uint(o[0]), __float_as_uint(o[1]), __float_as_uint(o[2]),
+                               __float_as_uint(o[3])));
     }
-    float* dst = out + r * a.D + c;
-#pragma unroll
-    for (int k = 0; k < 4; ++k)
-      st_v4(dst + 4 * k, make_uint4(__float_as_uint(o[4 * k]), __float_as_uint(o[4 * k + 1]),
-                                    __float_as_uint(o[4 * k + 2]), __float_as_uint(o[4 * k + 3])));
   }
 }
 
 template <typename CT, typename ST>
 int kv_dequant_t(const void* codes, const DqArgs& a, const void* s, const void* z, float* out,
                  cudaStream_t st) {
-  if (a.D % 16 == 0 && aligned16(out) && aligned16(codes)) {
-    const int64_t total = a.P * a.T * (a.D / 16);
-    int64_t want = (total + 255) / 256;
-    int grid = (int)(want < (int64_t)num_sms() * 16 ? (want > 0 ? want : 1) : (int64_t)num_sms() * 16);
-    kv_dequant16_kernel<CT, ST><<<grid, 256, 0, st>>>(static_cast<const CT*>(codes), a,
-                                                      static_cast<const ST*>(s),
-                                                      static_cast<const ST*>(z), out);
-    return launched("kv_dequant16_kernel");
+  if (a.D % 4 == 0 && aligned16(out) && reinterpret_cast<uintptr_t>(codes) % (4 * sizeof(CT)) == 0) {
+    const int64_t segs_per_p = (a.T * a.D + 511) / 512;
+    const int64_t warps_needed = a.P * segs_per_p;
+    const int64_t want = (warps_needed + 7) / 8;
+    const int grid = (int)(want < (int64_t)num_sms() * 8 ? (want > 0 ? want : 1) : (int64_t)num_sms() * 8);
+    int d_shift = -1;
+    if ((a.D & (a.D - 1)) == 0) {
+      d_shift = 0;
+      while ((int64_t(1) << d_shift) < a.D) ++d_shift;
+    }
+    kv_dequant_seg_kernel<CT, ST><<<grid, 256, 0, st>>>(static_cast<const CT*>(codes), a,
+                                                        static_cast<const ST*>(s),
+                                                        static_cast<const ST*>(z), out, segs_per_p,
+                                                        d_shift);
+    return launched("kv_dequant_seg_kernel");
   }
   int vec4 = (a.D % 4 == 0) && aligned16(out) &&
              (reinterpret_cast<uintptr_t>(codes) % (4 * sizeof(CT)) == 0);

@@ -93,7 +93,8 @@ __device__ __forceinline__ float nf4_quotient(float x, float scale, float rcp) {
 struct NfArgs {
   int64_t n, G, DG, n_groups, n_super;
   float lo;
-  int g_shift;  // log2(G) when G is a power of two, else -1
+  int g_shift;   // log2(G) when G is a power of two, else -1
+  int dg_shift;  // log2(DG) when DG is a power of two, else -1
 };
 
 inline int log2_exact(int64_t v) {
@@ -378,6 +379,125 @@ __global__ void __launch_bounds__(256) nf4_pack_bf16_kernel(const __nv_bfloat16*
   }
 }
 
+// bf16 input, G = 64, packed codes, n % 64 == 0 (the QLoRA default): one
+// thread per group, so the absmax, the reciprocal and the group's 32 code
+// bytes stay in one thread, and a 256-thread block covers exactly one
+// double-quantization super-group of DG = 256 scales.
+//   bucket: f = fmaf(p, 4096, 1.5*2^23 + 4608) holds rint(4096 p) + 4608 in
+//           its low mantissa bits, so bits(f) & 0x3F80 = 128 k with bucket
+//           k = (rint(4096 p) + 4608) >> 7 in [4, 68] for p in [-1, 1]
+//           (width 1/32, at most one threshold inside);
+//   table:  16 copies of the 128-entry (threshold, code) table, entry k of
+//           copy r at byte 128 k + 8 r; lane l reads copy l % 16, so the 16
+//           lanes of a half-warp never share a bank: the byte offset of an
+//           element's entry is one LOP3, (bits(f) & 0x3F80) | 8 (l % 16).
+constexpr int kG64Rep = 16;
+constexpr float kG64Magic = 12582912.0f + 4608.0f;
+
+// Bucket k holds the quotients with rint(4096 p) in [128 k - 4608,
+// 128 k - 4481], i.e. p in [(256 k - 9217) / 8192, (256 k - 8961) / 8192].
+__device__ __forceinline__ void build_lut_g64(int2* lut) {
+  for (int k = threadIdx.x; k < 128; k += blockDim.x) {
+    const float left = (float)(256 * k - 9217) / 8192.0f, right = (float)(256 * k - 8961) / 8192.0f;
+    int code = 0;
+    float th = __int_as_float(0x7f800000);
+    for (int i = 0; i < 15; ++i) {
+      const float t = kTheta[ThetaRow<__nv_bfloat16>::row][i];
+      code += (t <= left);
+      if (t > left && t <= right) th = t;
+    }
+    const int2 e = make_int2(__float_as_int(th), code);
+#pragma unroll
+    for (int r = 0; r < kG64Rep; ++r) lut[k * kG64Rep + r] = e;
+  }
+}
+
+// Codes of the 64 elements in w (element 8k + i at bits 4i of out[k]).
+// CHECK: the scale is not finite, so quotients may be NaN (code 0).
+template <bool CHECK>
+__device__ __forceinline__ void nf4_encode_g64(const uint4 (&w)[8], float rcp, const char* lutb,
+                                               uint32_t rep, uint32_t (&out)[8]) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const uint32_t ws[4] = {w[k].x, w[k].y, w[k].z, w[k].w};
+    uint32_t acc = 0;
+#pragma unroll
+    for (int j = 3; j >= 0; --j) {
+#pragma unroll
+      for (int h = 1; h >= 0; --h) {
+        const float x = __uint_as_float(h ? (ws[j] & 0xFFFF0000u) : (ws[j] << 16));
+        const float p = __fmul_rn(x, rcp);
+        const float f = fmaf(p, 4096.0f, kG64Magic);
+        const int2 e = *reinterpret_cast<const int2*>(lutb + ((__float_as_uint(f) & 0x3F80u) | rep));
+        int c = e.y + (p >= __int_as_float(e.x) ? 1 : 0);
+        if (CHECK) c = (p == p) ? c : 0;
+        acc = acc * 16u + (uint32_t)c;
+      }
+    }
+    out[k] = acc;
+  }
+}
+
+template <bool DQ>
+__global__ void __launch_bounds__(256, 3) nf4_pack_g64_kernel(const uint4* __restrict__ x,
+                                                              int64_t n_groups, int64_t n_super,
+                                                              float lo, uint4* __restrict__ codes,
+                                                              __nv_bfloat16* __restrict__ scales,
+                                                              __nv_bfloat16* __restrict__ q_scales,
+                                                              __nv_bfloat16* __restrict__ dq_scales) {
+  using T = __nv_bfloat16;
+  __shared__ __align__(16) int2 lut[128 * kG64Rep];
+  __shared__ uint32_t red[8];
+  build_lut_g64(lut);
+  __syncthreads();
+  const char* lutb = reinterpret_cast<const char*>(lut);
+  const uint32_t rep = (threadIdx.x & 15) * 8;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int64_t sg = blockIdx.x; sg < n_super; sg += gridDim.x) {
+    const int64_t g = sg * 256 + threadIdx.x;
+    const bool live = g < n_groups;
+    uint4 w[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) w[k] = live ? ld_nc_v4(x + g * 8 + k) : make_uint4(0, 0, 0, 0);
+    // |x| as unsigned bf16 pairs; the pair max keeps NaN (its pattern is above +inf)
+    uint32_t m2 = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      m2 = __vimax3_u16x2(m2, w[k].x & 0x7FFF7FFFu, w[k].y & 0x7FFF7FFFu);
+      m2 = __vimax3_u16x2(m2, w[k].z & 0x7FFF7FFFu, w[k].w & 0x7FFF7FFFu);
+    }
+    const float am = __uint_as_float(max(m2 & 0xFFFFu, m2 >> 16) << 16);
+    const float s = (am < lo) ? lo : am;  // clamp(min=1e-12) in bf16; NaN passes
+    const float rcp = __frcp_rn(s);
+    uint32_t out[8];
+    if (s <= 3.40282347e38f) nf4_encode_g64<false>(w, rcp, lutb, rep, out);
+    else nf4_encode_g64<true>(w, rcp, lutb, rep, out);
+    if (live) {
+      scales[g] = __float2bfloat16_rn(s);
+      codes[2 * g] = make_uint4(out[0], out[1], out[2], out[3]);
+      codes[2 * g + 1] = make_uint4(out[4], out[5], out[6], out[7]);
+    }
+    if constexpr (DQ) {
+      // absmax of the super-group's scales (s >= 0 or +NaN: integer order is float order)
+      const uint32_t mb = __reduce_max_sync(0xffffffffu, live ? __float_as_uint(s) : 0u);
+      if (lane == 0) red[warp] = mb;
+      __syncthreads();
+      uint32_t tot = red[0];
+#pragma unroll
+      for (int i = 1; i < 8; ++i) tot = max(tot, red[i]);
+      __syncthreads();
+      float dq = __uint_as_float(tot);
+      dq = (dq < lo) ? lo : dq;
+      if (threadIdx.x == 0) dq_scales[sg] = __float2bfloat16_rn(dq);
+      if (live) {
+        const float sn = tdiv<T>(s, dq);
+        const float q = tclamp(trint(tmul<T>(sn, 127.0f)), -127.0f, 127.0f);
+        q_scales[g] = __float2bfloat16_rn(q);
+      }
+    }
+  }
+}
+
 // Generic scalar path (any G): pass 1 writes the group scales (one block per
 // group), pass 2 writes codes for pairs of flat elements, so packed bytes are
 // always written whole even when a pair straddles two groups.
@@ -505,63 +625,81 @@ __global__ void __launch_bounds__(256) nf4_dequant_kernel(const void* __restrict
   }
 }
 
-// Vectorized dequantize of packed codes for 2-byte T: thread = 32 elements
-// (16 bytes of codes, 64 bytes of output), all in one group (G % 32 == 0).
+// Vectorized dequantize of packed codes for 2-byte T (G % 8 == 0): a chunk is
+// 8 elements (4 code bytes, 16 output bytes) inside one group, and lane l of a
+// warp takes chunks base + 32 k + l, so every load and store instruction of
+// the warp covers one contiguous span (128 bytes of codes, 512 of output).
 // pair[b] holds round_T(NF4_TABLE) of both nibbles of code byte b; the
 // product with the scale is __hmul2, whose correctly rounded result equals
 // round_T(fp32 product) because the product of two 8- or 11-bit significands
-// is exact in fp32.
+// is exact in fp32.  The 256-entry table is stored 32 times, entry b of copy
+// r at word 32 b + r, and lane l reads copy l: no bank conflicts.
+constexpr int kUnpackK = 4;  // chunks per lane per warp iteration
+
 template <typename T>
-__global__ void __launch_bounds__(256) nf4_unpack_vec_kernel(const uint4* __restrict__ codes,
+__global__ void __launch_bounds__(256) nf4_unpack_vec_kernel(const uint32_t* __restrict__ codes,
                                                              NfArgs a,
                                                              const T* __restrict__ scales,
                                                              const T* __restrict__ q_scales,
                                                              const T* __restrict__ dq_scales,
-                                                             T* __restrict__ out, int64_t nchunk) {
-  __shared__ uint32_t pair[256];
-  for (int b = threadIdx.x; b < 256; b += blockDim.x) {
+                                                             uint4* __restrict__ out, int64_t nchunk) {
+  __shared__ __align__(16) uint32_t pair[256 * 32];
+  {
+    const int b = threadIdx.x;  // blockDim.x == 256
     union {
       T h[2];
       uint32_t u;
     } pr;
     pr.h[0] = Ty<T>::from_f(Ty<T>::round(kNF4[b & 15]));
     pr.h[1] = Ty<T>::from_f(Ty<T>::round(kNF4[b >> 4]));
-    pair[b] = pr.u;
+    uint4* row = reinterpret_cast<uint4*>(pair + 32 * b);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) row[i] = make_uint4(pr.u, pr.u, pr.u, pr.u);
   }
   __syncthreads();
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nchunk;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t e0 = i * 32;
-    const int64_t g = a.g_shift >= 0 ? (e0 >> a.g_shift) : e0 / a.G;
-    float s;
-    if (q_scales) s = tmul<T>(tdiv<T>(Ty<T>::to_f(q_scales[g]), 127.0f), Ty<T>::to_f(dq_scales[g / a.DG]));
-    else s = Ty<T>::to_f(scales[g]);
-    union {
-      T h[2];
-      uint32_t u;
-    } s2;
-    s2.h[0] = s2.h[1] = Ty<T>::from_f(s);
-    const uint4 c = codes[i];
-    const uint32_t w[4] = {c.x, c.y, c.z, c.w};
-    uint32_t o[16];
+  const char* pb = reinterpret_cast<const char*>(pair);
+  const int lane = threadIdx.x & 31;
+  const uint32_t lane4 = (uint32_t)lane * 4;
+  const int c_shift = a.g_shift >= 3 ? a.g_shift - 3 : -1;  // chunk -> group
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int64_t span = 32 * kUnpackK;
+  for (int64_t base = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * span; base < nchunk;
+       base += warps * span) {
+    uint32_t w[kUnpackK];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int k = 0; k < kUnpackK; ++k) {
+      const int64_t c = base + 32 * k + lane;
+      w[k] = c < nchunk ? __ldg(codes + c) : 0u;
+    }
+#pragma unroll
+    for (int k = 0; k < kUnpackK; ++k) {
+      const int64_t c = base + 32 * k + lane;
+      if (c >= nchunk) break;
+      const int64_t g = c_shift >= 0 ? (c >> c_shift) : (c * 8) / a.G;
+      float s;
+      if (q_scales) s = tmul<T>(tdiv<T>(Ty<T>::to_f(q_scales[g]), 127.0f), Ty<T>::to_f(dq_scales[a.dg_shift >= 0 ? (g >> a.dg_shift) : g / a.DG]));
+      else s = Ty<T>::to_f(scales[g]);
+      union {
+        T h[2];
+        uint32_t u;
+      } s2;
+      s2.h[0] = s2.h[1] = Ty<T>::from_f(s);
+      uint32_t o[4];
 #pragma unroll
       for (int b = 0; b < 4; ++b) {
-        uint32_t pv = pair[(w[j] >> (8 * b)) & 255];
+        const uint32_t off = (b == 0 ? (w[k] << 7) : (w[k] >> (8 * b - 7))) & 0x7F80u;
+        uint32_t pv = *reinterpret_cast<const uint32_t*>(pb + (off | lane4));
         if constexpr (Ty<T>::code == LQ_BF16) {
           __nv_bfloat162 r = __hmul2(*reinterpret_cast<__nv_bfloat162*>(&pv),
                                      *reinterpret_cast<__nv_bfloat162*>(&s2.u));
-          o[j * 4 + b] = *reinterpret_cast<uint32_t*>(&r);
+          o[b] = *reinterpret_cast<uint32_t*>(&r);
         } else {
           __half2 r = __hmul2(*reinterpret_cast<__half2*>(&pv), *reinterpret_cast<__half2*>(&s2.u));
-          o[j * 4 + b] = *reinterpret_cast<uint32_t*>(&r);
+          o[b] = *reinterpret_cast<uint32_t*>(&r);
         }
       }
+      st_v4(out + c, make_uint4(o[0], o[1], o[2], o[3]));
     }
-    uint4* dst = reinterpret_cast<uint4*>(out + e0);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) st_v4(dst + k, make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]));
   }
 }
 
@@ -669,6 +807,13 @@ int nf4_quant_launch(const T* x, NfArgs a, void* codes, T* scales, T* qs, T* dqs
   int grid = grid_cap(a.n_super, 8);
   if constexpr (std::is_same<T, __nv_bfloat16>::value && CODE_DT == LQ_U4X2) {
     uint8_t* cp = static_cast<uint8_t*>(codes);
+    if (a.G == 64 && a.n % 64 == 0 && aligned16(codes) && (!DQ || a.DG == 256)) {
+      const int64_t n_chunks = (a.n_groups + 255) / 256;
+      nf4_pack_g64_kernel<DQ><<<grid_cap(n_chunks, 3), 256, 0, st>>>(
+          reinterpret_cast<const uint4*>(x), a.n_groups, n_chunks, a.lo, reinterpret_cast<uint4*>(cp),
+          scales, qs, dqs);
+      return launched("nf4_pack_g64_kernel");
+    }
     if (nvt == 1) nf4_pack_bf16_kernel<1, DQ><<<grid, 256, smem, st>>>(x, a, tps, cp, scales, qs, dqs);
     else if (nvt == 2) nf4_pack_bf16_kernel<2, DQ><<<grid, 256, smem, st>>>(x, a, tps, cp, scales, qs, dqs);
     else nf4_pack_bf16_kernel<4, DQ><<<grid, 256, smem, st>>>(x, a, tps, cp, scales, qs, dqs);
@@ -691,6 +836,7 @@ int nf4_quant_t(const void* x, int64_t n, int64_t G, int64_t DG, void* codes, in
   a.n_super = (a.n_groups + a.DG - 1) / a.DG;
   a.lo = lo_clamp_value<T>();
   a.g_shift = log2_exact(G);
+  a.dg_shift = log2_exact(a.DG);
   const T* xp = static_cast<const T*>(x);
   T* sp = static_cast<T*>(scales);
   if (DG > 0) {
@@ -722,19 +868,21 @@ int nf4_dequant_t(const void* codes, int cdt, int64_t n, int64_t G, int64_t DG, 
   a.n_super = 0;
   a.lo = 0;
   a.g_shift = log2_exact(G);
+  a.dg_shift = log2_exact(a.DG);
   const T* sp = static_cast<const T*>(s);
   const T* q = static_cast<const T*>(qs);
   const T* d = static_cast<const T*>(dqs);
   T* o = static_cast<T*>(out);
   int64_t done = 0;
-  if (sizeof(T) == 2 && cdt == LQ_U4X2 && G % 32 == 0 && aligned16(codes) && aligned16(out)) {
-    const int64_t nchunk = n / 32;
+  if (sizeof(T) == 2 && cdt == LQ_U4X2 && G % 8 == 0 && reinterpret_cast<uintptr_t>(codes) % 4 == 0 &&
+      aligned16(out)) {
+    const int64_t nchunk = n / 8;
     if (nchunk > 0) {
-      nf4_unpack_vec_kernel<T><<<grid_cap((nchunk + 255) / 256, 16), 256, 0, st>>>(
-          static_cast<const uint4*>(codes), a, sp, q, d, o, nchunk);
+      nf4_unpack_vec_kernel<T><<<grid_cap((nchunk + 256 * kUnpackK - 1) / (256 * kUnpackK), 6), 256, 0, st>>>(
+          static_cast<const uint32_t*>(codes), a, sp, q, d, reinterpret_cast<uint4*>(o), nchunk);
       int rc = launched("nf4_unpack_vec_kernel");
       if (rc) return rc;
-      done = nchunk * 32;
+      done = nchunk * 8;
     }
     if (done == n) return LQ_OK;
   }

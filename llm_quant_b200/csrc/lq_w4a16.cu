@@ -357,6 +357,160 @@ __global__ void __launch_bounds__(192, 1) w4a16_kernel(const __grid_constant__ C
 }
 
 // ---------------------------------------------------------------------------
+// Small M (M <= 16 tokens): the forward is a weight-streaming GEMV, bound by
+// HBM; a 128 x BT tensor-memory tile would sit mostly idle.  A block of 8
+// warps owns 16 weight rows; warp w takes the K steps w, w + 8, ... and runs
+// mma.sync.m16n8k16 (f32 accumulate) with the weights as the A operand and up
+// to 8 tokens per B tile.  The A fragment of a lane is (rows g, g+8) x (k
+// pairs 2c, 2c+8) of each 16-wide k tile (g = lane / 4, c = lane % 4), which
+// in the packed layout are nibbles (c, c+4) of words 2t and 2t+1 of its two
+// rows: one shift, one LOP3 with the magic exponent and one subtraction of
+// (magic + zero) give (q - zero) exactly in T.  The scale of the row's group
+// multiplies each K step's partial sums (sum_k (q - zero) * x) in fp32, so
+// the weights enter the MMA exactly; the eight warps' partial sums are added
+// in shared memory.
+// ---------------------------------------------------------------------------
+template <typename T> struct MmaOp;
+template <> struct MmaOp<__half> {
+  __device__ __forceinline__ static void mma(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+  __device__ __forceinline__ static uint32_t sub2(uint32_t v, uint32_t z) {
+    __half2 h = __hsub2(*reinterpret_cast<__half2*>(&v), *reinterpret_cast<__half2*>(&z));
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __device__ __forceinline__ static float hi_f(uint32_t pair) {
+    return __half2float(__ushort_as_half((unsigned short)(pair >> 16)));
+  }
+};
+template <> struct MmaOp<__nv_bfloat16> {
+  __device__ __forceinline__ static void mma(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+  __device__ __forceinline__ static uint32_t sub2(uint32_t v, uint32_t z) {
+    __nv_bfloat162 h = __hsub2(*reinterpret_cast<__nv_bfloat162*>(&v), *reinterpret_cast<__nv_bfloat162*>(&z));
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __device__ __forceinline__ static float hi_f(uint32_t pair) { return __uint_as_float(pair & 0xFFFF0000u); }
+};
+
+template <typename T, int NT8>
+__global__ void __launch_bounds__(256) w4a16_gemv_kernel(const T* __restrict__ x,
+                                                         const uint8_t* __restrict__ packed,
+                                                         const float* __restrict__ bias,
+                                                         T* __restrict__ y, W4Args a) {
+  __shared__ float red[8][NT8][32][4];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int r0 = blockIdx.x * 16;          // first weight row of the block
+  const int nt = r0 / kRows, rit = r0 % kRows + g;  // tile, row of lane in the tile
+  const uint8_t* wt = packed + (size_t)nt * a.n_kb * kWStage;
+  const uint32_t* pr = reinterpret_cast<const uint32_t*>(packed + (size_t)a.N * a.K / 2) +
+                       (size_t)nt * a.n_groups * kRows;
+  const uint16_t* xs = reinterpret_cast<const uint16_t*>(x);
+  float acc[NT8][4];
+#pragma unroll
+  for (int j = 0; j < NT8; ++j)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[j][i] = 0.0f;
+  // token rows of this lane's B fragments (0 beyond M)
+  int64_t xrow[NT8];
+  bool xlive[NT8];
+#pragma unroll
+  for (int j = 0; j < NT8; ++j) {
+    const int tok = 8 * j + g;
+    xlive[j] = tok < a.M;
+    xrow[j] = (int64_t)(xlive[j] ? tok : 0) * a.K;
+  }
+  for (int kb = warp; kb < a.n_kb; kb += 8) {
+    const uint4* src = reinterpret_cast<const uint4*>(wt + (size_t)kb * kWStage + rit * 32);
+    const uint4 w0 = __ldg(src), w1 = __ldg(src + 1);              // row g
+    const uint4 w2 = __ldg(src + 16), w3 = __ldg(src + 17);        // row g + 8
+    const int grp = (kb * kBK) / a.group;
+    const uint32_t zs0 = __ldg(pr + (size_t)grp * kRows + rit);
+    const uint32_t zs1 = __ldg(pr + (size_t)grp * kRows + rit + 8);
+    const uint32_t zb0 = __byte_perm(zs0, zs0, 0x1010), zb1 = __byte_perm(zs1, zs1, 0x1010);
+    const uint32_t ra[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    const uint32_t rb[8] = {w2.x, w2.y, w2.z, w2.w, w3.x, w3.y, w3.z, w3.w};
+    float part[NT8][4];
+#pragma unroll
+    for (int j = 0; j < NT8; ++j)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) part[j][i] = 0.0f;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      uint32_t af[4];
+      af[0] = MmaOp<T>::sub2(((ra[2 * t] >> (4 * c)) & 0x000F000Fu) | Act<T>::magic, zb0);
+      af[1] = MmaOp<T>::sub2(((rb[2 * t] >> (4 * c)) & 0x000F000Fu) | Act<T>::magic, zb1);
+      af[2] = MmaOp<T>::sub2(((ra[2 * t + 1] >> (4 * c)) & 0x000F000Fu) | Act<T>::magic, zb0);
+      af[3] = MmaOp<T>::sub2(((rb[2 * t + 1] >> (4 * c)) & 0x000F000Fu) | Act<T>::magic, zb1);
+      const int k = kb * kBK + 16 * t + 2 * c;
+#pragma unroll
+      for (int j = 0; j < NT8; ++j) {
+        const uint32_t b0 = xlive[j] ? __ldg(reinterpret_cast<const uint32_t*>(xs + xrow[j] + k)) : 0u;
+        const uint32_t b1 = xlive[j] ? __ldg(reinterpret_cast<const uint32_t*>(xs + xrow[j] + k + 8)) : 0u;
+        MmaOp<T>::mma(part[j], af, b0, b1);
+      }
+    }
+    // scales of rows g and g + 8 (high halves of the pairs)
+    const float s0 = MmaOp<T>::hi_f(zs0), s1 = MmaOp<T>::hi_f(zs1);
+#pragma unroll
+    for (int j = 0; j < NT8; ++j) {
+      acc[j][0] = fmaf(part[j][0], s0, acc[j][0]);
+      acc[j][1] = fmaf(part[j][1], s0, acc[j][1]);
+      acc[j][2] = fmaf(part[j][2], s1, acc[j][2]);
+      acc[j][3] = fmaf(part[j][3], s1, acc[j][3]);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < NT8; ++j)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) red[warp][j][lane][i] = acc[j][i];
+  __syncthreads();
+  // thread -> (j, lane, i) of the fragment; 32 * 4 * NT8 <= 256 outputs
+  if (threadIdx.x < 32 * 4 * NT8) {
+    const int i = threadIdx.x & 3, ln = (threadIdx.x >> 2) & 31, j = threadIdx.x >> 7;
+    float s = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) s += red[w][j][ln][i];
+    const int row = r0 + (ln >> 2) + (i >= 2 ? 8 : 0);
+    const int tok = 8 * j + 2 * (ln & 3) + (i & 1);
+    if (tok < a.M) {
+      if (bias) s = __fadd_rn(s, bias[row]);
+      y[(size_t)tok * a.N + row] = Ty<T>::from_f(s);
+    }
+  }
+}
+
+template <typename T>
+int launch_gemv(const void* x, int M, int N, int K, int group, const void* packed, const float* bias,
+                void* y, cudaStream_t st) {
+  W4Args a;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.group = group;
+  a.n_kb = K / kBK;
+  a.n_groups = K / group;
+  const int grid = N / 16;
+  if (M <= 8)
+    w4a16_gemv_kernel<T, 1><<<grid, 256, 0, st>>>(static_cast<const T*>(x), static_cast<const uint8_t*>(packed),
+                                                  bias, static_cast<T*>(y), a);
+  else
+    w4a16_gemv_kernel<T, 2><<<grid, 256, 0, st>>>(static_cast<const T*>(x), static_cast<const uint8_t*>(packed),
+                                                  bias, static_cast<T*>(y), a);
+  return launched("w4a16_gemv_kernel");
+}
+
+// ---------------------------------------------------------------------------
 // Packing: QuantizedLinear int8 codes + (scale, zero) -> kernel operand.
 //   codes: [N/128][K/64][128 rows][8 words]; word j of a row holds
 //          k = 8j..8j+7 with k = 8j+2p at bits 4p and k = 8j+2p+1 at bits 16+4p;
@@ -483,7 +637,7 @@ int launch_w4(const void* x, int M, int N, int K, int group, const void* packed,
 template <typename T>
 int w4_dispatch(const void* x, int M, int N, int K, int group, const void* packed,
                 const float* bias, void* y, int* err, cudaStream_t st) {
-  if (M <= 16) return launch_w4<T, 16, 8>(x, M, N, K, group, packed, bias, y, err, st);
+  if (M <= 16) return launch_gemv<T>(x, M, N, K, group, packed, bias, y, st);
   if (M <= 32) return launch_w4<T, 32, 8>(x, M, N, K, group, packed, bias, y, err, st);
   if (M <= 64) return launch_w4<T, 64, 8>(x, M, N, K, group, packed, bias, y, err, st);
   if (M <= 128) return launch_w4<T, 128, 6>(x, M, N, K, group, packed, bias, y, err, st);

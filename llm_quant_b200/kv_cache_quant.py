@@ -72,6 +72,7 @@ class KVCacheQuantizer:
     def _prep(self, x: torch.Tensor, what: str) -> torch.Tensor:
         _C.require_cuda(x, what=what)
         _C.require_float(x, what)
+        _C.check_clamp_bounds(x.dtype, self.n_bits, self.symmetric)
         return x.detach().contiguous()
 
     def _token_groups(self, x, tgroup, mode, out_dtype):

@@ -104,8 +104,13 @@ def mul(a, b, dt):
     return _op(lambda x, y: x * y, dt, a, b)
 
 
-def clamp(a, lo, hi):
-    """torch.clamp semantics: NaN passes through, -0.0 is kept."""
+def clamp(a, lo, hi, dt=None):
+    """torch.clamp semantics: NaN passes through, -0.0 is kept.  With ``dt``
+    the tensor is of that dtype, so the result is too: a bound that the dtype
+    cannot hold (qmax = 4095 in bf16) acts as its rounded value (4096), as
+    observed on the reference for 12-bit codes."""
+    if dt is not None:
+        lo, hi = rnd(np.float32(lo), dt), rnd(np.float32(hi), dt)
     a = np.asarray(a, np.float32)
     out = np.where(a < np.float32(lo), np.float32(lo), a)
     out = np.where(out > np.float32(hi), np.float32(hi), out)
@@ -175,7 +180,7 @@ def _scale_zp_from_minmax(x_min, x_max, dt, qmin, qmax, symmetric, amax=None):
     else:
         rngv = clamp_min(sub(x_max, x_min, dt), 1e-12, dt)
         scale = div(rngv, np.float32(qmax - qmin), dt)
-        zp = clamp(rint(div(-x_min, scale, dt)), qmin, qmax)
+        zp = clamp(rint(div(-x_min, scale, dt)), qmin, qmax, dt)
     return scale, zp
 
 
@@ -230,7 +235,7 @@ def quantize_tensor(x, xdt, scale, sdt, zp, zdt, n_bits=8, symmetric=True):
     t = div(x, scale, d1)
     d2 = result_type((t, d1), (zp, zdt))
     t = add(t, zp, d2)
-    return clamp(rint(t), qmin, qmax), d2
+    return clamp(rint(t), qmin, qmax, d2), d2
 
 
 def dequantize_tensor(q, qdt, scale, sdt, zp, zdt):
@@ -251,10 +256,10 @@ def fake_quantize(x, dt, n_bits=8, symmetric=True, scheme="per_tensor", group_si
     if scheme == "per_group" and x.ndim == 2:
         out_f, in_f = x.shape
         xg = pad_groups(x, group_size)
-        q = clamp(ste_round(add(div(xg, scale, dt), zp, dt)), qmin, qmax)
+        q = clamp(ste_round(add(div(xg, scale, dt), zp, dt)), qmin, qmax, dt)
         dq = mul(sub(q, zp, dt), scale, dt)
         return dq.reshape(out_f, -1)[:, :in_f]
-    q = clamp(ste_round(add(div(x, scale, dt), zp, dt)), qmin, qmax)
+    q = clamp(ste_round(add(div(x, scale, dt), zp, dt)), qmin, qmax, dt)
     return mul(sub(q, zp, dt), scale, dt)
 
 
@@ -452,10 +457,10 @@ def kv_quantize(x, dt, n_bits=8, symmetric=True, granularity=PER_TOKEN, group_si
         pad = ng * group_size - T
         xp = np.concatenate([x, np.zeros((B, H, pad, D), np.float32)], 2) if pad else x
         xg = xp.reshape(B, H, ng, group_size, D)
-        q = clamp(rint(add(div(xg, scale, dt), zp, dt)), qmin, qmax)
+        q = clamp(rint(add(div(xg, scale, dt), zp, dt)), qmin, qmax, dt)
         q = q.reshape(B, H, ng * group_size, D)[:, :, :T, :]
         return to_int(q, idt), scale[:, :, :, 0, :], zp[:, :, :, 0, :]
-    q = clamp(rint(add(div(x, scale, dt), zp, dt)), qmin, qmax)
+    q = clamp(rint(add(div(x, scale, dt), zp, dt)), qmin, qmax, dt)
     return to_int(q, idt), scale, zp
 
 

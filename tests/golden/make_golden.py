@@ -179,6 +179,38 @@ def gen_quantizer(ref):
                                 symmetric=sym, group_size=gs, dtype=wdt),
                w=lin.weight.data, bias=lin.bias.data, weight_int=ql.weight_int, scale=ql.scale,
                zero_point=ql.zero_point, x=x, y=y)
+    # wide codes (n_bits > 8): the reference's clamp converts qmax to the tensor
+    # dtype (4095 acts as 4096 in bf16); fp16 with qmax = 65535 raises instead
+    gw = torch.Generator().manual_seed(4242)
+    w = 0
+    for dtn, dt in DT.items():
+        for bits in (10, 12, 16):
+            for sym in (True, False):
+                if dtn == "float16" and bits == 16 and not sym:
+                    try:
+                        fake_quantize(torch.randn(4, 64).half(), bits, sym, QScheme.PER_TENSOR)
+                        raised = False
+                    except RuntimeError:
+                        raised = True
+                    st.add("wide_fp16_raises", dict(fn="wide_raises", dtype=dtn, n_bits=bits,
+                                                    symmetric=sym, raised=raised))
+                    continue
+                for scheme, shape, gs in (("per_group", (6, 192), 64), ("per_channel", (8, 48), 0),
+                                          ("per_tensor", (4, 64), 0)):
+                    x = (torch.randn(shape, generator=gw) * 2).to(dt)
+                    sch = QScheme(scheme)
+                    s, zp = compute_qparams(x, bits, sym, sch, gs if gs else 128)
+                    if scheme == "per_group":
+                        q = quantize_tensor(x.reshape(shape[0], -1, gs), s, zp, bits, sym)
+                    else:
+                        q = quantize_tensor(x, s, zp, bits, sym)
+                    dq = dequantize_tensor(q, s, zp)
+                    fq = fake_quantize(x, bits, sym, sch, gs if gs else 128)
+                    st.add(f"w{w:04d}", dict(fn="quantizer", dtype=dtn, scheme=scheme, shape=list(shape),
+                                             group_size=gs if gs else 128, symmetric=sym, n_bits=bits,
+                                             kind="wide"),
+                           x=x, scale=s, zp=zp, q=q, dq=dq, fq=fq)
+                    w += 1
     st.save("quantizer.npz")
 
 
@@ -363,6 +395,20 @@ def gen_kv(ref):
         _, fv = vc.update(0, v, v)
         tens.update({f"k{j}": k, f"v{j}": v, f"fk{j}": fk, f"fv{j}": fv})
     st.add("cache_mixed", dict(fn="kv_cache_mixed", dtype="bfloat16", chunks=[8, 8, 8]), **tens)
+    # wide codes (n_bits > 8; int16 codes when asymmetric, wrapped int8 when symmetric)
+    gw = torch.Generator().manual_seed(4243)
+    w = 0
+    for dtn, dt in DT.items():
+        for gran in ("per_token", "per_channel", "per_group"):
+            for bits, sym in ((12, False), (16, True), (10, True)):
+                x = (torch.randn(2, 3, 9, 24, generator=gw) * 2).to(dt)
+                qz = KVCacheQuantizer(bits, sym, G(gran), 4)
+                q, s, zp = qz.quantize(x)
+                dqv = qz.dequantize(q, s, zp)
+                st.add(f"kvw{w:04d}", dict(fn="kv", dtype=dtn, granularity=gran, symmetric=sym,
+                                           n_bits=bits, group_size=4, kind="wide"),
+                       x=x, q=q, scale=s, zp=zp, deq=dqv)
+                w += 1
     st.save("kv.npz")
 
 

@@ -154,6 +154,38 @@ def test_nf4_bucket_table_encoder_equals_argmin(dtype):
     assert np.array_equal(code, nf4_encode(rnd(p, dtype)))
 
 
+def test_nf4_g64_bucket_table_encoder_equals_argmin():
+    """The one-thread-per-group bf16 packing kernel buckets a quotient p by
+    k = (bits(fp32(4096 p + 1.5*2^23 + 4608)) & 0x3F80) >> 7, bucket k holding
+    p in [(256k - 9217)/8192, (256k - 8961)/8192], and codes it as (code at
+    the bucket's left edge) + (p >= threshold inside the bucket).  That equals
+    the reference argmin of round_bf16(p) for every bf16 value in [-1, 1],
+    dense samples, the thresholds and their fp32 neighbours."""
+    from oracle.lq_oracle import nf4_encode, rnd
+    th = np.array(_kernel_theta_rows()["bfloat16"], np.float32)
+    k = np.arange(128)
+    left = ((256 * k - 9217) / 8192).astype(np.float32)
+    right = ((256 * k - 8961) / 8192).astype(np.float32)
+    code_lo = (th[None, :] <= left[:, None]).sum(1)
+    inside = (th[None, :] > left[:, None]) & (th[None, :] <= right[:, None])
+    assert inside.sum(1).max() <= 1
+    theta = np.where(inside.any(1), (th[None, :] * inside).sum(1), np.inf).astype(np.float32)
+    u = (np.arange(0, 0x10000, dtype=np.uint32) << 16).view(np.float32)
+    rng = np.random.default_rng(2)
+    p = np.concatenate([u, rng.uniform(-1, 1, 500000).astype(np.float32), th,
+                        np.nextafter(th, np.float32(-2)), np.nextafter(th, np.float32(2)),
+                        left, right, np.nextafter(left, np.float32(2)),
+                        np.array([-1.0, 1.0, -0.0, 0.0], np.float32)])
+    with np.errstate(invalid="ignore"):
+        p = p[np.abs(p) <= 1]
+    # 4096 p is exact in fp32, so the float32 add is the kernel's single-rounding FFMA
+    f = (p * np.float32(4096)).astype(np.float32) + np.float32(12582912 + 4608)
+    b = (f.view(np.uint32) & 0x3F80) >> 7
+    assert b.min() >= 4 and b.max() <= 68
+    code = code_lo[b] + (p >= theta[b])
+    assert np.array_equal(code, nf4_encode(rnd(p, "bfloat16")))
+
+
 def test_host_rejects_cpu_tensors():
     import llm_quant_b200 as L
     x = torch.randn(4, 64)
@@ -210,3 +242,18 @@ def test_install_as_llm_quant():
         for k in [k for k in sys.modules if k == "llm_quant" or k.startswith("llm_quant.")]:
             del sys.modules[k]
         sys.modules.update(saved)
+
+
+def test_fp16_code_range_overflow_raises_like_reference():
+    """The reference's clamp converts qmax to the tensor dtype; for fp16 and
+    asymmetric 16-bit codes (qmax = 65535) that conversion raises.  The golden
+    fixture records the reference raising; this layer raises the same error
+    before any device work."""
+    import llm_quant_b200 as L
+    from golden_io import cases
+    (name, c), = list(cases("quantizer.npz", "wide_raises"))
+    assert c["params"]["raised"] is True
+    with pytest.raises(RuntimeError, match="c10::Half without overflow"):
+        L._C.check_clamp_bounds(torch.float16, 16, False)
+    L._C.check_clamp_bounds(torch.float16, 16, True)    # qmax 32767 fits
+    L._C.check_clamp_bounds(torch.bfloat16, 16, False)  # 65535 -> 65536 fits in bf16

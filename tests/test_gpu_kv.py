@@ -90,6 +90,24 @@ def test_kv_cache_capacity_growth_vs_oracle(L, gran, dtype):
         assert same_bits(to_np(fk), ok) and same_bits(to_np(fv), ov), j
 
 
+@pytest.mark.parametrize("gran", ["per_token", "per_channel", "per_group"])
+@pytest.mark.parametrize("n_bits,head_dim", [(12, 48), (8, 6), (4, 20), (12, 10)])
+def test_kv_cache_code_widths_and_head_dims(L, gran, n_bits, head_dim):
+    """16-bit codes (n_bits > 8), head dims that are not powers of two or not
+    multiples of 4, ragged chunks: full-cache read-out bit-exact vs the oracle."""
+    qcfg = dict(n_bits=n_bits, symmetric=gran != "per_channel", granularity=gran, group_size=2)
+    qz = L.KVCacheQuantizer(n_bits, qcfg["symmetric"], L.KVQuantGranularity(gran), 2)
+    cache = L.QuantizedKVCache(1, qz)
+    ocache = O.QuantizedKVCacheOracle(1, "bfloat16", qcfg)
+    g = torch.Generator().manual_seed(9)
+    for j, n in enumerate([5, 33, 2, 67]):
+        k = O.rnd((torch.randn(2, 2, n, head_dim, generator=g) * (1 + j)).numpy(), "bfloat16")
+        v = O.rnd(torch.randn(2, 2, n, head_dim, generator=g).numpy(), "bfloat16")
+        fk, fv = cache.update(0, to_dev(k, "bfloat16"), to_dev(v, "bfloat16"))
+        ok, ov = ocache.update(0, k, v)
+        assert same_bits(to_np(fk), ok) and same_bits(to_np(fv), ov), j
+
+
 def test_config3_layer(L):
     """One layer of the KV workload: K per-channel INT8, V per-token INT4, bf16
     [16, 8, 8192, 128] in 16 updates of 512 tokens; final update vs oracle."""

@@ -88,6 +88,73 @@ def test_nf4_vs_oracle(L, dtype, shape, gs):
         assert same_bits(to_np(ql._dequantize_base()), wb)
 
 
+def _g64_edge_weight(rows, cols):
+    """bf16 weight, group 64: groups holding every bf16 value in [-1, 1] next
+    to a 1.0 (scale 1, so each quotient is the value itself), random groups,
+    an all-zero group, a tiny-valued group, and groups with +inf, -inf, NaN."""
+    n = rows * cols
+    rng = np.random.default_rng(5)
+    x = (rng.standard_normal(n) * 0.02).astype(np.float32)
+    grid = (np.arange(0, 0x10000, dtype=np.uint32) << 16).view(np.float32)
+    with np.errstate(invalid="ignore"):
+        grid = grid[np.abs(grid) <= 1]
+    n_grid_groups = min((len(grid) + 62) // 63, n // 64 - 8)
+    for i in range(n_grid_groups):
+        part = grid[i * 63:(i + 1) * 63]
+        x[i * 64] = 1.0
+        x[i * 64 + 1:i * 64 + 1 + len(part)] = part
+    g = n // 64
+    x[(g - 1) * 64:(g - 1) * 64 + 64] = 0.0
+    x[(g - 2) * 64:(g - 1) * 64] *= 1e-30
+    x[(g - 3) * 64 + 5] = np.inf
+    x[(g - 4) * 64 + 9] = -np.inf
+    x[(g - 5) * 64 + 17] = np.nan
+    return O.rnd(x.reshape(rows, cols), "bfloat16")
+
+
+@pytest.mark.parametrize("double_quant", [True, False])
+@pytest.mark.parametrize("shape", [(16, 4096), (3, 6400), (17, 192), (1, 64 * 9)])
+def test_pack_base_bf16_g64_edges(L, shape, double_quant):
+    """bf16 / group 64 / whole groups (the one-thread-per-group packing kernel):
+    full and partial double-quantization super-groups, every bf16 quotient in
+    [-1, 1], zero, tiny, infinite and NaN groups; codes, scales and the
+    dequantized base bit-exact against the oracle."""
+    x = _g64_edge_weight(*shape)
+    ql = L.QLoRALinear(shape[1], shape[0], rank=2, group_size=64, double_quant=double_quant).cuda()
+    ql.pack_base(to_dev(x, "bfloat16"))
+    oc, os_ = O.nf4_quantize(x, "bfloat16", 64)
+    assert np.array_equal(to_np(ql.nf4_codes), oc)
+    if double_quant:
+        q, dq = O.double_quantize(os_, "bfloat16", 256)
+        assert same_bits(to_np(ql.dq_q_scales), q) and same_bits(to_np(ql.dq_scales), dq)
+        s = O.double_dequantize(q, dq, "bfloat16", 256)
+    else:
+        assert same_bits(to_np(ql.nf4_scales), os_)
+        s = os_
+    assert same_bits(to_np(ql._dequantize_base()), O.nf4_dequantize(oc, s, "bfloat16", 64))
+
+
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
+@pytest.mark.parametrize("shape,gs", [((40, 96), 8), ((33, 72), 24), ((9, 200), 40), ((31, 256), 128),
+                                      ((5, 77), 8)])
+def test_packed_unpack_group_sizes(L, dtype, shape, gs):
+    """QLoRALinear._dequantize_base for groups that are multiples of 8 (the
+    coalesced unpack kernel; power-of-two and other sizes) and a tail that is
+    not a whole 8-element chunk, with and without double quantization."""
+    x = O.rnd(seeded(shape, 3, 0.02, outliers=2).numpy(), dtype)
+    oc, os_ = O.nf4_quantize(x, dtype, gs)
+    for double_quant in (True, False):
+        ql = L.QLoRALinear(shape[1], shape[0], rank=2, group_size=gs, double_quant=double_quant).cuda()
+        ql.pack_base(to_dev(x, dtype))
+        assert np.array_equal(to_np(ql.nf4_codes), oc)
+        if double_quant:
+            q, dq = O.double_quantize(os_, dtype, 256)
+            s = O.double_dequantize(q, dq, dtype, 256)
+        else:
+            s = os_
+        assert same_bits(to_np(ql._dequantize_base()), O.nf4_dequantize(oc, s, dtype, gs))
+
+
 def test_qlora_state_dict_is_reference_format(L):
     lin = torch.nn.Linear(96, 40).cuda().to(torch.bfloat16)
     ql = L.QLoRA(rank=4, group_size=64).wrap_linear(lin)

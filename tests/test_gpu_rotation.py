@@ -62,7 +62,7 @@ def test_fht_3d_and_orthogonal(L):
 
 
 @pytest.mark.parametrize("dt", ["bfloat16", "float32", "float16"])
-@pytest.mark.parametrize("d", [64, 1024, 4096, 16384])
+@pytest.mark.parametrize("d", [64, 1024, 2048, 4096, 8192, 16384])
 @pytest.mark.parametrize("sym,bits", [(True, 4), (False, 4), (True, 8)])
 def test_fused_rotate_quant_bit_exact_on_own_transform(L, dt, d, sym, bits):
     x = O.rnd(seeded((96, d), 5, 1.0, outliers=max(1, d // 100), factor=50.0).numpy(), dt)
@@ -73,6 +73,49 @@ def test_fused_rotate_quant_bit_exact_on_own_transform(L, dt, d, sym, bits):
     so, zo = O.compute_qparams(h, dt, bits, sym, "per_channel")
     assert same_bits(to_np(s), so) and same_bits(to_np(z), zo)
     assert same_bits(to_np(fq), ref)
+
+
+def _edge_rows(d, dt):
+    """Rows whose transforms are ordinary, constant, a narrow all-positive
+    range, zero, tiny (scale below 2^-126), NaN, +-inf, huge and with strong
+    outliers: every branch of the fused kernels' quantization."""
+    rng = np.random.default_rng(d)
+    rows = [rng.standard_normal(d)]
+    e = np.zeros(d)
+    e[0] = 3.0
+    rows.append(e.copy())
+    e[5] = 0.01
+    rows.append(e)
+    rows.append(np.zeros(d))
+    rows.append(rng.standard_normal(d) * 1e-38)
+    r = rng.standard_normal(d)
+    r[7] = np.nan
+    rows.append(r)
+    r = rng.standard_normal(d)
+    r[9] = np.inf
+    rows.append(r)
+    r = rng.standard_normal(d)
+    r[3] = -np.inf
+    rows.append(r)
+    rows.append(rng.standard_normal(d) * 1e30)
+    r = rng.standard_normal(d)
+    r[::17] *= 100
+    rows.append(r)
+    rows.append(np.abs(rng.standard_normal(d)) + 40.0)
+    return O.rnd(np.stack(rows).astype(np.float32), dt)
+
+
+@pytest.mark.parametrize("dt", ["bfloat16", "float32", "float16"])
+@pytest.mark.parametrize("d", [2048, 4096, 8192])
+@pytest.mark.parametrize("sym,bits", [(True, 4), (False, 4), (True, 8), (False, 8), (True, 2)])
+def test_fused_rotate_quant_edge_rows(L, dt, d, sym, bits):
+    x = _edge_rows(d, dt)
+    xd = to_dev(x, dt)
+    h = to_np(L.fast_hadamard_transform(xd))
+    fq, s, z = L.hadamard_fake_quantize(xd, bits, sym, return_qparams=True)
+    so, zo = O.compute_qparams(h, dt, bits, sym, "per_channel")
+    assert same_bits(to_np(s), so) and same_bits(to_np(z), zo)
+    assert same_bits(to_np(fq), O.fake_quantize(h, dt, bits, sym, "per_channel"))
 
 
 def test_config2_full_size(L):
