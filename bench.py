@@ -48,14 +48,18 @@ LLAMA3_8B = [("q", 4096, 4096), ("k", 1024, 4096), ("v", 1024, 4096), ("o", 4096
              ("gate", 14336, 4096), ("up", 14336, 4096), ("down", 4096, 14336)]
 NUM_LAYERS = 32
 
-# dram__bytes_read.sum + dram__bytes_write.sum per launch of each workload's
-# dominant kernel, from the ncu captures summarised under profiles/ (None
-# until captured).
+# dram__bytes_read.sum + dram__bytes_write.sum of each workload's dominant
+# kernel from one ncu capture of its --profile case (summarised under
+# profiles/), per unit the kernel processes (weight / element), so the bench
+# scales it to its own launch; the W4A16 figure is per launch (same shape as
+# the bench).  Writes still held in L2 when a launch ends are not counted,
+# which is why some ratios sit below the algorithmic bytes.
 NCU_TRAFFIC = {
-    "nf4": None,
-    "group": None,
-    "rotquant": None,
-    "kv": None,
+    "nf4": 279.9e6 / (28672 * 4096),     # nf4_pack_g64_kernel, 2.38 B per weight
+    "group": 212.4e6 / (8192 * 4096),    # group_warp_kernel, 6.33 B per element
+    "rotquant": 209.7e6 / (16384 * 4096),  # fht3_kernel, 3.13 B per element
+    "kv": 277.2e6 / (8 * 8 * 8192 * 128),  # kv_dequant_seg_kernel, 4.13 B per element
+    "w4a16": 42.6e6,                     # w4a16_kernel at M = 1024, bytes per launch
 }
 
 
@@ -291,8 +295,8 @@ class NF4Workload:
         b_pack = 2 * n + n / 2 + 4 * ng + 2 * nd
         b_unpack = n / 2 + 2 * ng + 2 * nd + 2 * n
         return {
-            "nf4_quant_kernel (pack_base)": (b_pack, t_pack, n, "weights"),
-            "nf4_dequant_kernel (_dequantize_base)": (b_unpack, t_unpack, n, "weights"),
+            "nf4_pack_g64_kernel (pack_base)": (b_pack, t_pack, n, "weights"),
+            "nf4_unpack_vec_kernel (_dequantize_base)": (b_unpack, t_unpack, n, "weights"),
         }
 
     def e2e(self, steps, graph):
@@ -485,7 +489,7 @@ class RotQuantWorkload:
             c[0] += 1
         t = cuda_time_ms(self.ctx.torch, f, 40)
         n = self.xs[0].numel()
-        return {"fht_block_kernel (hadamard_fake_quantize)": (4.0 * n, t, n, "elements")}
+        return {"fht3_kernel (hadamard_fake_quantize)": (4.0 * n, t, n, "elements")}
 
     def e2e(self, steps, graph):
         torch = self.ctx.torch
@@ -595,7 +599,7 @@ class KVWorkload:
         side = cache._sides[0][0]
         t = cuda_time_ms(torch, side.dequantize, 10)
         n = side.T * self.B * self.H * self.D
-        return {"kv_dequant_kernel (full-cache fp32 read-out)": (5.0 * n, t, n, "elements")}
+        return {"kv_dequant_seg_kernel (full-cache fp32 read-out)": (5.0 * n, t, n, "elements")}
 
     def e2e(self, steps, graph):
         torch = self.ctx.torch
@@ -717,8 +721,8 @@ class W4A16Workload:
                 c[0] += 1
             t = cuda_time_ms(self.ctx.torch, f, 4 * self.LAYERS)
             wbytes = self.N * self.K / 2 + self.N * (self.K // 128) * 4
-            out[f"w4a16_kernel M={m}"] = (self.flops(m), t, m,
-                                          wbytes + 2 * m * self.K + 2 * m * self.N)
+            kname = "w4a16_gemv_kernel" if m <= 16 else "w4a16_kernel"
+            out[f"{kname} M={m}"] = (self.flops(m), t, m, wbytes + 2 * m * self.K + 2 * m * self.N)
         return out
 
     def e2e(self, steps, graph):
@@ -811,6 +815,8 @@ def profile_case(name, ctx):
         x = torch.randn(1024, 4096, generator=g, device=ctx.dev).half()
         for _ in range(3):
             ql(x)
+        for _ in range(3):
+            ql(x[:1])
     torch.cuda.synchronize()
     print(f"profile case {name} done")
 

@@ -334,18 +334,29 @@ __global__ void __launch_bounds__((1 << L) / 32) fht3_kernel(const T* __restrict
   const int t = threadIdx.x, lane = t & 31;
   const int base2 = (t & 15) + 272 * (t >> 4);
   const int base3 = NF * t + ((NF * t) >> 4);
+  constexpr int V = 16 / sizeof(T);
+  // this thread's 32 input elements of the current row; the next row's are
+  // loaded as soon as these are in registers, so the load overlaps the row
+  uint4 raw[32 / V];
+  if (blockIdx.x < a.rows) {
+#pragma unroll
+    for (int k = 0; k < 32 / V; ++k) raw[k] = ld_nc_v4(x + (int64_t)blockIdx.x * D + (int64_t)t * 32 + k * V);
+  }
   for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
     float2 v[16];
     {  // phase 1
-      const T* src = x + row * D + (int64_t)t * 32;
-      constexpr int V = 16 / sizeof(T);
 #pragma unroll
       for (int k = 0; k < 32 / V; ++k) {
         Vec16<T> u;
-        u.u = ld_nc_v4(src + k * V);
+        u.u = raw[k];
 #pragma unroll
         for (int i = 0; i < V; i += 2)
           v[(k * V + i) / 2] = make_float2(Ty<T>::to_f(u.v[i]), Ty<T>::to_f(u.v[i + 1]));
+      }
+      const int64_t nrow = row + gridDim.x;
+      if (nrow < a.rows) {
+#pragma unroll
+        for (int k = 0; k < 32 / V; ++k) raw[k] = ld_nc_v4(x + nrow * D + (int64_t)t * 32 + k * V);
       }
     }
 #pragma unroll

@@ -22,6 +22,7 @@
 #include <type_traits>
 
 #include "lq_common.cuh"
+#include "lq_tma.cuh"
 
 namespace lq {
 namespace {
@@ -438,61 +439,134 @@ __device__ __forceinline__ void nf4_encode_g64(const uint4 (&w)[8], float rcp, c
   }
 }
 
+struct G64Out {
+  uint4* codes;
+  __nv_bfloat16* scales;
+  __nv_bfloat16* q_scales;
+  __nv_bfloat16* dq_scales;
+  int64_t n_groups;
+  float lo;
+};
+
+// One super-group (256 groups, one per thread of the block): scale, codes,
+// and with DQ the second-level quantization of the 256 scales.
 template <bool DQ>
-__global__ void __launch_bounds__(256, 3) nf4_pack_g64_kernel(const uint4* __restrict__ x,
-                                                              int64_t n_groups, int64_t n_super,
-                                                              float lo, uint4* __restrict__ codes,
-                                                              __nv_bfloat16* __restrict__ scales,
-                                                              __nv_bfloat16* __restrict__ q_scales,
-                                                              __nv_bfloat16* __restrict__ dq_scales) {
+__device__ __forceinline__ void g64_group(const uint4 (&w)[8], int64_t sg, const G64Out& o,
+                                          const char* lutb, uint32_t rep, uint32_t* red) {
   using T = __nv_bfloat16;
-  __shared__ __align__(16) int2 lut[128 * kG64Rep];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t g = sg * 256 + threadIdx.x;
+  const bool live = g < o.n_groups;
+  // |x| as unsigned bf16 pairs; the pair max keeps NaN (its pattern is above +inf)
+  uint32_t m2 = 0;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    m2 = __vimax3_u16x2(m2, w[k].x & 0x7FFF7FFFu, w[k].y & 0x7FFF7FFFu);
+    m2 = __vimax3_u16x2(m2, w[k].z & 0x7FFF7FFFu, w[k].w & 0x7FFF7FFFu);
+  }
+  const float am = __uint_as_float(max(m2 & 0xFFFFu, m2 >> 16) << 16);
+  const float s = (am < o.lo) ? o.lo : am;  // clamp(min=1e-12) in bf16; NaN passes
+  const float rcp = __frcp_rn(s);
+  uint32_t out[8];
+  if (s <= 3.40282347e38f) nf4_encode_g64<false>(w, rcp, lutb, rep, out);
+  else nf4_encode_g64<true>(w, rcp, lutb, rep, out);
+  if (live) {
+    o.scales[g] = __float2bfloat16_rn(s);
+    o.codes[2 * g] = make_uint4(out[0], out[1], out[2], out[3]);
+    o.codes[2 * g + 1] = make_uint4(out[4], out[5], out[6], out[7]);
+  }
+  if constexpr (DQ) {
+    // absmax of the super-group's scales (s >= 0 or +NaN: integer order is float order)
+    const uint32_t mb = __reduce_max_sync(0xffffffffu, live ? __float_as_uint(s) : 0u);
+    if (lane == 0) red[warp] = mb;
+    __syncthreads();
+    uint32_t tot = red[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) tot = max(tot, red[i]);
+    __syncthreads();
+    float dq = __uint_as_float(tot);
+    dq = (dq < o.lo) ? o.lo : dq;
+    if (threadIdx.x == 0) o.dq_scales[sg] = __float2bfloat16_rn(dq);
+    if (live) {
+      const float sn = tdiv<T>(s, dq);
+      const float q = tclamp(trint(tmul<T>(sn, 127.0f)), -127.0f, 127.0f);
+      o.q_scales[g] = __float2bfloat16_rn(q);
+    }
+  }
+}
+
+// Input staging: the weight, viewed as [n_groups][128 bytes], is read by TMA
+// one super-group (256 rows = 32 KB) per copy with the 128-byte swizzle, into
+// a ring of kG64Stages shared-memory stages; row r's 16-byte chunk c lands at
+// chunk c ^ (r % 8), so thread t reads its group as chunks k ^ (t % 8) and
+// the 8 lanes of each quarter-warp hit 8 different bank groups.  Thread 0
+// issues the copies; a stage is refilled (with the super-group kG64Stages
+// iterations ahead) once every thread has read it.  Waits are bounded: a copy
+// that has not landed after 2 s ends the block, whose current super-group
+// then gets NaN scales.
+constexpr int kG64Stages = 2;
+constexpr int kG64StageBytes = 256 * 128;
+constexpr int kG64LutBytes = 128 * kG64Rep * 8;
+constexpr int kG64SmemBytes = kG64Stages * kG64StageBytes + kG64LutBytes + 64 + 1024;
+
+template <bool DQ>
+__global__ void __launch_bounds__(256, 2) nf4_pack_g64_kernel(const __grid_constant__ CUtensorMap tmap,
+                                                              int64_t n_super, G64Out o) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  int2* lut = reinterpret_cast<int2*>(smem + kG64Stages * kG64StageBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kG64Stages * kG64StageBytes + kG64LutBytes);
   __shared__ uint32_t red[8];
+  __shared__ int s_fail;
+  const int t = threadIdx.x;
+  const int64_t step = gridDim.x;
+  if (t == 0) {
+    s_fail = 0;
+    for (int i = 0; i < kG64Stages; ++i) mbar_init(&bars[i], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
   build_lut_g64(lut);
   __syncthreads();
+  if (t == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap)) : "memory");
+    for (int j = 0; j < kG64Stages; ++j) {
+      const int64_t sj = blockIdx.x + j * step;
+      if (sj < n_super) {
+        mbar_expect_tx(&bars[j], kG64StageBytes);
+        tma_load_2d(smem + j * kG64StageBytes, &tmap, 0, (int)(sj * 256), &bars[j]);
+      }
+    }
+  }
   const char* lutb = reinterpret_cast<const char*>(lut);
-  const uint32_t rep = (threadIdx.x & 15) * 8;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int64_t sg = blockIdx.x; sg < n_super; sg += gridDim.x) {
-    const int64_t g = sg * 256 + threadIdx.x;
-    const bool live = g < n_groups;
+  const uint32_t rep = (t & 15) * 8;
+  int it = 0;
+  int64_t sg = blockIdx.x;
+  for (; sg < n_super; sg += step, ++it) {
+    const int s = it % kG64Stages;
+    if (!mbar_wait(&bars[s], (it / kG64Stages) & 1)) s_fail = 1;
     uint4 w[8];
+    const uint8_t* row = smem + s * kG64StageBytes + t * 128;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) w[k] = live ? ld_nc_v4(x + g * 8 + k) : make_uint4(0, 0, 0, 0);
-    // |x| as unsigned bf16 pairs; the pair max keeps NaN (its pattern is above +inf)
-    uint32_t m2 = 0;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      m2 = __vimax3_u16x2(m2, w[k].x & 0x7FFF7FFFu, w[k].y & 0x7FFF7FFFu);
-      m2 = __vimax3_u16x2(m2, w[k].z & 0x7FFF7FFFu, w[k].w & 0x7FFF7FFFu);
+    for (int k = 0; k < 8; ++k) w[k] = *reinterpret_cast<const uint4*>(row + ((k ^ (t & 7)) << 4));
+    __syncthreads();  // stage s has been read by every thread
+    if (s_fail) break;
+    if (t == 0) {
+      const int64_t nsg = sg + kG64Stages * step;
+      if (nsg < n_super) {
+        mbar_expect_tx(&bars[s], kG64StageBytes);
+        tma_load_2d(smem + s * kG64StageBytes, &tmap, 0, (int)(nsg * 256), &bars[s]);
+      }
     }
-    const float am = __uint_as_float(max(m2 & 0xFFFFu, m2 >> 16) << 16);
-    const float s = (am < lo) ? lo : am;  // clamp(min=1e-12) in bf16; NaN passes
-    const float rcp = __frcp_rn(s);
-    uint32_t out[8];
-    if (s <= 3.40282347e38f) nf4_encode_g64<false>(w, rcp, lutb, rep, out);
-    else nf4_encode_g64<true>(w, rcp, lutb, rep, out);
-    if (live) {
-      scales[g] = __float2bfloat16_rn(s);
-      codes[2 * g] = make_uint4(out[0], out[1], out[2], out[3]);
-      codes[2 * g + 1] = make_uint4(out[4], out[5], out[6], out[7]);
-    }
-    if constexpr (DQ) {
-      // absmax of the super-group's scales (s >= 0 or +NaN: integer order is float order)
-      const uint32_t mb = __reduce_max_sync(0xffffffffu, live ? __float_as_uint(s) : 0u);
-      if (lane == 0) red[warp] = mb;
-      __syncthreads();
-      uint32_t tot = red[0];
-#pragma unroll
-      for (int i = 1; i < 8; ++i) tot = max(tot, red[i]);
-      __syncthreads();
-      float dq = __uint_as_float(tot);
-      dq = (dq < lo) ? lo : dq;
-      if (threadIdx.x == 0) dq_scales[sg] = __float2bfloat16_rn(dq);
-      if (live) {
-        const float sn = tdiv<T>(s, dq);
-        const float q = tclamp(trint(tmul<T>(sn, 127.0f)), -127.0f, 127.0f);
-        q_scales[g] = __float2bfloat16_rn(q);
+    g64_group<DQ>(w, sg, o, lutb, rep, red);
+  }
+  if (sg < n_super) {  // a copy timed out: mark this super-group, wait out the copies still in flight
+    const int64_t g = sg * 256 + t;
+    if (g < o.n_groups) o.scales[g] = __float2bfloat16_rn(__int_as_float(0x7fc00000));
+    if (t == 0) {
+      for (int j = 0; j < kG64Stages; ++j) {  // the timed-out copy and the ones issued after it
+        const int jt = it + j;
+        if (sg + j * step < n_super) mbar_wait(&bars[jt % kG64Stages], (jt / kG64Stages) & 1);
       }
     }
   }
@@ -644,6 +718,7 @@ __global__ void __launch_bounds__(256) nf4_unpack_vec_kernel(const uint32_t* __r
                                                              const T* __restrict__ dq_scales,
                                                              uint4* __restrict__ out, int64_t nchunk) {
   __shared__ __align__(16) uint32_t pair[256 * 32];
+  __shared__ uint32_t pair1[256];
   {
     const int b = threadIdx.x;  // blockDim.x == 256
     union {
@@ -652,9 +727,15 @@ __global__ void __launch_bounds__(256) nf4_unpack_vec_kernel(const uint32_t* __r
     } pr;
     pr.h[0] = Ty<T>::from_f(Ty<T>::round(kNF4[b & 15]));
     pr.h[1] = Ty<T>::from_f(Ty<T>::round(kNF4[b >> 4]));
-    uint4* row = reinterpret_cast<uint4*>(pair + 32 * b);
+    pair1[b] = pr.u;
+  }
+  __syncthreads();
+  // replicate: thread t fills words 4t..4t+3 of each 4 KB slice (copies of
+  // entry t/8 + 32j), so the 8 lanes of a quarter-warp store 128 contiguous bytes
 #pragma unroll
-    for (int i = 0; i < 8; ++i) row[i] = make_uint4(pr.u, pr.u, pr.u, pr.u);
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t v = pair1[(threadIdx.x >> 3) + 32 * j];
+    reinterpret_cast<uint4*>(pair)[threadIdx.x + 256 * j] = make_uint4(v, v, v, v);
   }
   __syncthreads();
   const char* pb = reinterpret_cast<const char*>(pair);
@@ -665,20 +746,29 @@ __global__ void __launch_bounds__(256) nf4_unpack_vec_kernel(const uint32_t* __r
   const int64_t span = 32 * kUnpackK;
   for (int64_t base = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * span; base < nchunk;
        base += warps * span) {
+    // every load of the iteration (codes and scales) is issued before any use
     uint32_t w[kUnpackK];
+    T sq[kUnpackK], sd[kUnpackK];
 #pragma unroll
     for (int k = 0; k < kUnpackK; ++k) {
       const int64_t c = base + 32 * k + lane;
-      w[k] = c < nchunk ? __ldg(codes + c) : 0u;
+      const bool live = c < nchunk;
+      const int64_t g = !live ? 0 : (c_shift >= 0 ? (c >> c_shift) : (c * 8) / a.G);
+      w[k] = live ? __ldg(codes + c) : 0u;
+      if (q_scales) {
+        sq[k] = q_scales[g];
+        sd[k] = dq_scales[a.dg_shift >= 0 ? (g >> a.dg_shift) : g / a.DG];
+      } else {
+        sq[k] = scales[g];
+      }
     }
 #pragma unroll
     for (int k = 0; k < kUnpackK; ++k) {
       const int64_t c = base + 32 * k + lane;
       if (c >= nchunk) break;
-      const int64_t g = c_shift >= 0 ? (c >> c_shift) : (c * 8) / a.G;
       float s;
-      if (q_scales) s = tmul<T>(tdiv<T>(Ty<T>::to_f(q_scales[g]), 127.0f), Ty<T>::to_f(dq_scales[a.dg_shift >= 0 ? (g >> a.dg_shift) : g / a.DG]));
-      else s = Ty<T>::to_f(scales[g]);
+      if (q_scales) s = tmul<T>(tdiv<T>(Ty<T>::to_f(sq[k]), 127.0f), Ty<T>::to_f(sd[k]));
+      else s = Ty<T>::to_f(sq[k]);
       union {
         T h[2];
         uint32_t u;
@@ -775,29 +865,50 @@ int grid_cap(int64_t want, int per_sm = 8) {
   return (int)(want < 1 ? 1 : (want < cap ? want : cap));
 }
 
+// TMA view of a bf16 weight as [n_groups][64 elements] (128-byte rows),
+// boxes of 256 rows, 128-byte swizzle; false when the driver entry point is
+// missing or rejects the map (the caller then uses the register path).
+bool g64_tensor_map(CUtensorMap* map, const void* x, int64_t n_groups) {
+  EncodeTiledFn enc = encode_fn();
+  if (enc == nullptr || n_groups >= (int64_t(1) << 31)) return false;
+  cuuint64_t dims[2] = {64, (cuuint64_t)n_groups};
+  cuuint64_t strides[1] = {128};
+  cuuint32_t box[2] = {64, 256};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <typename T, int CODE_DT, bool DQ>
 int nf4_quant_launch(const T* x, NfArgs a, void* codes, T* scales, T* qs, T* dqs, cudaStream_t st) {
   constexpr int V = 16 / sizeof(T);
   const bool vec = (a.G % V == 0) && aligned16(x) && (a.G / V) <= 32 * 4 &&
                    (CODE_DT != LQ_U4X2 || (a.G * 4) % 8 == 0) &&
                    (reinterpret_cast<uintptr_t>(codes) % (CODE_DT == LQ_I64 ? 16 : 4) == 0);
-  if (!DQ && !vec) {
+  // the fused one-pass kernels hold a group in a team of tps lanes x nvt
+  // vectors; other group sizes (and unaligned buffers) take the scalar path:
+  // scales, then codes, then (double quantization) the scales' second level
+  const int64_t nv = a.G / V;
+  int tps = 1, nvt = 1;
+  bool fused = vec;
+  if (fused && nv <= 32) {
+    while (tps < nv) tps <<= 1;
+    fused = (tps == nv);
+  } else if (fused) {
+    tps = 32;
+    nvt = (int)(nv / 32);
+    fused = (nv % 32 == 0) && (nvt == 2 || nvt == 4);
+  }
+  if (!fused) {
     nf4_scales_kernel<T><<<grid_cap(a.n_groups, 16), 256, 0, st>>>(x, a, scales);
     int rc = launched("nf4_scales_kernel");
     if (rc != LQ_OK) return rc;
     nf4_codes_kernel<T, CODE_DT><<<grid_cap((a.n + 511) / 512, 16), 256, 0, st>>>(x, a, scales, codes);
-    return launched("nf4_codes_kernel");
-  }
-  LQ_REQUIRE(vec, LQ_EALIGN, "fused NF4 packing needs group %% %d == 0 and 16-byte aligned input", V);
-  const int64_t nv = a.G / V;
-  int tps = 1, nvt = 1;
-  if (nv <= 32) {
-    while (tps < nv) tps <<= 1;
-    if (tps != nv) { set_error("group/%d must be a power of two <= 32 or a multiple of 32", V); return LQ_EINVAL; }
-  } else {
-    tps = 32;
-    nvt = (int)(nv / 32);
-    if (nv % 32 || (nvt != 2 && nvt != 4)) { set_error("unsupported NF4 group size %lld", (long long)a.G); return LQ_EINVAL; }
+    rc = launched("nf4_codes_kernel");
+    if (rc != LQ_OK || !DQ) return rc;
+    double_quant_kernel<T><<<grid_cap(a.n_super, 16), 256, 0, st>>>(scales, a.n_groups, a.DG, a.lo, qs, dqs);
+    return launched("double_quant_kernel");
   }
   if (!DQ) {
     a.DG = 256 / tps * 8;  // super-group = a few block iterations
@@ -809,10 +920,28 @@ int nf4_quant_launch(const T* x, NfArgs a, void* codes, T* scales, T* qs, T* dqs
     uint8_t* cp = static_cast<uint8_t*>(codes);
     if (a.G == 64 && a.n % 64 == 0 && aligned16(codes) && (!DQ || a.DG == 256)) {
       const int64_t n_chunks = (a.n_groups + 255) / 256;
-      nf4_pack_g64_kernel<DQ><<<grid_cap(n_chunks, 3), 256, 0, st>>>(
-          reinterpret_cast<const uint4*>(x), a.n_groups, n_chunks, a.lo, reinterpret_cast<uint4*>(cp),
-          scales, qs, dqs);
-      return launched("nf4_pack_g64_kernel");
+      CUtensorMap map;
+      if (g64_tensor_map(&map, x, a.n_groups)) {
+        G64Out o;
+        o.codes = reinterpret_cast<uint4*>(cp);
+        o.scales = scales;
+        o.q_scales = qs;
+        o.dq_scales = dqs;
+        o.n_groups = a.n_groups;
+        o.lo = a.lo;
+        auto kern = nf4_pack_g64_kernel<DQ>;
+        static std::atomic<uint64_t> attr_done{0};  // one bit per device
+        int dev = 0;
+        cudaGetDevice(&dev);
+        const uint64_t bit = 1ull << (dev & 63);
+        if (!(attr_done.load() & bit)) {
+          cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kG64SmemBytes);
+          LQ_REQUIRE(e == cudaSuccess, LQ_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+          attr_done.fetch_or(bit);
+        }
+        kern<<<grid_cap(n_chunks, 2), 256, kG64SmemBytes, st>>>(map, n_chunks, o);
+        return launched("nf4_pack_g64_kernel");
+      }
     }
     if (nvt == 1) nf4_pack_bf16_kernel<1, DQ><<<grid, 256, smem, st>>>(x, a, tps, cp, scales, qs, dqs);
     else if (nvt == 2) nf4_pack_bf16_kernel<2, DQ><<<grid, 256, smem, st>>>(x, a, tps, cp, scales, qs, dqs);

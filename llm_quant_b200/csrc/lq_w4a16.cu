@@ -23,6 +23,7 @@
 // code in *err (when given), drains its outstanding copies (bounded), frees
 // its tensor memory and returns.
 #include "lq_common.cuh"
+#include "lq_tma.cuh"
 
 namespace lq {
 namespace {
@@ -33,66 +34,8 @@ constexpr int kWStage = kRows * kBK / 2;  // packed codes per stage: 4 KB
 constexpr int kSStage = kRows * 4;        // (zero, scale) pairs per stage: 512 B
 constexpr int kAcol = 256;        // first TMEM column of the A slots
 constexpr uint32_t kTmemCols = 512;
-constexpr uint64_t kWaitNs = 2000000000ull;  // bounded waits give up after 2 s
 
-// ---- PTX wrappers ----------------------------------------------------------
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count));
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(b)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-// Bounded wait; false once kWaitNs of wall time has passed.
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity) {
-  if (mbar_try(b, parity)) return true;
-  const uint64_t t0 = global_ns();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try(b, parity)) return true;
-    if ((i & 255) == 0 && global_ns() - t0 > kWaitNs) return false;
-  }
-}
-// Warp-uniform bounded wait (every lane polls; all agree on the outcome).
-__device__ __forceinline__ bool mbar_wait_warp(uint64_t* b, uint32_t parity) {
-  return __all_sync(0xffffffffu, mbar_wait(b, parity));
-}
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
-                                            uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
+// ---- tensor-core PTX wrappers ----------------------------------------------
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -430,16 +373,39 @@ __global__ void __launch_bounds__(256) w4a16_gemv_kernel(const T* __restrict__ x
     xlive[j] = tok < a.M;
     xrow[j] = (int64_t)(xlive[j] ? tok : 0) * a.K;
   }
-  for (int kb = warp; kb < a.n_kb; kb += 8) {
+  // the next K step's codes and (zero, scale) pairs are loaded before the
+  // current one is computed
+  uint4 w0, w1, w2, w3;
+  uint32_t zs0 = 0, zs1 = 0;
+  auto load_step = [&](int kb, uint4& a0, uint4& a1, uint4& b0, uint4& b1, uint32_t& z0, uint32_t& z1) {
     const uint4* src = reinterpret_cast<const uint4*>(wt + (size_t)kb * kWStage + rit * 32);
-    const uint4 w0 = __ldg(src), w1 = __ldg(src + 1);              // row g
-    const uint4 w2 = __ldg(src + 16), w3 = __ldg(src + 17);        // row g + 8
+    a0 = __ldg(src);
+    a1 = __ldg(src + 1);  // row g
+    b0 = __ldg(src + 16);
+    b1 = __ldg(src + 17);  // row g + 8
     const int grp = (kb * kBK) / a.group;
-    const uint32_t zs0 = __ldg(pr + (size_t)grp * kRows + rit);
-    const uint32_t zs1 = __ldg(pr + (size_t)grp * kRows + rit + 8);
+    z0 = __ldg(pr + (size_t)grp * kRows + rit);
+    z1 = __ldg(pr + (size_t)grp * kRows + rit + 8);
+  };
+  if (warp < a.n_kb) load_step(warp, w0, w1, w2, w3, zs0, zs1);
+  for (int kb = warp; kb < a.n_kb; kb += 8) {
+    uint4 n0 = w0, n1 = w1, n2 = w2, n3 = w3;
+    uint32_t nz0 = zs0, nz1 = zs1;
+    if (kb + 8 < a.n_kb) load_step(kb + 8, n0, n1, n2, n3, nz0, nz1);
     const uint32_t zb0 = __byte_perm(zs0, zs0, 0x1010), zb1 = __byte_perm(zs1, zs1, 0x1010);
     const uint32_t ra[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
     const uint32_t rb[8] = {w2.x, w2.y, w2.z, w2.w, w3.x, w3.y, w3.z, w3.w};
+    // this K step's B fragments (token rows of the lane), loaded up front
+    uint32_t bx[NT8][4][2];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const int k = kb * kBK + 16 * t + 2 * c;
+#pragma unroll
+      for (int j = 0; j < NT8; ++j) {
+        bx[j][t][0] = xlive[j] ? __ldg(reinterpret_cast<const uint32_t*>(xs + xrow[j] + k)) : 0u;
+        bx[j][t][1] = xlive[j] ? __ldg(reinterpret_cast<const uint32_t*>(xs + xrow[j] + k + 8)) : 0u;
+      }
+    }
     float part[NT8][4];
 #pragma unroll
     for (int j = 0; j < NT8; ++j)
@@ -452,13 +418,8 @@ __global__ void __launch_bounds__(256) w4a16_gemv_kernel(const T* __restrict__ x
       af[1] = MmaOp<T>::sub2(((rb[2 * t] >> (4 * c)) & 0x000F000Fu) | Act<T>::magic, zb1);
       af[2] = MmaOp<T>::sub2(((ra[2 * t + 1] >> (4 * c)) & 0x000F000Fu) | Act<T>::magic, zb0);
       af[3] = MmaOp<T>::sub2(((rb[2 * t + 1] >> (4 * c)) & 0x000F000Fu) | Act<T>::magic, zb1);
-      const int k = kb * kBK + 16 * t + 2 * c;
 #pragma unroll
-      for (int j = 0; j < NT8; ++j) {
-        const uint32_t b0 = xlive[j] ? __ldg(reinterpret_cast<const uint32_t*>(xs + xrow[j] + k)) : 0u;
-        const uint32_t b1 = xlive[j] ? __ldg(reinterpret_cast<const uint32_t*>(xs + xrow[j] + k + 8)) : 0u;
-        MmaOp<T>::mma(part[j], af, b0, b1);
-      }
+      for (int j = 0; j < NT8; ++j) MmaOp<T>::mma(part[j], af, bx[j][t][0], bx[j][t][1]);
     }
     // scales of rows g and g + 8 (high halves of the pairs)
     const float s0 = MmaOp<T>::hi_f(zs0), s1 = MmaOp<T>::hi_f(zs1);
@@ -469,6 +430,12 @@ __global__ void __launch_bounds__(256) w4a16_gemv_kernel(const T* __restrict__ x
       acc[j][2] = fmaf(part[j][2], s1, acc[j][2]);
       acc[j][3] = fmaf(part[j][3], s1, acc[j][3]);
     }
+    w0 = n0;
+    w1 = n1;
+    w2 = n2;
+    w3 = n3;
+    zs0 = nz0;
+    zs1 = nz1;
   }
 #pragma unroll
   for (int j = 0; j < NT8; ++j)
@@ -575,23 +542,6 @@ __global__ void __launch_bounds__(256) w4a16_pack_kernel(const int8_t* __restric
 }
 
 // ---- host side ---------------------------------------------------------------
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess)
-      return (EncodeTiledFn) nullptr;
-    return reinterpret_cast<EncodeTiledFn>(p);
-  }();
-  return fn;
-}
-
 template <typename T, int BT, int S>
 int launch_w4(const void* x, int M, int N, int K, int group, const void* packed, const float* bias,
               void* y, int* err, cudaStream_t st) {
