@@ -673,6 +673,7 @@ class W4A16Workload:
     `kernels`, cycling through the layers.  Weak scaling (replicas)."""
     name = "w4a16"
     workload = "quantized_linear_w4a16_K4096_N14336_g128_fp16_M1024_x6_layers"
+    main_kernel = "w4a16_kernel"
     Ms = (1, 16, 128, 1024, 4096)
     K, N = 4096, 14336
     LAYERS = 6
@@ -730,7 +731,7 @@ class W4A16Workload:
         copied in from pinned host memory and y copied back, every step."""
         torch = self.ctx.torch
         host = self.x[1024].cpu().pin_memory()
-        out = torch.empty(1024, self.N, dtype=torch.float16).pin_memory()
+        out = torch.empty(1024, self.N, dtype=self.x[1024].dtype).pin_memory()
         dev = self.x[1024]
         torch.cuda.synchronize()
         graphs, ys = [], []
@@ -783,6 +784,80 @@ class W4A16Workload:
                 "sample": f"oracle dequant + numpy fp32 matmul, M={M}, K={K}, N={N}, median of 3"}
 
 
+class QLoRALinearWorkload(W4A16Workload):
+    """QLoRALinear forward with a bf16 NF4 base (block 64, double quant) of
+    Linear(4096, 14336) shape, rank-16 LoRA, bf16 activations: the fused NF4
+    base product (lq_nf4_linear) plus the LoRA path.  Six layers with distinct
+    weights; a step is the forward of all six at M = 1024 tokens, and FLOPs
+    count the base product only (the rank-16 LoRA path adds 0.8 % more work
+    inside the timed region).  `kernels` times the fused base product alone at
+    every M.  Weak scaling (replicas)."""
+    name = "qlora_linear"
+    workload = "qlora_linear_nf4_bf16_K4096_N14336_block64_dq256_M1024_x6_layers"
+    main_kernel = "nf4_linear_kernel"
+
+    def __init__(self, ctx):
+        torch = ctx.torch
+        import llm_quant_b200 as L
+        from llm_quant_b200 import nf4_linear
+        self.ctx, self.L, self.nl = ctx, L, nf4_linear
+        g = torch.Generator(device=ctx.dev).manual_seed(0)
+        self.qls = []
+        for _ in range(self.LAYERS):
+            w = (torch.randn(self.N, self.K, generator=g, device=ctx.dev) * 0.02).to(torch.bfloat16)
+            ql = L.QLoRALinear(self.K, self.N, rank=16, group_size=64).to(ctx.dev)
+            with torch.no_grad():
+                ql.lora_B.normal_(0, 0.02, generator=g)
+            ql.pack_base(w)
+            ql.requires_grad_(False)
+            self.qls.append(ql)
+        self.ql = self.qls[0]
+        self.x = {m: torch.randn(m, self.K, generator=g, device=ctx.dev).to(torch.bfloat16)
+                  for m in self.Ms}
+        for ql in self.qls:
+            ql(self.x[1])  # builds the kernel operand
+        self.n_local = self.LAYERS
+        self.n_total = self.LAYERS * ctx.world
+        self.unit = "TFLOP/s"
+
+    def kernels(self):
+        out = {}
+        for m in self.Ms:
+            x = self.x[m]
+            c = [0]
+
+            def f():
+                self.nl.base_linear(self.qls[c[0] % self.LAYERS], x)
+                c[0] += 1
+            t = cuda_time_ms(self.ctx.torch, f, 4 * self.LAYERS)
+            wbytes = self.N * self.K / 2 + self.N * (self.K // 64) * 4
+            kname = "nf4_linear_gemv_kernel" if m <= 16 else "nf4_linear_kernel"
+            out[f"{kname} M={m}"] = (self.flops(m), t, m, wbytes + 2 * m * self.K + 2 * m * self.N)
+        return out
+
+    @staticmethod
+    def cpu_baseline():
+        """Oracle QLoRALinear base product: NF4 dequant (double quant) of the
+        bf16 base, then x @ W^T in fp32 (numpy BLAS), M = 64 tokens."""
+        from oracle import lq_oracle as O
+        rng = np.random.default_rng(0)
+        K, N, M = 4096, 14336, 64
+        w = O.rnd((rng.standard_normal((N, K)) * 0.02).astype(np.float32), "bfloat16")
+        codes, sc = O.nf4_quantize(w, "bfloat16", 64)
+        q, dq = O.double_quantize(sc, "bfloat16", 256)
+        x = O.rnd(rng.standard_normal((M, K)).astype(np.float32), "bfloat16")
+        ts = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            wf = O.nf4_dequantize(codes, O.double_dequantize(q, dq, "bfloat16", 256), "bfloat16", 64)
+            _ = x @ wf.reshape(N, K).T
+            ts.append(time.perf_counter() - t0)
+        t = statistics.median(ts)
+        return {"value": 2.0 * M * K * N / t / 1e12, "unit": "TFLOP/s",
+                "cores": _threads(), "kind": "port",
+                "sample": f"oracle NF4 dequant + numpy fp32 matmul, M={M}, K={K}, N={N}, median of 3"}
+
+
 def profile_case(name, ctx):
     """A small case of each workload's dominant kernel for ncu captures:
     inputs larger than L2 (126 MB) but a few hundred MB at most, 3 launches."""
@@ -817,12 +892,22 @@ def profile_case(name, ctx):
             ql(x)
         for _ in range(3):
             ql(x[:1])
+    elif name == "qlora_linear":
+        w = (torch.randn(14336, 4096, generator=g, device=ctx.dev) * 0.02).to(torch.bfloat16)
+        ql = L.QLoRALinear(4096, 14336, rank=16, group_size=64).to(ctx.dev)
+        ql.pack_base(w)
+        ql.requires_grad_(False)
+        x = torch.randn(1024, 4096, generator=g, device=ctx.dev).to(torch.bfloat16)
+        for _ in range(3):
+            ql(x)
+        for _ in range(3):
+            ql(x[:1])
     torch.cuda.synchronize()
     print(f"profile case {name} done")
 
 
 WORKLOADS = {"nf4": NF4Workload, "group": GroupWorkload, "rotquant": RotQuantWorkload,
-             "kv": KVWorkload, "w4a16": W4A16Workload}
+             "kv": KVWorkload, "w4a16": W4A16Workload, "qlora_linear": QLoRALinearWorkload}
 
 
 # ─────────────────────────────────────────────────────────────────────────────
@@ -897,7 +982,7 @@ def run_ours(args):
     kern = W.kernels()
     traffic = NCU_TRAFFIC.get(W.name)
     if unit == "TFLOP/s":
-        name = "w4a16_kernel M=1024"
+        name = f"{W.main_kernel} M=1024"
         fl, kms, m, wb = kern[name]
         achieved = fl / (kms * 1e-3) / 1e12
         roofline = {"bound": "tensor", "kernel": name, "achieved": achieved, "peak": tflops,

@@ -252,8 +252,9 @@ int lq_hadamard_fake_quant(const void* x, int dtype, int64_t rows, int64_t d, in
  * the activation dtype.
  * lq_w4a16_linear: y[M, N] = x[M, K] @ dequant(W)^T + bias, x / y in act_dtype
  * (LQ_F16 or LQ_BF16), bias fp32 [N] or NULL, fp32 accumulation on the tensor
- * cores (tcgen05.mma; A = weights dequantized into tensor memory, B =
- * activations by TMA).  Requires N % 128 == 0, K % 64 == 0, group % 64 == 0.
+ * cores (M > 16: tcgen05.mma, A = weights dequantized into tensor memory, B =
+ * activations by TMA; M <= 16: a weight-streaming mma.sync kernel).
+ * Requires N % 128 == 0, K % 64 == 0, group % 64 == 0.
  * err (device int, may be NULL) receives a non-zero code if a bounded
  * device-side wait ran out (the kernel then returns early). */
 size_t lq_w4a16_packed_bytes(int64_t N, int64_t K, int64_t group);
@@ -263,6 +264,27 @@ int lq_w4a16_pack(const int8_t* weight_int, const void* scale, const void* zero_
 int lq_w4a16_linear(const void* x, int act_dtype, int64_t M, int64_t N, int64_t K,
                     int64_t group, const void* packed, const float* bias, void* y, int* err,
                     void* stream);
+
+/* ---- NF4 linear (replaces QLoRALinear.forward's base path, qlora.py:306-312) --
+ * The reference dequantizes the whole NF4 base weight (_dequantize_base,
+ * qlora.py:294-304) and calls F.linear; here the table lookup and the block
+ * scale are fused into the same GEMM kernels as lq_w4a16_linear.
+ * lq_nf4_linear_pack builds the operand (lq_nf4_linear_packed_bytes() bytes,
+ * 16-byte aligned) from the module's packed codes (LQ_U4X2 layout of the
+ * flattened [N, K] weight) and its block scales: either `scales` [N*K/group],
+ * or q_scales [N*K/group] + dq_scales [.. / dq_group] (the double
+ * quantization, restored as round(round(q/127) * dq) in s_dtype, exactly as
+ * _dequantize_base does).  Requires N % 128 == 0, K % 64 == 0,
+ * group % 64 == 0 and K % group == 0.
+ * lq_nf4_linear: y[M, N] = x[M, K] @ W^T + bias with W = round_T(NF4[code] *
+ * scale), x / y in act_dtype (LQ_F16 or LQ_BF16), bias fp32 [N] or NULL, fp32
+ * accumulation; err as for lq_w4a16_linear. */
+size_t lq_nf4_linear_packed_bytes(int64_t N, int64_t K);
+int lq_nf4_linear_pack(const void* codes, const void* scales, const void* q_scales,
+                       const void* dq_scales, int s_dtype, int64_t N, int64_t K, int64_t group,
+                       int64_t dq_group, int act_dtype, void* packed, void* stream);
+int lq_nf4_linear(const void* x, int act_dtype, int64_t M, int64_t N, int64_t K,
+                  const void* packed, const float* bias, void* y, int* err, void* stream);
 
 #ifdef __cplusplus
 }

@@ -65,11 +65,14 @@ _SIGS = {
     "lq_hadamard_fake_quant": [_V, _I, _L, _L, _I, _I, _V, _V, _V, _V],
     "lq_w4a16_pack": [_V, _V, _V, _I, _L, _L, _L, _I, _I, _V, _V],
     "lq_w4a16_linear": [_V, _I, _L, _L, _L, _L, _V, _V, _V, _V, _V],
+    "lq_nf4_linear_pack": [_V, _V, _V, _V, _I, _L, _L, _L, _L, _I, _V, _V],
+    "lq_nf4_linear": [_V, _I, _L, _L, _L, _V, _V, _V, _V, _V],
 }
 _SIZE_SIGS = {
     "lq_tensor_qparams_workspace_size": [_L],
     "lq_channel_qparams_workspace_size": [_L, _L, _L],
     "lq_w4a16_packed_bytes": [_L, _L, _L],
+    "lq_nf4_linear_packed_bytes": [_L, _L],
 }
 
 _lib = None

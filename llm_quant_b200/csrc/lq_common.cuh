@@ -113,6 +113,11 @@ template <typename T> __device__ __forceinline__ float tmul(float a, float b) {
   return Ty<T>::round(__fmul_rn(a, b));
 }
 
+// NF4_TABLE as float32 (qlora.py:50-55).
+static __device__ __constant__ float kNF4[16] = {
+    -1.0f, -0.6962f, -0.5251f, -0.3949f, -0.2844f, -0.1848f, -0.0911f, 0.0f,
+    0.0796f, 0.1609f, 0.2461f, 0.3379f, 0.4407f, 0.5626f, 0.7230f, 1.0f};
+
 // torch.clamp(v, lo, hi): NaN passes, -0.0 is kept.
 __device__ __forceinline__ float tclamp(float v, float lo, float hi) {
   v = (v < lo) ? lo : v;

@@ -27,10 +27,6 @@
 namespace lq {
 namespace {
 
-// NF4_TABLE as float32 (qlora.py:50-55).
-__device__ __constant__ float kNF4[16] = {
-    -1.0f, -0.6962f, -0.5251f, -0.3949f, -0.2844f, -0.1848f, -0.0911f, 0.0f,
-    0.0796f, 0.1609f, 0.2461f, 0.3379f, 0.4407f, 0.5626f, 0.7230f, 1.0f};
 
 // Decision thresholds on the unrounded quotient, per input dtype
 // (row 0: fp32, 1: fp16, 2: bf16).

@@ -106,6 +106,10 @@ template <typename T> struct Act;
 template <> struct Act<__half> {
   static constexpr int fmt = 0;
   static constexpr uint32_t magic = 0x64006400u;  // fp16 1024.0 in both halves
+  __device__ __forceinline__ static uint32_t mul2(uint32_t v, uint32_t s) {
+    __half2 h = __hmul2(*reinterpret_cast<__half2*>(&v), *reinterpret_cast<__half2*>(&s));
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
   __device__ __forceinline__ static uint32_t sub_mul(uint32_t v, uint32_t zb, uint32_t s) {
     __half2 h = __hsub2(*reinterpret_cast<__half2*>(&v), *reinterpret_cast<__half2*>(&zb));
     h = __hmul2(h, *reinterpret_cast<__half2*>(&s));
@@ -115,6 +119,10 @@ template <> struct Act<__half> {
 template <> struct Act<__nv_bfloat16> {
   static constexpr int fmt = 1;
   static constexpr uint32_t magic = 0x43004300u;  // bf16 128.0 in both halves
+  __device__ __forceinline__ static uint32_t mul2(uint32_t v, uint32_t s) {
+    __nv_bfloat162 h = __hmul2(*reinterpret_cast<__nv_bfloat162*>(&v), *reinterpret_cast<__nv_bfloat162*>(&s));
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
   __device__ __forceinline__ static uint32_t sub_mul(uint32_t v, uint32_t zb, uint32_t s) {
     __nv_bfloat162 h = __hsub2(*reinterpret_cast<__nv_bfloat162*>(&v), *reinterpret_cast<__nv_bfloat162*>(&zb));
     h = __hmul2(h, *reinterpret_cast<__nv_bfloat162*>(&s));
@@ -126,26 +134,59 @@ struct W4Args {
   int M, N, K, group, n_kb, n_groups;
 };
 
-template <typename T, int BT, int S>
+// NF4 weights (QLoRALinear): code byte b = elements 2i (low nibble) and
+// 2i+1 (high nibble) -> the pair (round_T(NF4[lo]), round_T(NF4[hi])).  The
+// 256-entry table is stored 32 times, entry b of copy r at word 32 b + r, so
+// lane r of a warp reads copy r and 32 independent lookups never share a
+// bank.  tmp holds the 256 pairs while the copies are written.  Every thread
+// of the block calls this (it synchronizes).
+constexpr int kPairLutWords = 256 * 32;
+template <typename T>
+__device__ __forceinline__ void build_pair_lut(uint32_t* lut, uint32_t* tmp) {
+  for (int b = threadIdx.x; b < 256; b += blockDim.x) {
+    union {
+      T h[2];
+      uint32_t u;
+    } pr;
+    pr.h[0] = Ty<T>::from_f(Ty<T>::round(kNF4[b & 15]));
+    pr.h[1] = Ty<T>::from_f(Ty<T>::round(kNF4[b >> 4]));
+    tmp[b] = pr.u;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < kPairLutWords / 4; i += blockDim.x) {
+    const uint32_t v = tmp[i >> 3];  // words 4i..4i+3 are copies of entry i / 8
+    reinterpret_cast<uint4*>(lut)[i] = make_uint4(v, v, v, v);
+  }
+}
+
+// Byte offset of the table word for byte b (0..3) of w, in copy `lane`.
+__device__ __forceinline__ uint32_t pair_lut_off(uint32_t w, int b, uint32_t lane4) {
+  const uint32_t off = (b == 0 ? (w << 7) : (w >> (8 * b - 7))) & 0x7F80u;
+  return off | lane4;
+}
+
+template <typename T, int BT, int S, bool NF>
 struct Smem {
   static constexpr int kX = BT * kBK * 2;  // activation tile bytes per stage
   static constexpr int off_x = 0;
   static constexpr int off_w = off_x + S * kX;
   static constexpr int off_s = off_w + S * kWStage;
-  static constexpr int off_bar = off_s + S * kSStage;
+  static constexpr int off_lut = off_s + S * kSStage;             // NF4 pair table (NF only)
+  static constexpr int off_tmp = off_lut + (NF ? kPairLutWords * 4 : 0);
+  static constexpr int off_bar = off_tmp + (NF ? 1024 : 0);
   // barriers: full_x[S], full_w[S], a_full[S], empty[S], acc_full
   static constexpr int n_bar = 4 * S + 1;
   static constexpr int off_tmem = off_bar + n_bar * 8;
   static constexpr int bytes = off_tmem + 16 + 1024;  // + alignment slack
 };
 
-template <typename T, int BT, int S>
+template <typename T, int BT, int S, bool NF>
 __global__ void __launch_bounds__(192, 1) w4a16_kernel(const __grid_constant__ CUtensorMap tmap_x,
                                                        const uint8_t* __restrict__ packed,
                                                        const float* __restrict__ bias,
                                                        T* __restrict__ y, W4Args a,
                                                        int* __restrict__ err) {
-  using L = Smem<T, BT, S>;
+  using L = Smem<T, BT, S, NF>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::off_bar);
@@ -181,6 +222,9 @@ __global__ void __launch_bounds__(192, 1) w4a16_kernel(const __grid_constant__ C
                      smem_u32(tmem_slot)),
                  "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if constexpr (NF) {
+    build_pair_lut<T>(reinterpret_cast<uint32_t*>(smem + L::off_lut), reinterpret_cast<uint32_t*>(smem + L::off_tmp));
   }
   tc_fence_before();
   __syncthreads();
@@ -255,13 +299,24 @@ __global__ void __launch_bounds__(192, 1) w4a16_kernel(const __grid_constant__ C
       const uint32_t sc = __byte_perm(zs, zs, 0x3232);
       const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
       uint32_t r[32];
+      if constexpr (NF) {
+        // byte c = k pair (2c, 2c+1) -> table pair * scale = round_T(NF4 * scale)
+        const char* lb = reinterpret_cast<const char*>(smem + L::off_lut);
+        const uint32_t l4 = (uint32_t)lane << 2;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+        for (int c = 0; c < 32; ++c) {
+          const uint32_t pv = *reinterpret_cast<const uint32_t*>(lb + pair_lut_off(w[c >> 2], c & 3, l4));
+          r[c] = Act<T>::mul2(pv, sc);
+        }
+      } else {
 #pragma unroll
-        for (int p = 0; p < 4; ++p) {
-          // nibbles (4p, 16+4p) of word j are k = 8j+2p (low half), 8j+2p+1 (high half)
-          const uint32_t v = ((w[j] >> (4 * p)) & 0x000F000Fu) | Act<T>::magic;
-          r[j * 4 + p] = Act<T>::sub_mul(v, zb, sc);
+        for (int j = 0; j < 8; ++j) {
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            // nibbles (4p, 16+4p) of word j are k = 8j+2p (low half), 8j+2p+1 (high half)
+            const uint32_t v = ((w[j] >> (4 * p)) & 0x000F000Fu) | Act<T>::magic;
+            r[j * 4 + p] = Act<T>::sub_mul(v, zb, sc);
+          }
         }
       }
       tmem_st32(lane_base + kAcol + s * (kBK / 2), r);
@@ -345,12 +400,18 @@ template <> struct MmaOp<__nv_bfloat16> {
   __device__ __forceinline__ static float hi_f(uint32_t pair) { return __uint_as_float(pair & 0xFFFF0000u); }
 };
 
-template <typename T, int NT8>
+template <typename T, int NT8, bool NF>
 __global__ void __launch_bounds__(256) w4a16_gemv_kernel(const T* __restrict__ x,
                                                          const uint8_t* __restrict__ packed,
                                                          const float* __restrict__ bias,
                                                          T* __restrict__ y, W4Args a) {
   __shared__ float red[8][NT8][32][4];
+  __shared__ __align__(16) uint32_t lut[NF ? kPairLutWords : 4];
+  __shared__ uint32_t ltmp[NF ? 256 : 1];
+  if constexpr (NF) {
+    build_pair_lut<T>(lut, ltmp);
+    __syncthreads();
+  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
   const int r0 = blockIdx.x * 16;          // first weight row of the block
@@ -414,10 +475,20 @@ __global__ void __launch_bounds__(256) w4a16_gemv_kernel(const T* __restrict__ x
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
       uint32_t af[4];
-      af[0] = MmaOp<T>::sub2(((ra[2 * t] >> (4 * c)) & 0x000F000Fu) | Act<T>::magic, zb0);
-      af[1] = MmaOp<T>::sub2(((rb[2 * t] >> (4 * c)) & 0x000F000Fu) | Act<T>::magic, zb1);
-      af[2] = MmaOp<T>::sub2(((ra[2 * t + 1] >> (4 * c)) & 0x000F000Fu) | Act<T>::magic, zb0);
-      af[3] = MmaOp<T>::sub2(((rb[2 * t + 1] >> (4 * c)) & 0x000F000Fu) | Act<T>::magic, zb1);
+      if constexpr (NF) {
+        // byte c of words 2t, 2t+1 = k pairs (16t + 2c, +8): table pairs, scaled below
+        const char* lb = reinterpret_cast<const char*>(lut);
+        const uint32_t l4 = (uint32_t)lane << 2;
+        af[0] = *reinterpret_cast<const uint32_t*>(lb + ((((ra[2 * t] >> (8 * c)) & 0xFFu) << 7) | l4));
+        af[1] = *reinterpret_cast<const uint32_t*>(lb + ((((rb[2 * t] >> (8 * c)) & 0xFFu) << 7) | l4));
+        af[2] = *reinterpret_cast<const uint32_t*>(lb + ((((ra[2 * t + 1] >> (8 * c)) & 0xFFu) << 7) | l4));
+        af[3] = *reinterpret_cast<const uint32_t*>(lb + ((((rb[2 * t + 1] >> (8 * c)) & 0xFFu) << 7) | l4));
+      } else {
+        af[0] = MmaOp<T>::sub2(((ra[2 * t] >> (4 * c)) & 0x000F000Fu) | Act<T>::magic, zb0);
+        af[1] = MmaOp<T>::sub2(((rb[2 * t] >> (4 * c)) & 0x000F000Fu) | Act<T>::magic, zb1);
+        af[2] = MmaOp<T>::sub2(((ra[2 * t + 1] >> (4 * c)) & 0x000F000Fu) | Act<T>::magic, zb0);
+        af[3] = MmaOp<T>::sub2(((rb[2 * t + 1] >> (4 * c)) & 0x000F000Fu) | Act<T>::magic, zb1);
+      }
 #pragma unroll
       for (int j = 0; j < NT8; ++j) MmaOp<T>::mma(part[j], af, bx[j][t][0], bx[j][t][1]);
     }
@@ -457,7 +528,7 @@ __global__ void __launch_bounds__(256) w4a16_gemv_kernel(const T* __restrict__ x
   }
 }
 
-template <typename T>
+template <typename T, bool NF>
 int launch_gemv(const void* x, int M, int N, int K, int group, const void* packed, const float* bias,
                 void* y, cudaStream_t st) {
   W4Args a;
@@ -469,10 +540,10 @@ int launch_gemv(const void* x, int M, int N, int K, int group, const void* packe
   a.n_groups = K / group;
   const int grid = N / 16;
   if (M <= 8)
-    w4a16_gemv_kernel<T, 1><<<grid, 256, 0, st>>>(static_cast<const T*>(x), static_cast<const uint8_t*>(packed),
+    w4a16_gemv_kernel<T, 1, NF><<<grid, 256, 0, st>>>(static_cast<const T*>(x), static_cast<const uint8_t*>(packed),
                                                   bias, static_cast<T*>(y), a);
   else
-    w4a16_gemv_kernel<T, 2><<<grid, 256, 0, st>>>(static_cast<const T*>(x), static_cast<const uint8_t*>(packed),
+    w4a16_gemv_kernel<T, 2, NF><<<grid, 256, 0, st>>>(static_cast<const T*>(x), static_cast<const uint8_t*>(packed),
                                                   bias, static_cast<T*>(y), a);
   return launched("w4a16_gemv_kernel");
 }
@@ -541,11 +612,65 @@ __global__ void __launch_bounds__(256) w4a16_pack_kernel(const int8_t* __restric
   }
 }
 
+// ---------------------------------------------------------------------------
+// NF4 linear operand (QLoRALinear base weight) from the module's packed codes
+// (flattened weight, element 2i in the low nibble of byte i) and its block
+// scales:
+//   codes: [N/128][K/64][128 rows][32 bytes] in that natural nibble order, so
+//          byte c of a row's K step is the k pair (2c, 2c+1);
+//   pairs: [N/128][K/64][128 rows] (0, scale) in the activation type: the
+//          scale of the block holding the row's 64-element K step, restored
+//          from the double quantization when given (round(round(q/127)*dq) in
+//          the scales' dtype, as _dequantize_base computes it).
+// ---------------------------------------------------------------------------
+template <typename T, typename ST>
+__global__ void __launch_bounds__(256) nf4lin_pack_kernel(const uint32_t* __restrict__ codes,
+                                                          const ST* __restrict__ scales,
+                                                          const ST* __restrict__ q_scales,
+                                                          const ST* __restrict__ dq_scales,
+                                                          int64_t dq_group, int N, int K, int group,
+                                                          uint8_t* __restrict__ packed) {
+  const int n_kb = K / kBK;
+  const int64_t words = (int64_t)N * K / 8;
+  uint32_t* out = reinterpret_cast<uint32_t*>(packed);
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < words;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int j = (int)(t & 7);
+    const int64_t r0 = t >> 3;  // (nt, kb, row)
+    const int row = (int)(r0 % kRows);
+    const int64_t r1 = r0 / kRows;
+    const int kb = (int)(r1 % n_kb);
+    const int nt = (int)(r1 / n_kb);
+    const int64_t n = (int64_t)nt * kRows + row;
+    out[t] = codes[(n * K + kb * kBK + j * 8) / 8];
+  }
+  const int64_t pairs = (int64_t)N * n_kb;
+  uint32_t* pout = reinterpret_cast<uint32_t*>(packed + (int64_t)N * K / 2);
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < pairs;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int row = (int)(t % kRows);
+    const int64_t r1 = t / kRows;
+    const int kb = (int)(r1 % n_kb);
+    const int nt = (int)(r1 / n_kb);
+    const int64_t n = (int64_t)nt * kRows + row;
+    const int64_t g = (n * K + (int64_t)kb * kBK) / group;
+    const float sv = q_scales ? tmul<ST>(tdiv<ST>(Ty<ST>::to_f(q_scales[g]), 127.0f), Ty<ST>::to_f(dq_scales[g / dq_group]))
+                              : Ty<ST>::to_f(scales[g]);
+    union {
+      T h[2];
+      uint32_t u;
+    } pr;
+    pr.h[0] = Ty<T>::from_f(0.0f);
+    pr.h[1] = Ty<T>::from_f(sv);
+    pout[t] = pr.u;
+  }
+}
+
 // ---- host side ---------------------------------------------------------------
-template <typename T, int BT, int S>
+template <typename T, int BT, int S, bool NF>
 int launch_w4(const void* x, int M, int N, int K, int group, const void* packed, const float* bias,
               void* y, int* err, cudaStream_t st) {
-  using L = Smem<T, BT, S>;
+  using L = Smem<T, BT, S, NF>;
   EncodeTiledFn enc = encode_fn();
   LQ_REQUIRE(enc != nullptr, LQ_ECUDA, "cuTensorMapEncodeTiled unavailable");
   CUtensorMap map;
@@ -565,7 +690,7 @@ int launch_w4(const void* x, int M, int N, int K, int group, const void* packed,
   a.group = group;
   a.n_kb = K / kBK;
   a.n_groups = K / group;
-  auto kern = w4a16_kernel<T, BT, S>;
+  auto kern = w4a16_kernel<T, BT, S, NF>;
   // every CTA allocates all 512 tensor-memory columns: request enough shared
   // memory that only one CTA fits on an SM, so none waits in tcgen05.alloc
   const int smem_bytes = L::bytes > 117 * 1024 ? L::bytes : 117 * 1024;
@@ -584,14 +709,14 @@ int launch_w4(const void* x, int M, int N, int K, int group, const void* packed,
   return launched("w4a16_kernel");
 }
 
-template <typename T>
+template <typename T, bool NF>
 int w4_dispatch(const void* x, int M, int N, int K, int group, const void* packed,
                 const float* bias, void* y, int* err, cudaStream_t st) {
-  if (M <= 16) return launch_gemv<T>(x, M, N, K, group, packed, bias, y, st);
-  if (M <= 32) return launch_w4<T, 32, 8>(x, M, N, K, group, packed, bias, y, err, st);
-  if (M <= 64) return launch_w4<T, 64, 8>(x, M, N, K, group, packed, bias, y, err, st);
-  if (M <= 128) return launch_w4<T, 128, 6>(x, M, N, K, group, packed, bias, y, err, st);
-  return launch_w4<T, 256, 4>(x, M, N, K, group, packed, bias, y, err, st);
+  if (M <= 16) return launch_gemv<T, NF>(x, M, N, K, group, packed, bias, y, st);
+  if (M <= 32) return launch_w4<T, 32, 8, NF>(x, M, N, K, group, packed, bias, y, err, st);
+  if (M <= 64) return launch_w4<T, 64, 8, NF>(x, M, N, K, group, packed, bias, y, err, st);
+  if (M <= 128) return launch_w4<T, 128, 6, NF>(x, M, N, K, group, packed, bias, y, err, st);
+  return launch_w4<T, 256, 4, NF>(x, M, N, K, group, packed, bias, y, err, st);
 }
 
 template <typename T, typename ST>
@@ -626,10 +751,74 @@ int check_shape(int64_t N, int64_t K, int64_t group) {
   return LQ_OK;
 }
 
+template <typename T, typename ST>
+int nf4lin_pack_t(const void* codes, const void* s, const void* qs, const void* dqs, int64_t dq_group,
+                  int N, int K, int group, void* packed, cudaStream_t st) {
+  int64_t work = (int64_t)N * K / 8;
+  int grid = (int)((work + 255) / 256);
+  if (grid > num_sms() * 16) grid = num_sms() * 16;
+  nf4lin_pack_kernel<T, ST><<<grid, 256, 0, st>>>(static_cast<const uint32_t*>(codes), static_cast<const ST*>(s),
+                                                  static_cast<const ST*>(qs), static_cast<const ST*>(dqs),
+                                                  dq_group, N, K, group, static_cast<uint8_t*>(packed));
+  return launched("nf4lin_pack_kernel");
+}
+
+template <typename T>
+int nf4lin_pack_s(const void* codes, const void* s, const void* qs, const void* dqs, int sdt,
+                  int64_t dq_group, int N, int K, int group, void* packed, cudaStream_t st) {
+  switch (sdt) {
+    case LQ_F32: return nf4lin_pack_t<T, float>(codes, s, qs, dqs, dq_group, N, K, group, packed, st);
+    case LQ_F16: return nf4lin_pack_t<T, __half>(codes, s, qs, dqs, dq_group, N, K, group, packed, st);
+    case LQ_BF16: return nf4lin_pack_t<T, __nv_bfloat16>(codes, s, qs, dqs, dq_group, N, K, group, packed, st);
+    default: set_error("unsupported scale dtype %d", sdt); return LQ_EDTYPE;
+  }
+}
+
 }  // namespace
 }  // namespace lq
 
 using namespace lq;
+
+extern "C" size_t lq_nf4_linear_packed_bytes(int64_t N, int64_t K) {
+  if (N <= 0 || K <= 0) return 0;
+  return (size_t)(N * K / 2 + N * (K / kBK) * 4);
+}
+
+extern "C" int lq_nf4_linear_pack(const void* codes, const void* scales, const void* q_scales,
+                                  const void* dq_scales, int s_dtype, int64_t N, int64_t K,
+                                  int64_t group, int64_t dq_group, int act_dtype, void* packed,
+                                  void* stream) {
+  int rc = check_shape(N, K, group);
+  if (rc) return rc;
+  LQ_REQUIRE(codes && packed, LQ_EINVAL, "NULL pointer");
+  LQ_REQUIRE(scales || (q_scales && dq_scales && dq_group > 0), LQ_EINVAL,
+             "need the block scales, or q_scales + dq_scales + dq_group");
+  LQ_REQUIRE(reinterpret_cast<uintptr_t>(codes) % 4 == 0 && aligned16(packed), LQ_EALIGN,
+             "codes must be 4-byte and packed 16-byte aligned");
+  cudaStream_t st = as_stream(stream);
+  const void* s = q_scales ? nullptr : scales;
+  const void* qs = q_scales ? q_scales : nullptr;
+  const void* dqs = q_scales ? dq_scales : nullptr;
+  if (act_dtype == LQ_F16) return nf4lin_pack_s<__half>(codes, s, qs, dqs, s_dtype, dq_group, (int)N, (int)K, (int)group, packed, st);
+  if (act_dtype == LQ_BF16) return nf4lin_pack_s<__nv_bfloat16>(codes, s, qs, dqs, s_dtype, dq_group, (int)N, (int)K, (int)group, packed, st);
+  set_error("NF4 linear activations must be fp16 or bf16 (got dtype %d)", act_dtype);
+  return LQ_EDTYPE;
+}
+
+extern "C" int lq_nf4_linear(const void* x, int act_dtype, int64_t M, int64_t N, int64_t K,
+                             const void* packed, const float* bias, void* y, int* err, void* stream) {
+  int rc = check_shape(N, K, kBK);
+  if (rc) return rc;
+  LQ_REQUIRE(M >= 0 && M < (1LL << 31), LQ_EINVAL, "bad M");
+  if (M == 0) return LQ_OK;
+  LQ_REQUIRE(x && packed && y, LQ_EINVAL, "NULL pointer");
+  LQ_REQUIRE(aligned16(x) && aligned16(packed), LQ_EALIGN, "x and packed must be 16-byte aligned");
+  cudaStream_t st = as_stream(stream);
+  if (act_dtype == LQ_F16) return w4_dispatch<__half, true>(x, (int)M, (int)N, (int)K, kBK, packed, bias, y, err, st);
+  if (act_dtype == LQ_BF16) return w4_dispatch<__nv_bfloat16, true>(x, (int)M, (int)N, (int)K, kBK, packed, bias, y, err, st);
+  set_error("NF4 linear activations must be fp16 or bf16 (got dtype %d)", act_dtype);
+  return LQ_EDTYPE;
+}
 
 extern "C" size_t lq_w4a16_packed_bytes(int64_t N, int64_t K, int64_t group) {
   if (N <= 0 || K <= 0 || group <= 0) return 0;
@@ -660,8 +849,8 @@ extern "C" int lq_w4a16_linear(const void* x, int act_dtype, int64_t M, int64_t 
   LQ_REQUIRE(x && packed && y, LQ_EINVAL, "NULL pointer");
   LQ_REQUIRE(aligned16(x) && aligned16(packed), LQ_EALIGN, "x and packed must be 16-byte aligned");
   cudaStream_t st = as_stream(stream);
-  if (act_dtype == LQ_F16) return w4_dispatch<__half>(x, (int)M, (int)N, (int)K, (int)group, packed, bias, y, err, st);
-  if (act_dtype == LQ_BF16) return w4_dispatch<__nv_bfloat16>(x, (int)M, (int)N, (int)K, (int)group, packed, bias, y, err, st);
+  if (act_dtype == LQ_F16) return w4_dispatch<__half, false>(x, (int)M, (int)N, (int)K, (int)group, packed, bias, y, err, st);
+  if (act_dtype == LQ_BF16) return w4_dispatch<__nv_bfloat16, false>(x, (int)M, (int)N, (int)K, (int)group, packed, bias, y, err, st);
   set_error("W4A16 activations must be fp16 or bf16 (got dtype %d)", act_dtype);
   return LQ_EDTYPE;
 }

@@ -1,0 +1,117 @@
+"""Fused NF4 base product for QLoRALinear.forward (qlora.py:306-312).
+
+The reference's forward dequantizes the whole NF4 base weight
+(``_dequantize_base``, qlora.py:294-304) and calls ``F.linear``; with a bf16 or
+fp16 base that call fails, because the bias and the LoRA factors stay fp32.
+Here, for fp16 / bf16 activations of the base weight's dtype, the base product
+runs in one kernel that looks the NF4 codes up and applies the block scale on
+the fly (``lq_nf4_linear``: tensor cores, fp32 accumulation, the fp32 bias
+added before the one rounding), with the weights exactly those
+``_dequantize_base`` returns.  fp32 activations keep the reference's
+computation.
+
+The kernel operand (codes re-tiled + one restored scale per row and 64-wide K
+step) is built on first use and cached on the module, keyed on the storage
+and version counter of every buffer it is built from, so ``pack_base``, a
+state-dict load or an in-place edit of the scales rebuilds it.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _C
+from .core.w4a16 import _err_flag
+
+
+def _use_dq(ql) -> bool:
+    return ql.double_quant and hasattr(ql, "dq_q_scales")
+
+
+def base_dtype(ql) -> torch.dtype:
+    return (ql.dq_q_scales if _use_dq(ql) else ql.nf4_scales).dtype
+
+
+def eligible(ql, x: torch.Tensor) -> bool:
+    K, N, G = ql.in_features, ql.out_features, ql.group_size
+    return (x.is_cuda and x.dtype in (torch.float16, torch.bfloat16) and x.dtype == base_dtype(ql)
+            and x.shape[-1] == K and ql.nf4_codes_packed.is_cuda
+            and N % 128 == 0 and K % 64 == 0 and G % 64 == 0 and K % G == 0)
+
+
+def _sources(ql):
+    ts = [ql.nf4_codes_packed]
+    ts += [ql.dq_q_scales, ql.dq_scales] if _use_dq(ql) else [ql.nf4_scales]
+    return ts
+
+
+def packed_operand(ql, act_dtype: torch.dtype) -> torch.Tensor:
+    """Build (or fetch the cached) kernel operand for `act_dtype`."""
+    src = _sources(ql)
+    key = (act_dtype, src[0].device) + tuple((t.data_ptr(), t._version) for t in src)
+    cached = getattr(ql, "_nf4lin", None)
+    if cached is not None and cached[0] == key:
+        return cached[1]
+    N, K, G = ql.out_features, ql.in_features, ql.group_size
+    codes = ql.nf4_codes_packed
+    packed = torch.empty(_C.lib().lq_nf4_linear_packed_bytes(N, K), dtype=torch.uint8,
+                         device=codes.device)
+    if _use_dq(ql):
+        qs = ql.dq_q_scales.contiguous()
+        dq = ql.dq_scales.to(qs.dtype).contiguous()
+        _C.call("lq_nf4_linear_pack", codes.data_ptr(), None, qs.data_ptr(), dq.data_ptr(),
+                _C.dt(qs), N, K, G, ql._dq_gs, _C.dt(act_dtype), packed.data_ptr(),
+                _C.stream_ptr(codes))
+    else:
+        s = ql.nf4_scales.contiguous()
+        _C.call("lq_nf4_linear_pack", codes.data_ptr(), s.data_ptr(), None, None, _C.dt(s), N, K,
+                G, 0, _C.dt(act_dtype), packed.data_ptr(), _C.stream_ptr(codes))
+    ql._nf4lin = (key, packed)
+    return packed
+
+
+def _forward(ql, x: torch.Tensor, bias) -> torch.Tensor:
+    packed = packed_operand(ql, x.dtype)
+    N, K = ql.out_features, ql.in_features
+    x2 = x.reshape(-1, K)
+    if not x2.is_contiguous() or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    M = x2.shape[0]
+    y = torch.empty(M, N, dtype=x.dtype, device=x.device)
+    b = None
+    if bias is not None:
+        b = bias.detach()
+        if b.dtype != torch.float32 or not b.is_contiguous():
+            b = b.float().contiguous()
+    _C.call("lq_nf4_linear", x2.data_ptr(), _C.dt(x2), M, N, K, packed.data_ptr(), _C.ptr(b),
+            y.data_ptr(), _err_flag(x.device).data_ptr(), _C.stream_ptr(x2))
+    return y.reshape(*x.shape[:-1], N)
+
+
+class _BaseLinear(torch.autograd.Function):
+    """y = x @ W_base^T + bias; the base is frozen, so the backward returns
+    the gradients of x (through the dequantized base) and of the bias."""
+
+    @staticmethod
+    def forward(ctx, x, bias, ql):
+        ctx.ql = ql
+        return _forward(ql, x, bias)
+
+    @staticmethod
+    def backward(ctx, gy):
+        ql = ctx.ql
+        N, K = ql.out_features, ql.in_features
+        g2 = gy.reshape(-1, N)
+        gx = gb = None
+        if ctx.needs_input_grad[0]:
+            gx = (g2 @ ql._dequantize_base().to(gy.dtype)).reshape(*gy.shape[:-1], K)
+        if ctx.needs_input_grad[1]:
+            gb = g2.float().sum(0)
+        return gx, gb, None
+
+
+def base_linear(ql, x: torch.Tensor) -> torch.Tensor:
+    """The fused base product (+ bias) of QLoRALinear for eligible x."""
+    if torch.is_grad_enabled() and (x.requires_grad or (ql.bias is not None and ql.bias.requires_grad)):
+        return _BaseLinear.apply(x, ql.bias, ql)
+    return _forward(ql, x, ql.bias)

@@ -277,6 +277,15 @@ class QLoRALinear(nn.Module):
         return out
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        """qlora.py:306-312.  fp16 / bf16 activations of the base weight's dtype
+        take the fused NF4 kernel for the base product (the reference fails
+        there: its bias and LoRA factors stay fp32), with the LoRA path in the
+        activations' dtype; other inputs follow the reference exactly."""
+        from . import nf4_linear
+        if nf4_linear.eligible(self, x):
+            out = nf4_linear.base_linear(self, x)
+            lora = F.linear(F.linear(x, self.lora_A.to(x.dtype)), self.lora_B.to(x.dtype))
+            return out + lora * self.scaling
         w_base = self._dequantize_base()
         out = F.linear(x, w_base, self.bias)
         out = out + F.linear(F.linear(x, self.lora_A), self.lora_B) * self.scaling

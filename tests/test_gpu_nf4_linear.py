@@ -1,0 +1,114 @@
+"""GPU tests of the fused NF4 base product of QLoRALinear.forward
+(qlora.py:306-312) for fp16 / bf16 activations.
+
+The reference's forward computes F.linear(x, _dequantize_base(), bias) plus
+the LoRA term; with a half-precision base that call raises (its bias and LoRA
+factors are fp32), so the oracle here is the same sum computed in fp32 from
+the module's own dequantized base weight (which the QLoRA tests pin bit for
+bit against the reference).  Tolerance, as for QuantizedLinear's W4A16
+forward: max |y - y_ref| <= 1e-2 * max |y_ref|.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def L():
+    import llm_quant_b200
+    return llm_quant_b200
+
+
+def _module(L, N, K, dtype, gs, dq, seed, rank=8):
+    g = torch.Generator().manual_seed(seed)
+    w = (torch.randn(N, K, generator=g) * 0.02).to(dtype).cuda()
+    ql = L.QLoRALinear(K, N, rank=rank, group_size=gs, double_quant=dq).cuda()
+    with torch.no_grad():
+        ql.lora_B.copy_(torch.randn(N, rank, generator=g) * 0.05)
+        ql.bias.copy_(torch.randn(N, generator=g) * 0.1)
+    ql.pack_base(w)
+    return ql, g
+
+
+def _reference(ql, x):
+    w = ql._dequantize_base().float()
+    xf = x.float()
+    return (xf @ w.T + ql.bias.float()
+            + (xf @ ql.lora_A.float().T) @ ql.lora_B.float().T * ql.scaling)
+
+
+def _check(y, ref):
+    err = (y.float() - ref).abs().max().item()
+    assert err <= 1e-2 * ref.abs().max().item() + 1e-3, (err, ref.abs().max().item())
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("N,K,gs,dq", [(128, 64, 64, True), (256, 128, 64, False),
+                                       (384, 4096, 64, True), (128, 512, 128, True)])
+@pytest.mark.parametrize("M", [1, 3, 8, 9, 16, 17, 64, 100, 300])
+def test_fused_forward_matches_fp32_reference(L, dtype, N, K, gs, dq, M):
+    ql, g = _module(L, N, K, dtype, gs, dq, seed=N + K + M)
+    x = torch.randn(M, K, generator=g).to(dtype).cuda()
+    from llm_quant_b200 import nf4_linear
+    assert nf4_linear.eligible(ql, x)
+    y = ql(x)
+    assert y.dtype == dtype and y.shape == (M, N)
+    _check(y, _reference(ql, x))
+
+
+def test_fused_forward_3d_input_and_no_bias(L):
+    g = torch.Generator().manual_seed(5)
+    w = (torch.randn(256, 256, generator=g) * 0.02).to(torch.bfloat16).cuda()
+    ql = L.QLoRALinear(256, 256, rank=4, group_size=64, bias=False).cuda()
+    ql.pack_base(w)
+    x = torch.randn(2, 7, 256, generator=g).to(torch.bfloat16).cuda()
+    y = ql(x)
+    assert y.shape == (2, 7, 256)
+    w_ = ql._dequantize_base().float()
+    ref = x.float() @ w_.T  # lora_B is zero-initialised
+    _check(y, ref)
+
+
+def test_gradients_flow(L):
+    ql, g = _module(L, 256, 512, torch.bfloat16, 64, True, seed=11)
+    x = torch.randn(33, 512, generator=g).to(torch.bfloat16).cuda().requires_grad_(True)
+    y = ql(x)
+    gy = torch.randn_like(y)
+    y.backward(gy)
+    assert x.grad is not None and ql.lora_A.grad is not None and ql.lora_B.grad is not None
+    assert ql.bias.grad is not None
+    np.testing.assert_allclose(ql.bias.grad.cpu().numpy(), gy.float().sum(0).cpu().numpy(),
+                               rtol=1e-5, atol=1e-4)
+    # x.grad against the fp32 chain rule of the same forward
+    w = ql._dequantize_base().float()
+    lora_w = (ql.lora_B.float() @ ql.lora_A.float()) * ql.scaling
+    ref = gy.float() @ (w + lora_w)
+    _check(x.grad, ref)
+
+
+def test_operand_rebuilt_after_repack(L):
+    ql, g = _module(L, 128, 256, torch.bfloat16, 64, True, seed=21)
+    x = torch.randn(20, 256, generator=g).to(torch.bfloat16).cuda()
+    y1 = ql(x)
+    w2 = (torch.randn(128, 256, generator=g) * 0.05).to(torch.bfloat16).cuda()
+    ql.pack_base(w2)
+    y2 = ql(x)
+    _check(y2, _reference(ql, x))
+    assert not torch.equal(y1, y2)
+
+
+def test_fp32_path_is_the_reference_computation(L):
+    g = torch.Generator().manual_seed(3)
+    w = torch.randn(128, 64, generator=g).cuda() * 0.02
+    ql = L.QLoRALinear(64, 128, rank=4, group_size=64).cuda()
+    ql.pack_base(w)
+    x = torch.randn(5, 64, generator=g).cuda()
+    from llm_quant_b200 import nf4_linear
+    assert not nf4_linear.eligible(ql, x)
+    wb = ql._dequantize_base()
+    ref = torch.nn.functional.linear(x, wb, ql.bias) + torch.nn.functional.linear(
+        torch.nn.functional.linear(x, ql.lora_A), ql.lora_B) * ql.scaling
+    assert torch.equal(ql(x), ref)
