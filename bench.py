@@ -722,7 +722,7 @@ class W4A16Workload:
                 c[0] += 1
             t = cuda_time_ms(self.ctx.torch, f, 4 * self.LAYERS)
             wbytes = self.N * self.K / 2 + self.N * (self.K // 128) * 4
-            kname = "w4a16_gemv_kernel" if m <= 16 else "w4a16_kernel"
+            kname = "w4a16_gemv_kernel" if m <= 8 else "w4a16_kernel"
             out[f"{kname} M={m}"] = (self.flops(m), t, m, wbytes + 2 * m * self.K + 2 * m * self.N)
         return out
 
@@ -831,7 +831,7 @@ class QLoRALinearWorkload(W4A16Workload):
                 c[0] += 1
             t = cuda_time_ms(self.ctx.torch, f, 4 * self.LAYERS)
             wbytes = self.N * self.K / 2 + self.N * (self.K // 64) * 4
-            kname = "nf4_linear_gemv_kernel" if m <= 16 else "nf4_linear_kernel"
+            kname = "nf4_linear_gemv_kernel" if m <= 8 else "nf4_linear_kernel"
             out[f"{kname} M={m}"] = (self.flops(m), t, m, wbytes + 2 * m * self.K + 2 * m * self.N)
         return out
 

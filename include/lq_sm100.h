@@ -252,8 +252,8 @@ int lq_hadamard_fake_quant(const void* x, int dtype, int64_t rows, int64_t d, in
  * the activation dtype.
  * lq_w4a16_linear: y[M, N] = x[M, K] @ dequant(W)^T + bias, x / y in act_dtype
  * (LQ_F16 or LQ_BF16), bias fp32 [N] or NULL, fp32 accumulation on the tensor
- * cores (M > 16: tcgen05.mma, A = weights dequantized into tensor memory, B =
- * activations by TMA; M <= 16: a weight-streaming mma.sync kernel).
+ * cores (M > 8: tcgen05.mma, A = weights dequantized into tensor memory, B =
+ * activations by TMA; M <= 8: a weight-streaming mma.sync kernel).
  * Requires N % 128 == 0, K % 64 == 0, group % 64 == 0.
  * err (device int, may be NULL) receives a non-zero code if a bounded
  * device-side wait ran out (the kernel then returns early). */
@@ -285,6 +285,18 @@ int lq_nf4_linear_pack(const void* codes, const void* scales, const void* q_scal
                        int64_t dq_group, int act_dtype, void* packed, void* stream);
 int lq_nf4_linear(const void* x, int act_dtype, int64_t M, int64_t N, int64_t K,
                   const void* packed, const float* bias, void* y, int* err, void* stream);
+
+/* ---- SpQR outliers (replaces the outlier restore of SpQRLinear.forward, spqr.py:191-193)
+ * With the int part of the weight done by lq_w4a16_linear, the fp outliers are a
+ * sparse correction C (outlier minus dequantized int weight at each masked
+ * position) stored by rows: row_ids[n_rows] (int32), row_ptr[n_rows + 1]
+ * (int32), cols[nnz] (int32), vals[nnz] (fp32).  lq_sparse_row_add adds it:
+ * y[m, row_ids[r]] += sum_j x[m, cols[j]] * vals[j] over j in
+ * [row_ptr[r], row_ptr[r+1]), summed in fp32 and rounded once into y.
+ * x [M, K] and y [M, N] row-major in dtype (LQ_F32 / LQ_F16 / LQ_BF16). */
+int lq_sparse_row_add(const void* x, int dtype, int64_t M, int64_t K, int64_t N,
+                      const int32_t* row_ptr, const int32_t* row_ids, int64_t n_rows,
+                      const int32_t* cols, const float* vals, void* y, void* stream);
 
 #ifdef __cplusplus
 }

@@ -67,6 +67,7 @@ _SIGS = {
     "lq_w4a16_linear": [_V, _I, _L, _L, _L, _L, _V, _V, _V, _V, _V],
     "lq_nf4_linear_pack": [_V, _V, _V, _V, _I, _L, _L, _L, _L, _I, _V, _V],
     "lq_nf4_linear": [_V, _I, _L, _L, _L, _V, _V, _V, _V, _V],
+    "lq_sparse_row_add": [_V, _I, _L, _L, _L, _V, _V, _L, _V, _V, _V, _V],
 }
 _SIZE_SIGS = {
     "lq_tensor_qparams_workspace_size": [_L],

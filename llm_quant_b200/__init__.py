@@ -42,6 +42,8 @@ from .kv_cache_quant import (
     PerTokenKVCacheQuantizer, PerChannelKVCacheQuantizer,
     PerGroupKVCacheQuantizer, kv_cache_memory_ratio,
 )
+from .gptq import GPTQLinear
+from .spqr import SpQRLinear
 
 __all__ = [
     "QScheme", "ste_round", "compute_qparams",
@@ -54,15 +56,17 @@ __all__ = [
     "KVQuantGranularity", "KVCacheQuantizer", "QuantizedKVCache",
     "PerTokenKVCacheQuantizer", "PerChannelKVCacheQuantizer",
     "PerGroupKVCacheQuantizer", "kv_cache_memory_ratio",
+    "GPTQLinear", "SpQRLinear",
     "install_as_llm_quant",
 ]
 
 
 def install_as_llm_quant() -> None:
-    """Make ``import llm_quant[.core[.quantizer|.rotation]|.qlora|.kv_cache_quant]``
-    resolve to this package (for code and tests written against the reference)."""
+    """Make ``import llm_quant[.core[.quantizer|.rotation]|.qlora|.kv_cache_quant|
+    .gptq|.spqr]`` resolve to this package (for code and tests written against the
+    reference; of gptq / spqr only the layers are here)."""
     import sys
-    from . import core, qlora, kv_cache_quant
+    from . import core, qlora, kv_cache_quant, gptq, spqr
     from .core import quantizer, rotation
     mod = sys.modules[__name__]
     sys.modules["llm_quant"] = mod
@@ -71,3 +75,5 @@ def install_as_llm_quant() -> None:
     sys.modules["llm_quant.core.rotation"] = rotation
     sys.modules["llm_quant.qlora"] = qlora
     sys.modules["llm_quant.kv_cache_quant"] = kv_cache_quant
+    sys.modules["llm_quant.gptq"] = gptq
+    sys.modules["llm_quant.spqr"] = spqr

@@ -307,6 +307,38 @@ def fake_quantize(
 # QuantizedLinear
 # ──────────────────────────────────────────────────────────────────────────────
 
+def int_weight_fp32(m, what: str) -> torch.Tensor:
+    """``(weight_int.float() - zero_point) * scale`` per group of the input dim
+    (or per row when group_size <= 0), in fp32 -- the weight the forward of
+    QuantizedLinear / GPTQLinear / SpQRLinear builds before F.linear
+    (core/quantizer.py:264-279, gptq.py:302-314, spqr.py:172-189)."""
+    _C.require_cuda(m.weight_int, m.scale, m.zero_point, what=what)
+    N, K = m.out_features, m.in_features
+    wi = m.weight_int.contiguous()
+    s = m.scale.reshape(N, -1).contiguous()
+    z = m.zero_point.reshape(N, -1)
+    z = (z.to(s.dtype) if z.dtype != s.dtype else z).contiguous()
+    out = torch.empty(N, K, dtype=torch.float32, device=wi.device)
+    if m.group_size > 0:
+        ng = s.shape[1]
+        tg = m.group_size
+    else:
+        ng, tg = 1, K
+    _C.call("lq_kv_dequant", wi.data_ptr(), _C.I8, N, K, 1, K, 2, tg, s.data_ptr(),
+            z.data_ptr(), _C.dt(s), ng, out.data_ptr(), _C.stream_ptr(wi))
+    return out
+
+
+def int_linear_forward(m, x: torch.Tensor) -> torch.Tensor:
+    """Forward of an int-weight linear: the fused W4A16 kernel for fp16 / bf16
+    activations when the layout allows it, else the reference's fp32
+    dequantize + F.linear."""
+    from . import w4a16
+    if w4a16.eligible(m, x):
+        return w4a16.linear(m, x)
+    return F.linear(x, int_weight_fp32(m, type(m).__name__), m.bias)
+
+
 class QuantizedLinear(nn.Module):
     """Drop-in ``nn.Linear`` replacement storing INT weights (core/quantizer.py:192-301).
 
@@ -384,30 +416,14 @@ class QuantizedLinear(nn.Module):
 
     def dequantized_weight(self) -> torch.Tensor:
         """The fp32 weight the reference's forward builds (core/quantizer.py:264-279)."""
-        _C.require_cuda(self.weight_int, self.scale, self.zero_point, what="QuantizedLinear")
-        N, K = self.out_features, self.in_features
-        wi = self.weight_int.contiguous()
-        s = self.scale.contiguous()
-        z = self.zero_point.to(s.dtype).contiguous() if self.zero_point.dtype != s.dtype else self.zero_point.contiguous()
-        out = torch.empty(N, K, dtype=torch.float32, device=wi.device)
-        if self.group_size > 0:
-            ng = s.shape[1]
-            tg = self.group_size
-        else:
-            ng, tg = 1, K
-        _C.call("lq_kv_dequant", wi.data_ptr(), _C.I8, N, K, 1, K, 2, tg, s.data_ptr(),
-                z.data_ptr(), _C.dt(s), ng, out.data_ptr(), _C.stream_ptr(wi))
-        return out
+        return int_weight_fp32(self, "QuantizedLinear")
 
     def _w4a16_eligible(self, x: torch.Tensor) -> bool:
         from . import w4a16
         return w4a16.eligible(self, x)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        if self._w4a16_eligible(x):
-            from . import w4a16
-            return w4a16.linear(self, x)
-        return F.linear(x, self.dequantized_weight(), self.bias)
+        return int_linear_forward(self, x)
 
     @classmethod
     def from_linear(cls, linear: nn.Linear, n_bits: int = 8,

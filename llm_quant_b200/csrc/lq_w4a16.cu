@@ -187,6 +187,9 @@ __global__ void __launch_bounds__(192, 1) w4a16_kernel(const __grid_constant__ C
                                                        T* __restrict__ y, W4Args a,
                                                        int* __restrict__ err) {
   using L = Smem<T, BT, S, NF>;
+  static_assert(BT % 16 == 0 && BT <= kAcol && kAcol + S * (kBK / 2) <= (int)kTmemCols,
+                "accumulator and A slots must fit tensor memory without overlap");
+  static_assert(L::bytes <= 227 * 1024, "shared memory per CTA");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::off_bar);
@@ -355,9 +358,11 @@ __global__ void __launch_bounds__(192, 1) w4a16_kernel(const __grid_constant__ C
 }
 
 // ---------------------------------------------------------------------------
-// Small M (M <= 16 tokens): the forward is a weight-streaming GEMV, bound by
-// HBM; a 128 x BT tensor-memory tile would sit mostly idle.  A block of 8
-// warps owns 16 weight rows; warp w takes the K steps w, w + 8, ... and runs
+// Small M (M <= 8 tokens): the forward is a weight-streaming GEMV, bound by
+// HBM; a 128 x BT tensor-memory tile would sit mostly idle.  A block of
+// kGemvWarps warps owns 16 weight rows (small enough that every block of the
+// grid is resident at once); warp w takes the K steps w, w + kGemvWarps, ...
+// (the next one's loads issued before the current one is used) and runs
 // mma.sync.m16n8k16 (f32 accumulate) with the weights as the A operand and up
 // to 8 tokens per B tile.  The A fragment of a lane is (rows g, g+8) x (k
 // pairs 2c, 2c+8) of each 16-wide k tile (g = lane / 4, c = lane % 4), which
@@ -365,8 +370,8 @@ __global__ void __launch_bounds__(192, 1) w4a16_kernel(const __grid_constant__ C
 // rows: one shift, one LOP3 with the magic exponent and one subtraction of
 // (magic + zero) give (q - zero) exactly in T.  The scale of the row's group
 // multiplies each K step's partial sums (sum_k (q - zero) * x) in fp32, so
-// the weights enter the MMA exactly; the eight warps' partial sums are added
-// in shared memory.
+// the weights enter the MMA exactly; the warps' partial sums are added in
+// shared memory.
 // ---------------------------------------------------------------------------
 template <typename T> struct MmaOp;
 template <> struct MmaOp<__half> {
@@ -400,12 +405,14 @@ template <> struct MmaOp<__nv_bfloat16> {
   __device__ __forceinline__ static float hi_f(uint32_t pair) { return __uint_as_float(pair & 0xFFFF0000u); }
 };
 
+constexpr int kGemvWarps = 4;  // warps per block = K split of a 16-row group
+
 template <typename T, int NT8, bool NF>
-__global__ void __launch_bounds__(256) w4a16_gemv_kernel(const T* __restrict__ x,
+__global__ void __launch_bounds__(32 * kGemvWarps) w4a16_gemv_kernel(const T* __restrict__ x,
                                                          const uint8_t* __restrict__ packed,
                                                          const float* __restrict__ bias,
                                                          T* __restrict__ y, W4Args a) {
-  __shared__ float red[8][NT8][32][4];
+  __shared__ float red[kGemvWarps][NT8][32][4];
   __shared__ __align__(16) uint32_t lut[NF ? kPairLutWords : 4];
   __shared__ uint32_t ltmp[NF ? 256 : 1];
   if constexpr (NF) {
@@ -449,10 +456,10 @@ __global__ void __launch_bounds__(256) w4a16_gemv_kernel(const T* __restrict__ x
     z1 = __ldg(pr + (size_t)grp * kRows + rit + 8);
   };
   if (warp < a.n_kb) load_step(warp, w0, w1, w2, w3, zs0, zs1);
-  for (int kb = warp; kb < a.n_kb; kb += 8) {
+  for (int kb = warp; kb < a.n_kb; kb += kGemvWarps) {
     uint4 n0 = w0, n1 = w1, n2 = w2, n3 = w3;
     uint32_t nz0 = zs0, nz1 = zs1;
-    if (kb + 8 < a.n_kb) load_step(kb + 8, n0, n1, n2, n3, nz0, nz1);
+    if (kb + kGemvWarps < a.n_kb) load_step(kb + kGemvWarps, n0, n1, n2, n3, nz0, nz1);
     const uint32_t zb0 = __byte_perm(zs0, zs0, 0x1010), zb1 = __byte_perm(zs1, zs1, 0x1010);
     const uint32_t ra[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
     const uint32_t rb[8] = {w2.x, w2.y, w2.z, w2.w, w3.x, w3.y, w3.z, w3.w};
@@ -514,11 +521,11 @@ __global__ void __launch_bounds__(256) w4a16_gemv_kernel(const T* __restrict__ x
     for (int i = 0; i < 4; ++i) red[warp][j][lane][i] = acc[j][i];
   __syncthreads();
   // thread -> (j, lane, i) of the fragment; 32 * 4 * NT8 <= 256 outputs
-  if (threadIdx.x < 32 * 4 * NT8) {
-    const int i = threadIdx.x & 3, ln = (threadIdx.x >> 2) & 31, j = threadIdx.x >> 7;
+  for (int o = threadIdx.x; o < 32 * 4 * NT8; o += blockDim.x) {
+    const int i = o & 3, ln = (o >> 2) & 31, j = o >> 7;
     float s = 0.0f;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) s += red[w][j][ln][i];
+    for (int w = 0; w < kGemvWarps; ++w) s += red[w][j][ln][i];
     const int row = r0 + (ln >> 2) + (i >= 2 ? 8 : 0);
     const int tok = 8 * j + 2 * (ln & 3) + (i & 1);
     if (tok < a.M) {
@@ -540,10 +547,10 @@ int launch_gemv(const void* x, int M, int N, int K, int group, const void* packe
   a.n_groups = K / group;
   const int grid = N / 16;
   if (M <= 8)
-    w4a16_gemv_kernel<T, 1, NF><<<grid, 256, 0, st>>>(static_cast<const T*>(x), static_cast<const uint8_t*>(packed),
+    w4a16_gemv_kernel<T, 1, NF><<<grid, 32 * kGemvWarps, 0, st>>>(static_cast<const T*>(x), static_cast<const uint8_t*>(packed),
                                                   bias, static_cast<T*>(y), a);
   else
-    w4a16_gemv_kernel<T, 2, NF><<<grid, 256, 0, st>>>(static_cast<const T*>(x), static_cast<const uint8_t*>(packed),
+    w4a16_gemv_kernel<T, 2, NF><<<grid, 32 * kGemvWarps, 0, st>>>(static_cast<const T*>(x), static_cast<const uint8_t*>(packed),
                                                   bias, static_cast<T*>(y), a);
   return launched("w4a16_gemv_kernel");
 }
@@ -709,14 +716,38 @@ int launch_w4(const void* x, int M, int N, int K, int group, const void* packed,
   return launched("w4a16_kernel");
 }
 
+// Token-tile width for M > 128: one CTA per SM runs one 128 x BT tile at a
+// time, so a launch takes ceil(tiles / SMs) waves of time proportional to
+// BT; pick the width with the least waves * BT (M = 1024 on 148 SMs: 224
+// gives 560 tiles in 4 waves, 256 would give 448 tiles, also 4 waves).
+inline int pick_bt(int M, int N) {
+  const int sms = num_sms();
+  int best = 256;
+  int64_t best_cost = INT64_MAX;
+  for (int bt : {256, 224, 192}) {
+    const int64_t tiles = (int64_t)(N / kRows) * ((M + bt - 1) / bt);
+    const int64_t cost = (tiles + sms - 1) / sms * bt;
+    if (cost < best_cost) { best_cost = cost; best = bt; }
+  }
+  return best;
+}
+
+// Stages: as many 64-wide K steps in flight as shared memory allows (the
+// NF4 variant also holds its 33 KB pair table).
 template <typename T, bool NF>
 int w4_dispatch(const void* x, int M, int N, int K, int group, const void* packed,
                 const float* bias, void* y, int* err, cudaStream_t st) {
-  if (M <= 16) return launch_gemv<T, NF>(x, M, N, K, group, packed, bias, y, st);
+  if (M <= 8) return launch_gemv<T, NF>(x, M, N, K, group, packed, bias, y, st);
+  if (M <= 16) return launch_w4<T, 16, 8, NF>(x, M, N, K, group, packed, bias, y, err, st);
   if (M <= 32) return launch_w4<T, 32, 8, NF>(x, M, N, K, group, packed, bias, y, err, st);
   if (M <= 64) return launch_w4<T, 64, 8, NF>(x, M, N, K, group, packed, bias, y, err, st);
-  if (M <= 128) return launch_w4<T, 128, 6, NF>(x, M, N, K, group, packed, bias, y, err, st);
-  return launch_w4<T, 256, 4, NF>(x, M, N, K, group, packed, bias, y, err, st);
+  if (M <= 128) return launch_w4<T, 128, 8, NF>(x, M, N, K, group, packed, bias, y, err, st);
+  constexpr int S = NF ? 5 : 6;
+  switch (pick_bt(M, N)) {
+    case 224: return launch_w4<T, 224, S, NF>(x, M, N, K, group, packed, bias, y, err, st);
+    case 192: return launch_w4<T, 192, S, NF>(x, M, N, K, group, packed, bias, y, err, st);
+    default: return launch_w4<T, 256, S, NF>(x, M, N, K, group, packed, bias, y, err, st);
+  }
 }
 
 template <typename T, typename ST>

@@ -280,6 +280,36 @@ def quantized_linear_quantize_weights(w, dt, n_bits=8, symmetric=True, group_siz
     return to_int(q, np.int8), scale.reshape(out_f, -1), zp.reshape(out_f, -1)
 
 
+def gptq_linear_pack(w_q, w, dt, n_bits=4, symmetric=True, group_size=128):
+    """GPTQLinear.pack (gptq.py:285-299): the given codes as int8, the qparams
+    of the original weight.  Returns (weight_int, scale, zero_point)."""
+    w = np.asarray(w, np.float32)
+    out_f = w.shape[0]
+    scheme = "per_group" if group_size > 0 else "per_channel"
+    scale, zp = compute_qparams(w, dt, n_bits, symmetric, scheme, group_size)
+    wi = np.asarray(w_q).astype(np.int64).astype(np.int8)
+    return wi, scale.reshape(out_f, -1), zp.reshape(out_f, -1)
+
+
+def spqr_linear_pack(w, mask, dt, n_bits=4, group_size=128):
+    """SpQRLinear.pack (spqr.py:128-170): outliers kept in fp (mask order),
+    the rest quantized symmetrically with the outliers zeroed.  Returns
+    (weight_int, scale, zero_point, outlier_vals)."""
+    w = np.asarray(w, np.float32)
+    mask = np.asarray(mask, bool)
+    vals = w[mask].astype(np.float32)
+    w0 = np.where(mask, np.float32(0.0), w).astype(np.float32)
+    wi, scale, zp = quantized_linear_quantize_weights(w0, dt, n_bits, True, group_size)
+    return wi, scale, zp, vals
+
+
+def spqr_linear_dequant_weight(weight_int, scale, sdt, zp, zdt, group_size, in_features, mask, vals):
+    """The fp32 weight SpQRLinear.forward builds (spqr.py:172-193)."""
+    w = quantized_linear_dequant_weight(weight_int, scale, sdt, zp, zdt, group_size, in_features).copy()
+    w[np.asarray(mask, bool)] = np.asarray(vals, np.float32)
+    return w
+
+
 def quantized_linear_dequant_weight(weight_int, scale, sdt, zp, zdt, group_size, in_features):
     """The fp32 weight QuantizedLinear.forward builds (core/quantizer.py:264-279)."""
     wi = np.asarray(weight_int, np.float32)

@@ -437,9 +437,58 @@ def gen_grad(ref):
     st.save("grad.npz")
 
 
+def gen_layers(ref):
+    """GPTQLinear / SpQRLinear (gptq.py:257-325, spqr.py:102-208): buffers after
+    pack, forward on seeded x, and the dequantized weight the forward builds,
+    read out exactly as layer(I) = W^T (bias-free copies)."""
+    from llm_quant.gptq import GPTQLinear
+    from llm_quant.spqr import SpQRLinear
+    st = Store()
+    g = torch.Generator().manual_seed(777)
+    for i, (inf_, outf, bits, sym, gs) in enumerate([(64, 16, 4, True, 32), (32, 16, 4, True, 0),
+                                                     (200, 24, 4, False, 128), (128, 32, 3, True, 64),
+                                                     (256, 128, 4, False, 64)]):
+        W = torch.randn(outf, inf_, generator=g)
+        lo, hi = (-(2 ** (bits - 1)), 2 ** (bits - 1) - 1) if sym else (0, 2 ** bits - 1)
+        w_q = torch.randint(lo, hi + 1, (outf, inf_), generator=g)
+        ql = GPTQLinear(inf_, outf, n_bits=bits, symmetric=sym, group_size=gs, bias=True)
+        ql.pack(w_q, W)
+        with torch.no_grad():
+            ql.bias.copy_(torch.randn(outf, generator=g) * 0.1)
+        x = torch.randn(5, inf_, generator=g)
+        y = ql(x)
+        nb = GPTQLinear(inf_, outf, n_bits=bits, symmetric=sym, group_size=gs, bias=False)
+        nb.pack(w_q, W)
+        wT = nb(torch.eye(inf_))
+        st.add(f"gptq{i}", dict(fn="gptq", in_features=inf_, out_features=outf, n_bits=bits,
+                                symmetric=sym, group_size=gs),
+               W=W, w_q=w_q.to(torch.int8), weight_int=ql.weight_int, scale=ql.scale,
+               zero_point=ql.zero_point, bias=ql.bias.data, x=x, y=y, wT=wT)
+    for i, (inf_, outf, bits, gs, frac) in enumerate([(64, 32, 4, 32, 0.02), (32, 16, 8, 0, 0.05),
+                                                      (200, 24, 4, 128, 0.01), (256, 128, 4, 64, 0.01)]):
+        W = torch.randn(outf, inf_, generator=g)
+        mask = torch.rand(outf, inf_, generator=g) < frac
+        mask[0, 0] = True
+        layer = SpQRLinear(inf_, outf, n_bits=bits, group_size=gs, bias=True)
+        layer.pack(W, mask)
+        with torch.no_grad():
+            layer.bias.copy_(torch.randn(outf, generator=g) * 0.1)
+        x = torch.randn(5, inf_, generator=g)
+        y = layer(x)
+        nb = SpQRLinear(inf_, outf, n_bits=bits, group_size=gs, bias=False)
+        nb.pack(W, mask)
+        wT = nb(torch.eye(inf_))
+        st.add(f"spqr{i}", dict(fn="spqr", in_features=inf_, out_features=outf, n_bits=bits,
+                                group_size=gs, sparsity=layer.sparsity),
+               W=W, mask=mask.to(torch.uint8), weight_int=layer.weight_int, scale=layer.scale,
+               zero_point=layer.zero_point, outlier_vals=layer.outlier_vals, bias=layer.bias.data,
+               x=x, y=y, wT=wT)
+    st.save("layers.npz")
+
+
 if __name__ == "__main__":
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     ref = _import_reference()
-    which = sys.argv[1:] or ["quantizer", "rotation", "nf4", "kv", "grad"]
+    which = sys.argv[1:] or ["quantizer", "rotation", "nf4", "kv", "grad", "layers"]
     for name in which:
         globals()[f"gen_{name}"](ref)

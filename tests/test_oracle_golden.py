@@ -177,3 +177,28 @@ def test_kv_cache_mixed_granularity():
     for j in range(3):
         fk, fv = cache.update(0, _p(c, f"k{j}"), _p(c, f"v{j}"))
         assert same_bits(fk, _p(c, f"fk{j}")) and same_bits(fv, _p(c, f"fv{j}"))
+
+
+@pytest.mark.parametrize("name,c", list(cases("layers.npz", "gptq")), ids=lambda v: v if isinstance(v, str) else "")
+def test_oracle_gptq_linear(name, c):
+    p = c["params"]
+    wi, s, z = O.gptq_linear_pack(c["w_q"][0], c["W"][0], "float32", p["n_bits"], p["symmetric"],
+                                  p["group_size"])
+    assert np.array_equal(wi, c["weight_int"][0])
+    assert same_bits(s, c["scale"][0]) and same_bits(z, c["zero_point"][0])
+    w = O.quantized_linear_dequant_weight(wi, s, "float32", z, "float32", p["group_size"],
+                                          p["in_features"])
+    assert same_bits(w.T, c["wT"][0])
+
+
+@pytest.mark.parametrize("name,c", list(cases("layers.npz", "spqr")), ids=lambda v: v if isinstance(v, str) else "")
+def test_oracle_spqr_linear(name, c):
+    p = c["params"]
+    mask = c["mask"][0].astype(bool)
+    wi, s, z, vals = O.spqr_linear_pack(c["W"][0], mask, "float32", p["n_bits"], p["group_size"])
+    assert np.array_equal(wi, c["weight_int"][0])
+    assert same_bits(s, c["scale"][0]) and same_bits(z, c["zero_point"][0])
+    assert same_bits(vals, c["outlier_vals"][0])
+    w = O.spqr_linear_dequant_weight(wi, s, "float32", z, "float32", p["group_size"],
+                                     p["in_features"], mask, vals)
+    assert same_bits(w.T, c["wT"][0])
