@@ -704,7 +704,7 @@ __global__ void __launch_bounds__(256) nf4_dequant_kernel(const void* __restrict
 // round_T(fp32 product) because the product of two 8- or 11-bit significands
 // is exact in fp32.  The 256-entry table is stored 32 times, entry b of copy
 // r at word 32 b + r, and lane l reads copy l: no bank conflicts.
-constexpr int kUnpackK = 4;  // chunks per lane per warp iteration
+constexpr int kUnpackK = 8;  // chunks per lane per warp iteration
 
 template <typename T>
 __global__ void __launch_bounds__(256) nf4_unpack_vec_kernel(const uint32_t* __restrict__ codes,

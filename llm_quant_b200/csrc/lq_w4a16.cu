@@ -717,17 +717,18 @@ int launch_w4(const void* x, int M, int N, int K, int group, const void* packed,
 }
 
 // Token-tile width for M > 128: one CTA per SM runs one 128 x BT tile at a
-// time, so a launch takes ceil(tiles / SMs) waves of time proportional to
-// BT; pick the width with the least waves * BT (M = 1024 on 148 SMs: 224
-// gives 560 tiles in 4 waves, 256 would give 448 tiles, also 4 waves).
+// time and a tile's time is dominated by its 64-wide K steps, whose cost
+// hardly depends on BT (measured: 1.1k cycles per step at BT = 256 and 192),
+// so a launch costs about ceil(tiles / SMs) waves; take the widest tile
+// among those with the fewest waves.
 inline int pick_bt(int M, int N) {
   const int sms = num_sms();
   int best = 256;
-  int64_t best_cost = INT64_MAX;
+  int64_t best_waves = INT64_MAX;
   for (int bt : {256, 224, 192}) {
     const int64_t tiles = (int64_t)(N / kRows) * ((M + bt - 1) / bt);
-    const int64_t cost = (tiles + sms - 1) / sms * bt;
-    if (cost < best_cost) { best_cost = cost; best = bt; }
+    const int64_t waves = (tiles + sms - 1) / sms;
+    if (waves < best_waves) { best_waves = waves; best = bt; }
   }
   return best;
 }
