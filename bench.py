@@ -341,12 +341,16 @@ class NF4Workload:
         from llm_quant_b200.sharded import flatten_bytes, gather_to_rank0
         flat = flatten_bytes([t for m in self.mods for t in
                               (m.nf4_codes_packed, m.nf4_scales, m.dq_q_scales, m.dq_scales)])
+        # NCCL sets up the gather's peer connections on first use: warm them up
+        gather_to_rank0(torch.zeros(1 << 20, dtype=torch.uint8, device=flat.device))
         torch.cuda.synchronize()
         self.ctx.barrier()
-        t0 = time.perf_counter()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
         gather_to_rank0(flat)
+        e1.record()
         torch.cuda.synchronize()
-        return (time.perf_counter() - t0) * 1e3, flat.numel()
+        return e0.elapsed_time(e1), flat.numel()
 
     @staticmethod
     def cpu_baseline():
