@@ -132,7 +132,18 @@ template <> struct Act<__nv_bfloat16> {
 
 struct W4Args {
   int M, N, K, group, n_kb, n_groups;
+  int kb_shift;  // log2(group / kBK) when that is a power of two, else -1
 };
+
+inline int kb_shift_of(int group) {
+  const int r = group / kBK;
+  return (r & (r - 1)) == 0 ? __builtin_ctz(r) : -1;
+}
+
+// group index of K step kb (group is a multiple of kBK)
+__device__ __forceinline__ int group_of(const W4Args& a, int kb) {
+  return a.kb_shift >= 0 ? kb >> a.kb_shift : (kb * kBK) / a.group;
+}
 
 // NF4 weights (QLoRALinear): code byte b = elements 2i (low nibble) and
 // 2i+1 (high nibble) -> the pair (round_T(NF4[lo]), round_T(NF4[hi])).  The
@@ -247,7 +258,7 @@ __global__ void __launch_bounds__(192, 1) w4a16_kernel(const __grid_constant__ C
         tma_load_2d(smem + L::off_x + s * L::kX, &tmap_x, i * kBK, m0, &full_x[s]);
         mbar_expect_tx(&full_w[s], kWStage + kSStage);
         bulk_load(smem + L::off_w + s * kWStage, wtile + (size_t)i * kWStage, kWStage, &full_w[s]);
-        const int g = (i * kBK) / a.group;
+        const int g = group_of(a, i);
         bulk_load(smem + L::off_s + s * kSStage, stile + (size_t)g * kSStage, kSStage, &full_w[s]);
         issued = i + 1;
       }
@@ -360,9 +371,10 @@ __global__ void __launch_bounds__(192, 1) w4a16_kernel(const __grid_constant__ C
 // ---------------------------------------------------------------------------
 // Small M (M <= 8 tokens): the forward is a weight-streaming GEMV, bound by
 // HBM; a 128 x BT tensor-memory tile would sit mostly idle.  A block of
-// kGemvWarps warps owns 16 weight rows (small enough that every block of the
-// grid is resident at once); warp w takes the K steps w, w + kGemvWarps, ...
-// (the next one's loads issued before the current one is used) and runs
+// kGemvWarps warps owns 16 (NF: 32) weight rows, small enough that every block
+// of the grid is resident at once; warp w takes the K steps w, w + kGemvWarps,
+// ... (their weights streamed by cp.async into a per-warp ring; 512-byte TMA
+// bulk copies measured slower here, bound by their request rate) and runs
 // mma.sync.m16n8k16 (f32 accumulate) with the weights as the A operand and up
 // to 8 tokens per B tile.  The A fragment of a lane is (rows g, g+8) x (k
 // pairs 2c, 2c+8) of each 16-wide k tile (g = lane / 4, c = lane % 4), which
@@ -405,134 +417,154 @@ template <> struct MmaOp<__nv_bfloat16> {
   __device__ __forceinline__ static float hi_f(uint32_t pair) { return __uint_as_float(pair & 0xFFFF0000u); }
 };
 
-constexpr int kGemvWarps = 4;  // warps per block = K split of a 16-row group
+constexpr int kGemvWarps = 4;  // warps per block = K split of the block's rows
 
-template <typename T, int NT8, bool NF>
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Block = R16 x 16 consecutive weight rows (inside one 128-row tile); warp w
+// takes the K steps w, w + kGemvWarps, ... of all of them.  A K step's slice
+// of the block -- R16 x 512 contiguous bytes of codes and R16 x 64 of (zero,
+// scale) pairs -- is copied with 16-byte cp.async (L2 only) into the warp's
+// own ring of DEPTH stages, so each warp keeps DEPTH steps of weights in
+// flight without registers; the activations of the next step are loaded into
+// registers (from L1 / L2: every block reads the same x) while the current one
+// is multiplied.
+template <typename T, bool NF, int R16, int DEPTH>
 __global__ void __launch_bounds__(32 * kGemvWarps) w4a16_gemv_kernel(const T* __restrict__ x,
                                                          const uint8_t* __restrict__ packed,
                                                          const float* __restrict__ bias,
                                                          T* __restrict__ y, W4Args a) {
-  __shared__ float red[kGemvWarps][NT8][32][4];
-  __shared__ __align__(16) uint32_t lut[NF ? kPairLutWords : 4];
-  __shared__ uint32_t ltmp[NF ? 256 : 1];
-  if constexpr (NF) {
-    build_pair_lut<T>(lut, ltmp);
-    __syncthreads();
-  }
+  constexpr int kCodes = R16 * 512, kStage = R16 * 576;
+  extern __shared__ __align__(16) uint8_t gv_smem[];
+  uint32_t* lut = reinterpret_cast<uint32_t*>(gv_smem);                                  // NF: pair table
+  float* red = reinterpret_cast<float*>(gv_smem + (NF ? kPairLutWords * 4 + 1024 : 0));  // [warps][R16][32][4]
+  uint8_t* ring = reinterpret_cast<uint8_t*>(red + kGemvWarps * R16 * 128);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
-  const int r0 = blockIdx.x * 16;          // first weight row of the block
-  const int nt = r0 / kRows, rit = r0 % kRows + g;  // tile, row of lane in the tile
-  const uint8_t* wt = packed + (size_t)nt * a.n_kb * kWStage;
-  const uint32_t* pr = reinterpret_cast<const uint32_t*>(packed + (size_t)a.N * a.K / 2) +
-                       (size_t)nt * a.n_groups * kRows;
-  const uint16_t* xs = reinterpret_cast<const uint16_t*>(x);
-  float acc[NT8][4];
-#pragma unroll
-  for (int j = 0; j < NT8; ++j)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) acc[j][i] = 0.0f;
-  // token rows of this lane's B fragments (0 beyond M)
-  int64_t xrow[NT8];
-  bool xlive[NT8];
-#pragma unroll
-  for (int j = 0; j < NT8; ++j) {
-    const int tok = 8 * j + g;
-    xlive[j] = tok < a.M;
-    xrow[j] = (int64_t)(xlive[j] ? tok : 0) * a.K;
+  if constexpr (NF) {
+    build_pair_lut<T>(lut, reinterpret_cast<uint32_t*>(gv_smem + kPairLutWords * 4));
+    __syncthreads();
   }
-  // the next K step's codes and (zero, scale) pairs are loaded before the
-  // current one is computed
-  uint4 w0, w1, w2, w3;
-  uint32_t zs0 = 0, zs1 = 0;
-  auto load_step = [&](int kb, uint4& a0, uint4& a1, uint4& b0, uint4& b1, uint32_t& z0, uint32_t& z1) {
-    const uint4* src = reinterpret_cast<const uint4*>(wt + (size_t)kb * kWStage + rit * 32);
-    a0 = __ldg(src);
-    a1 = __ldg(src + 1);  // row g
-    b0 = __ldg(src + 16);
-    b1 = __ldg(src + 17);  // row g + 8
-    const int grp = (kb * kBK) / a.group;
-    z0 = __ldg(pr + (size_t)grp * kRows + rit);
-    z1 = __ldg(pr + (size_t)grp * kRows + rit + 8);
+  uint8_t* my = ring + warp * DEPTH * kStage;
+  const int r0 = blockIdx.x * 16 * R16;  // first weight row of the block
+  const int nt = r0 / kRows, rit0 = r0 % kRows;
+  const uint8_t* codes = packed + ((size_t)nt * a.n_kb * kRows + rit0) * 32;
+  const uint8_t* pairs = packed + (size_t)a.N * a.K / 2 + ((size_t)nt * a.n_groups * kRows + rit0) * 4;
+  auto issue = [&](int kb, uint8_t* dst) {
+    const uint8_t* cs = codes + (size_t)kb * kRows * 32;
+#pragma unroll
+    for (int i = 0; i < R16; ++i) cp_async16(dst + (i * 32 + lane) * 16, cs + (i * 32 + lane) * 16);
+    if (lane < 4 * R16) cp_async16(dst + kCodes + lane * 16, pairs + (size_t)group_of(a, kb) * kRows * 4 + lane * 16);
   };
-  if (warp < a.n_kb) load_step(warp, w0, w1, w2, w3, zs0, zs1);
-  for (int kb = warp; kb < a.n_kb; kb += kGemvWarps) {
-    uint4 n0 = w0, n1 = w1, n2 = w2, n3 = w3;
-    uint32_t nz0 = zs0, nz1 = zs1;
-    if (kb + kGemvWarps < a.n_kb) load_step(kb + kGemvWarps, n0, n1, n2, n3, nz0, nz1);
-    const uint32_t zb0 = __byte_perm(zs0, zs0, 0x1010), zb1 = __byte_perm(zs1, zs1, 0x1010);
-    const uint32_t ra[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-    const uint32_t rb[8] = {w2.x, w2.y, w2.z, w2.w, w3.x, w3.y, w3.z, w3.w};
-    // this K step's B fragments (token rows of the lane), loaded up front
-    uint32_t bx[NT8][4][2];
+  // this warp's K steps: kb = warp + i * kGemvWarps, i < n_my
+  const int n_my = a.n_kb > warp ? (a.n_kb - warp + kGemvWarps - 1) / kGemvWarps : 0;
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      const int k = kb * kBK + 16 * t + 2 * c;
-#pragma unroll
-      for (int j = 0; j < NT8; ++j) {
-        bx[j][t][0] = xlive[j] ? __ldg(reinterpret_cast<const uint32_t*>(xs + xrow[j] + k)) : 0u;
-        bx[j][t][1] = xlive[j] ? __ldg(reinterpret_cast<const uint32_t*>(xs + xrow[j] + k + 8)) : 0u;
-      }
-    }
-    float part[NT8][4];
-#pragma unroll
-    for (int j = 0; j < NT8; ++j)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) part[j][i] = 0.0f;
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      uint32_t af[4];
-      if constexpr (NF) {
-        // byte c of words 2t, 2t+1 = k pairs (16t + 2c, +8): table pairs, scaled below
-        const char* lb = reinterpret_cast<const char*>(lut);
-        const uint32_t l4 = (uint32_t)lane << 2;
-        af[0] = *reinterpret_cast<const uint32_t*>(lb + ((((ra[2 * t] >> (8 * c)) & 0xFFu) << 7) | l4));
-        af[1] = *reinterpret_cast<const uint32_t*>(lb + ((((rb[2 * t] >> (8 * c)) & 0xFFu) << 7) | l4));
-        af[2] = *reinterpret_cast<const uint32_t*>(lb + ((((ra[2 * t + 1] >> (8 * c)) & 0xFFu) << 7) | l4));
-        af[3] = *reinterpret_cast<const uint32_t*>(lb + ((((rb[2 * t + 1] >> (8 * c)) & 0xFFu) << 7) | l4));
-      } else {
-        af[0] = MmaOp<T>::sub2(((ra[2 * t] >> (4 * c)) & 0x000F000Fu) | Act<T>::magic, zb0);
-        af[1] = MmaOp<T>::sub2(((rb[2 * t] >> (4 * c)) & 0x000F000Fu) | Act<T>::magic, zb1);
-        af[2] = MmaOp<T>::sub2(((ra[2 * t + 1] >> (4 * c)) & 0x000F000Fu) | Act<T>::magic, zb0);
-        af[3] = MmaOp<T>::sub2(((rb[2 * t + 1] >> (4 * c)) & 0x000F000Fu) | Act<T>::magic, zb1);
-      }
-#pragma unroll
-      for (int j = 0; j < NT8; ++j) MmaOp<T>::mma(part[j], af, bx[j][t][0], bx[j][t][1]);
-    }
-    // scales of rows g and g + 8 (high halves of the pairs)
-    const float s0 = MmaOp<T>::hi_f(zs0), s1 = MmaOp<T>::hi_f(zs1);
-#pragma unroll
-    for (int j = 0; j < NT8; ++j) {
-      acc[j][0] = fmaf(part[j][0], s0, acc[j][0]);
-      acc[j][1] = fmaf(part[j][1], s0, acc[j][1]);
-      acc[j][2] = fmaf(part[j][2], s1, acc[j][2]);
-      acc[j][3] = fmaf(part[j][3], s1, acc[j][3]);
-    }
-    w0 = n0;
-    w1 = n1;
-    w2 = n2;
-    w3 = n3;
-    zs0 = nz0;
-    zs1 = nz1;
+  for (int i = 0; i < DEPTH; ++i) {
+    if (i < n_my) issue(warp + i * kGemvWarps, my + i * kStage);
+    cp_async_commit();
   }
+  // B fragment of lane (g, c): x[token g][k = 16t + 2c (+1), 16t + 2c + 8 (+9)].
+  // Lanes of tokens >= M read token 0: their columns are never stored.
+  const uint32_t* xr = reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint16_t*>(x) +
+                                                         (size_t)(g < a.M ? g : 0) * a.K + 2 * c);
+  auto load_x = [&](int kb, uint32_t (&bx)[4][2]) {
+    const uint32_t* p = xr + kb * (kBK / 2);
 #pragma unroll
-  for (int j = 0; j < NT8; ++j)
+    for (int t = 0; t < 4; ++t) {
+      bx[t][0] = __ldg(p + 8 * t);
+      bx[t][1] = __ldg(p + 8 * t + 4);
+    }
+  };
+  float acc[R16][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) red[warp][j][lane][i] = acc[j][i];
+  for (int r = 0; r < R16; ++r)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[r][i] = 0.0f;
+  uint32_t bx[4][2];
+  if (n_my > 0) load_x(warp, bx);
+#pragma unroll 2
+  for (int i = 0; i < n_my; ++i) {
+    const int kb = warp + i * kGemvWarps;
+    uint8_t* st = my + (i % DEPTH) * kStage;
+    uint32_t nx[4][2];
+    if (i + 1 < n_my) load_x(kb + kGemvWarps, nx);
+    cp_async_wait<DEPTH - 1>();
+    __syncwarp();
+#pragma unroll
+    for (int r = 0; r < R16; ++r) {
+      const uint4* src = reinterpret_cast<const uint4*>(st + r * 512);
+      const uint4 w0 = src[2 * g], w1 = src[2 * g + 1];        // row g
+      const uint4 w2 = src[2 * g + 16], w3 = src[2 * g + 17];  // row g + 8
+      const uint32_t zs0 = *reinterpret_cast<const uint32_t*>(st + kCodes + r * 64 + 4 * g);
+      const uint32_t zs1 = *reinterpret_cast<const uint32_t*>(st + kCodes + r * 64 + 4 * (g + 8));
+      const uint32_t zb0 = __byte_perm(zs0, zs0, 0x1010), zb1 = __byte_perm(zs1, zs1, 0x1010);
+      const uint32_t ra[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      const uint32_t rb[8] = {w2.x, w2.y, w2.z, w2.w, w3.x, w3.y, w3.z, w3.w};
+      float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        uint32_t af[4];
+        if constexpr (NF) {
+          // byte c of words 2t, 2t+1 = k pairs (16t + 2c, +8): table pairs, scaled below
+          const char* lb = reinterpret_cast<const char*>(lut);
+          const uint32_t l4 = (uint32_t)lane << 2;
+          af[0] = *reinterpret_cast<const uint32_t*>(lb + ((((ra[2 * t] >> (8 * c)) & 0xFFu) << 7) | l4));
+          af[1] = *reinterpret_cast<const uint32_t*>(lb + ((((rb[2 * t] >> (8 * c)) & 0xFFu) << 7) | l4));
+          af[2] = *reinterpret_cast<const uint32_t*>(lb + ((((ra[2 * t + 1] >> (8 * c)) & 0xFFu) << 7) | l4));
+          af[3] = *reinterpret_cast<const uint32_t*>(lb + ((((rb[2 * t + 1] >> (8 * c)) & 0xFFu) << 7) | l4));
+        } else {
+          af[0] = MmaOp<T>::sub2(((ra[2 * t] >> (4 * c)) & 0x000F000Fu) | Act<T>::magic, zb0);
+          af[1] = MmaOp<T>::sub2(((rb[2 * t] >> (4 * c)) & 0x000F000Fu) | Act<T>::magic, zb1);
+          af[2] = MmaOp<T>::sub2(((ra[2 * t + 1] >> (4 * c)) & 0x000F000Fu) | Act<T>::magic, zb0);
+          af[3] = MmaOp<T>::sub2(((rb[2 * t + 1] >> (4 * c)) & 0x000F000Fu) | Act<T>::magic, zb1);
+        }
+        MmaOp<T>::mma(part, af, bx[t][0], bx[t][1]);
+      }
+      // scales of rows g and g + 8 (high halves of the pairs)
+      const float s0 = MmaOp<T>::hi_f(zs0), s1 = MmaOp<T>::hi_f(zs1);
+      acc[r][0] = fmaf(part[0], s0, acc[r][0]);
+      acc[r][1] = fmaf(part[1], s0, acc[r][1]);
+      acc[r][2] = fmaf(part[2], s1, acc[r][2]);
+      acc[r][3] = fmaf(part[3], s1, acc[r][3]);
+    }
+    __syncwarp();  // every lane has read the stage before it is refilled
+    if (i + DEPTH < n_my) issue(kb + DEPTH * kGemvWarps, st);
+    cp_async_commit();
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      bx[t][0] = nx[t][0];
+      bx[t][1] = nx[t][1];
+    }
+  }
+  cp_async_wait<0>();
+#pragma unroll
+  for (int r = 0; r < R16; ++r)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) red[((warp * R16 + r) * 32 + lane) * 4 + i] = acc[r][i];
   __syncthreads();
-  // thread -> (j, lane, i) of the fragment; 32 * 4 * NT8 <= 256 outputs
-  for (int o = threadIdx.x; o < 32 * 4 * NT8; o += blockDim.x) {
-    const int i = o & 3, ln = (o >> 2) & 31, j = o >> 7;
-    float s = 0.0f;
+  // thread -> (r, lane, i) of the fragments; tokens 2c, 2c+1 are columns 0/1
+  for (int o = threadIdx.x; o < R16 * 128; o += blockDim.x) {
+    const int i = o & 3, ln = (o >> 2) & 31, r = o >> 7;
+    float sum = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kGemvWarps; ++w) s += red[w][j][ln][i];
-    const int row = r0 + (ln >> 2) + (i >= 2 ? 8 : 0);
-    const int tok = 8 * j + 2 * (ln & 3) + (i & 1);
+    for (int w = 0; w < kGemvWarps; ++w) sum += red[((w * R16 + r) * 32 + ln) * 4 + i];
+    const int row = r0 + 16 * r + (ln >> 2) + (i >= 2 ? 8 : 0);
+    const int tok = 2 * (ln & 3) + (i & 1);
     if (tok < a.M) {
-      if (bias) s = __fadd_rn(s, bias[row]);
-      y[(size_t)tok * a.N + row] = Ty<T>::from_f(s);
+      if (bias) sum = __fadd_rn(sum, bias[row]);
+      y[(size_t)tok * a.N + row] = Ty<T>::from_f(sum);
     }
   }
+}
+
+template <bool NF, int R16, int DEPTH>
+constexpr int gemv_smem() {
+  return (NF ? kPairLutWords * 4 + 1024 : 0) + kGemvWarps * R16 * 512 + kGemvWarps * DEPTH * R16 * 576;
 }
 
 template <typename T, bool NF>
@@ -545,13 +577,16 @@ int launch_gemv(const void* x, int M, int N, int K, int group, const void* packe
   a.group = group;
   a.n_kb = K / kBK;
   a.n_groups = K / group;
-  const int grid = N / 16;
-  if (M <= 8)
-    w4a16_gemv_kernel<T, 1, NF><<<grid, 32 * kGemvWarps, 0, st>>>(static_cast<const T*>(x), static_cast<const uint8_t*>(packed),
-                                                  bias, static_cast<T*>(y), a);
-  else
-    w4a16_gemv_kernel<T, 2, NF><<<grid, 32 * kGemvWarps, 0, st>>>(static_cast<const T*>(x), static_cast<const uint8_t*>(packed),
-                                                  bias, static_cast<T*>(y), a);
+  a.kb_shift = kb_shift_of(group);
+  // the NF table (33 KB) limits blocks per SM: 32 rows per block keeps the
+  // whole grid resident for N up to ~19K
+  constexpr int R16 = NF ? 2 : 1, DEPTH = NF ? 4 : 8;
+  constexpr int smem = gemv_smem<NF, R16, DEPTH>();
+  auto kern = w4a16_gemv_kernel<T, NF, R16, DEPTH>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return launched("w4a16_gemv_kernel (attribute)");
+  kern<<<N / (16 * R16), 32 * kGemvWarps, smem, st>>>(static_cast<const T*>(x), static_cast<const uint8_t*>(packed),
+                                                      bias, static_cast<T*>(y), a);
   return launched("w4a16_gemv_kernel");
 }
 
@@ -697,6 +732,7 @@ int launch_w4(const void* x, int M, int N, int K, int group, const void* packed,
   a.group = group;
   a.n_kb = K / kBK;
   a.n_groups = K / group;
+  a.kb_shift = kb_shift_of(group);
   auto kern = w4a16_kernel<T, BT, S, NF>;
   // every CTA allocates all 512 tensor-memory columns: request enough shared
   // memory that only one CTA fits on an SM, so none waits in tcgen05.alloc
