@@ -862,6 +862,115 @@ class QLoRALinearWorkload(W4A16Workload):
                 "sample": f"oracle NF4 dequant + numpy fp32 matmul, M={M}, K={K}, N={N}, median of 3"}
 
 
+class KVAttentionWorkload:
+    """Decode attention over the quantized KV cache (QuantizedKVCache.attend):
+    4 layers, each a cache of B=8 x 8 kv heads x 8192 tokens x head_dim 128
+    quantized per token to symmetric INT8 (the cache's default quantizer) from
+    fp16; 32 query heads (4 per kv head), one query token.  A step attends all
+    4 layers (4 x 138 MB of codes and scales: more than L2, each layer read
+    from HBM).  Independent replicas per GPU (weak scaling)."""
+    name = "kv_attention"
+    workload = "kv_decode_attention_int8_pertoken_B8_Hkv8_Hq32_T8192_D128_fp16_x4layers"
+    main_kernel = "kv_attn_kernel"
+    B, H, HQ, T, D, LAYERS = 8, 8, 32, 8192, 128, 4
+
+    def __init__(self, ctx):
+        torch = ctx.torch
+        import llm_quant_b200 as L
+        self.ctx, self.L = ctx, L
+        g = torch.Generator(device=ctx.dev).manual_seed(ctx.rank)
+        self.cache = L.QuantizedKVCache(self.LAYERS, max_seq_len=self.T)
+        for layer in range(self.LAYERS):
+            for _ in range(self.T // 2048):
+                k = torch.randn(self.B, self.H, 2048, self.D, generator=g, device=ctx.dev).half()
+                v = torch.randn(self.B, self.H, 2048, self.D, generator=g, device=ctx.dev).half()
+                self.cache.append(layer, k, v)
+                del k, v
+        self.q = torch.randn(self.B, self.HQ, 1, self.D, generator=g, device=ctx.dev).half()
+        self.n_local = self.LAYERS
+        self.n_total = self.LAYERS * ctx.world
+
+    def bytes_per_layer(self):
+        bht = self.B * self.H * self.T
+        # K + V int8 codes, fp16 scale + zero point per token for each, q in, out
+        return 2 * bht * self.D + 2 * 2 * bht * 2 + 2 * self.B * self.HQ * self.D * 2
+
+    def bytes_for(self, n_layers):
+        return self.bytes_per_layer() * n_layers
+
+    def step(self):
+        for layer in range(self.LAYERS):
+            self.cache.attend(layer, self.q)
+
+    def kernels(self):
+        torch = self.ctx.torch
+        c = [0]
+
+        def f():
+            self.cache.attend(c[0] % self.LAYERS, self.q)
+            c[0] += 1
+        t = cuda_time_ms(torch, f, 4 * self.LAYERS)
+        n = self.B * self.H * self.T
+        return {"kv_attn_kernel + combine (one layer)": (float(self.bytes_per_layer()), t, n,
+                                                         "cached tokens")}
+
+    def e2e(self, steps, graph):
+        """attend() through the public API for every layer, with the query
+        copied in from pinned host memory and the output copied back."""
+        torch = self.ctx.torch
+        hq = self.q.cpu().pin_memory()
+        dq = torch.empty_like(self.q)
+        outs = [torch.empty(self.q.shape, dtype=self.q.dtype).pin_memory() for _ in range(self.LAYERS)]
+
+        def one():
+            for layer in range(self.LAYERS):
+                dq.copy_(hq, non_blocking=True)
+                outs[layer].copy_(self.cache.attend(layer, dq), non_blocking=True)
+
+        one()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            one()
+        e1.record()
+        torch.cuda.synchronize()
+        nb = self.q.numel() * 2 * self.LAYERS
+        return e0.elapsed_time(e1) / steps, nb, nb
+
+    def gather(self):
+        return 0.0, 0
+
+    @staticmethod
+    def cpu_baseline():
+        """The reference's read path on the host: dequantize the cached codes
+        to fp32 (oracle kv_dequantize) and attend (numpy), for 2 (batch, kv
+        head) slices of the same cache shape."""
+        from oracle import lq_oracle as O
+        rng = np.random.default_rng(0)
+        T, D, G, n = 8192, 128, 4, 2
+        sl = []
+        for _ in range(n):
+            k = O.rnd(rng.standard_normal((1, 1, T, D)).astype(np.float32), "float16")
+            v = O.rnd(rng.standard_normal((1, 1, T, D)).astype(np.float32), "float16")
+            kq = O.kv_quantize(k, "float16", 8, True, O.PER_TOKEN)
+            vq = O.kv_quantize(v, "float16", 8, True, O.PER_TOKEN)
+            q = O.rnd(rng.standard_normal((1, G, 1, D)).astype(np.float32), "float16")
+            sl.append((kq, vq, q))
+
+        def run(x):
+            (kc, ks, kz), (vc, vs, vz), q = x
+            fk = O.kv_dequantize(kc, ks, "float16", kz, "float16")
+            fv = O.kv_dequantize(vc, vs, "float16", vz, "float16")
+            O.kv_attention(q, fk, fv)
+
+        t, nt = cpu_time(run, sl)
+        b = n * (2 * T * D + 2 * 2 * T * 2 + 2 * G * D * 2)
+        return {"value": b / t / 1e9, "unit": "GB/s", "cores": min(nt, n), "kind": "port",
+                "sample": f"oracle dequantize + float64 attention, {n} (batch, kv head) slices of "
+                          f"{T} tokens x {D}, 4 query heads each ({nt} threads), median of 3"}
+
+
 def profile_case(name, ctx):
     """A small case of each workload's dominant kernel for ncu captures:
     inputs larger than L2 (126 MB) but a few hundred MB at most, 3 launches."""
@@ -896,6 +1005,14 @@ def profile_case(name, ctx):
             ql(x)
         for _ in range(3):
             ql(x[:1])
+    elif name == "kv_attention":
+        cache = L.QuantizedKVCache(1, max_seq_len=4096)
+        for _ in range(2):
+            k = torch.randn(8, 8, 2048, 128, generator=g, device=ctx.dev).half()
+            cache.append(0, k, k)
+        q = torch.randn(8, 32, 1, 128, generator=g, device=ctx.dev).half()
+        for _ in range(3):
+            cache.attend(0, q)
     elif name == "qlora_linear":
         w = (torch.randn(14336, 4096, generator=g, device=ctx.dev) * 0.02).to(torch.bfloat16)
         ql = L.QLoRALinear(4096, 14336, rank=16, group_size=64).to(ctx.dev)
@@ -911,7 +1028,8 @@ def profile_case(name, ctx):
 
 
 WORKLOADS = {"nf4": NF4Workload, "group": GroupWorkload, "rotquant": RotQuantWorkload,
-             "kv": KVWorkload, "w4a16": W4A16Workload, "qlora_linear": QLoRALinearWorkload}
+             "kv": KVWorkload, "w4a16": W4A16Workload, "qlora_linear": QLoRALinearWorkload,
+             "kv_attention": KVAttentionWorkload}
 
 
 # ─────────────────────────────────────────────────────────────────────────────
@@ -938,7 +1056,8 @@ def run_reference(args):
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": 1e3 * statistics.median(ts), "higher_is_better": True,
             "scaling": "strong" if args.workload in ("nf4", "kv") else "weak",
-            "vs_baseline": None, "dtype": "bf16" if args.workload != "group" else "f32",
+            "vs_baseline": None,
+            "dtype": {"group": "f32", "w4a16": "f16", "kv_attention": "f16"}.get(args.workload, "bf16"),
             "data": "synthetic (seeded)", "impl": "reference",
             "config": {"workload": W.workload, "sample": cb["sample"]},
             "cpu_baseline": cb,
@@ -1029,7 +1148,7 @@ def run_ours(args):
             "higher_is_better": True,
             "scaling": "strong" if W.name in ("nf4", "kv") else "weak",
             "vs_baseline": None,
-            "dtype": {"group": "f32", "w4a16": "f16"}.get(W.name, "bf16"),
+            "dtype": {"group": "f32", "w4a16": "f16", "kv_attention": "f16"}.get(W.name, "bf16"),
             "data": "synthetic (seeded torch.randn on the device)",
             "config": {"workload": W.workload, "parallelism": f"layer-shard x{ctx.world}"
                        if W.name in ("nf4", "kv") else f"independent x{ctx.world}",

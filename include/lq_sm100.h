@@ -141,6 +141,35 @@ int lq_kv_append(const void* x, int x_dtype, int64_t P, int64_t Tn, int64_t D, i
                  int64_t codes_pitch_t, int64_t t_offset, void* scale, void* zero_point,
                  int64_t sz_pitch, int64_t sz_offset, int merge, void* stream);
 
+/* ---- decode attention over the quantized cache ---------------------------------
+ * out[b, hq, i, :] = softmax(q[b, hq, i, :] . K^T * sm_scale) V with K, V the
+ * fp32 dequantization (code - zero) * scale of the cache storage above
+ * (kv_cache_quant.py:221-267; the reference returns the whole dequantized
+ * cache from update(), kv_cache_quant.py:379-382, and leaves attention to the
+ * caller).  The codes are read in place; K / V are never materialized.
+ *   q, out   [B, Hq, Sq, D] contiguous, q_dtype (f32 / f16 / bf16); query
+ *            head hq reads kv head hq / (Hq / H).
+ *   codes    [B*H, cap, D] (LQ_I8, or LQ_I16 with codes <= 1024), T tokens
+ *            valid, cap a multiple of 16.
+ *   *_gran   0 per-token: scale/zp [B*H, pitch] (pitch >= cap, pitch * size
+ *              of s_dtype a multiple of 16 bytes),
+ *            1 per-channel: scale/zp [B*H, D],
+ *            2 per-group: scale/zp [B*H, pitch, D], *_group tokens per row
+ *              (a multiple of 16).
+ *   causal   1: query position i sees tokens t <= T - Sq + i.
+ * Codes, scales and zero points must be 16-byte aligned.  When the work is
+ * split along the tokens the call needs lq_kv_attention_workspace_bytes()
+ * bytes of workspace (0 = none needed).  D = 64 or 128. */
+size_t lq_kv_attention_workspace_bytes(int64_t B, int64_t Hq, int64_t H, int64_t Sq, int64_t D,
+                                       int64_t T);
+int lq_kv_attention(const void* q, int q_dtype, int64_t B, int64_t Hq, int64_t H, int64_t Sq,
+                    int64_t D, int64_t T, int64_t cap, int code_dtype, const void* k_codes,
+                    int k_gran, int64_t k_group, const void* k_scale, const void* k_zp,
+                    int64_t k_pitch, const void* v_codes, int v_gran, int64_t v_group,
+                    const void* v_scale, const void* v_zp, int64_t v_pitch, int s_dtype,
+                    float sm_scale, int causal, void* out, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
 /* ---- per-tensor qparams -------------------------------------------------------
  * compute_qparams PER_TENSOR (core/quantizer.py:63-72): scale = 0-dim,
  * zero_point = [1] (sym) or 0-dim (asym), both in x's dtype.  x is n

@@ -68,12 +68,17 @@ _SIGS = {
     "lq_nf4_linear_pack": [_V, _V, _V, _V, _I, _L, _L, _L, _L, _I, _V, _V],
     "lq_nf4_linear": [_V, _I, _L, _L, _L, _V, _V, _V, _V, _V],
     "lq_sparse_row_add": [_V, _I, _L, _L, _L, _V, _V, _L, _V, _V, _V, _V],
+    "lq_kv_attention": [_V, _I, _L, _L, _L, _L, _L, _L, _L, _I,
+                        _V, _I, _L, _V, _V, _L,
+                        _V, _I, _L, _V, _V, _L,
+                        _I, ctypes.c_float, _I, _V, _V, ctypes.c_size_t, _V],
 }
 _SIZE_SIGS = {
     "lq_tensor_qparams_workspace_size": [_L],
     "lq_channel_qparams_workspace_size": [_L, _L, _L],
     "lq_w4a16_packed_bytes": [_L, _L, _L],
     "lq_nf4_linear_packed_bytes": [_L, _L],
+    "lq_kv_attention_workspace_bytes": [_L, _L, _L, _L, _L, _L],
 }
 
 _lib = None

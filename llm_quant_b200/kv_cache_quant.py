@@ -11,6 +11,11 @@ K / V) instead of concatenating the whole cache; the full dequantized K and
 V it returns are written by one more kernel each.  Semantics follow the
 reference, including its PER_CHANNEL scale merge with ``torch.maximum``
 that does not requantize earlier codes (kv_cache_quant.py:395-402).
+
+Beyond the reference: ``QuantizedKVCache.append`` stores a chunk without
+returning the dequantized cache, and ``QuantizedKVCache.attend`` computes
+decode attention straight from the stored codes (``lq_kv_attention``), so a
+decode step reads the cache once, in its quantized size.
 """
 
 from __future__ import annotations
@@ -251,6 +256,7 @@ class _CacheSide:
         B, H, D = self.B, self.H, self.D
         if need_t > self.cap:
             cap = max(need_t, 2 * self.cap, 64)
+            cap = (cap + 15) // 16 * 16  # whole 16-token tiles for lq_kv_attention
             codes = torch.empty(B, H, cap, D, dtype=self.code_dtype, device=self.device)
             if self.T:
                 codes[:, :, :self.T].copy_(self.codes[:, :, :self.T])
@@ -350,17 +356,79 @@ class QuantizedKVCache(nn.Module):
     ) -> Tuple[torch.Tensor, torch.Tensor]:
         """Append new K, V [B, H, S_new, D] and return the full dequantized fp32
         K, V [B, H, S_total, D] (kv_cache_quant.py:336-382)."""
+        self.append(layer_idx, key, value)
+        ks, vs = self._sides[layer_idx]
+        return ks.dequantize(), vs.dequantize()
+
+    def _side_pair(self, layer_idx: int, key: torch.Tensor, value: torch.Tensor):
         sides = self._sides[layer_idx]
         if sides is None:
             vq = self.value_quantizer or self.quantizer
             sides = (_CacheSide(self.quantizer, key, self.max_seq_len),
                      _CacheSide(vq, value, self.max_seq_len))
             self._sides[layer_idx] = sides
-        ks, vs = sides
+        return sides
+
+    def append(self, layer_idx: int, key: torch.Tensor, value: torch.Tensor) -> None:
+        """The storing half of ``update``: quantize and append new K, V
+        [B, H, S_new, D] without building the dequantized cache (for callers
+        that attend with ``attend``)."""
+        ks, vs = self._side_pair(layer_idx, key, value)
         ks.append(key)
         vs.append(value)
         self._cache[layer_idx] = ks.views() + vs.views()
-        return ks.dequantize(), vs.dequantize()
+
+    def attend(self, layer_idx: int, query: torch.Tensor, scale: Optional[float] = None,
+               causal: bool = False) -> torch.Tensor:
+        """softmax(query K^T * scale) V over a layer's cached tokens, where K
+        and V are exactly the fp32 tensors ``update`` / ``get`` return
+        (kv_cache_quant.py:221-267), computed from the codes in place.
+
+        query [B, Hq, Sq, D] with Hq a multiple of the cached heads H (query
+        head h reads kv head h // (Hq // H)); ``scale`` defaults to D ** -0.5;
+        ``causal`` aligns the Sq queries to the end of the cache (query i sees
+        tokens t <= T - Sq + i).  Returns [B, Hq, Sq, D] in query's dtype.
+        Supported: head dim 64 or 128, the same code dtype for K and V, codes
+        of at most 10 bits, per-group sizes that are multiples of 16."""
+        sides = self._sides[layer_idx]
+        if sides is None:
+            raise RuntimeError(f"QuantizedKVCache.attend: layer {layer_idx} is empty")
+        ks, vs = sides
+        _C.require_cuda(query, what="QuantizedKVCache.attend")
+        _C.require_float(query, "QuantizedKVCache.attend")
+        if query.ndim != 4 or query.shape[0] != ks.B or query.shape[3] != ks.D or \
+                query.shape[1] % ks.H:
+            raise RuntimeError(
+                f"QuantizedKVCache.attend: query {list(query.shape)} does not match the cache "
+                f"[{ks.B}, {ks.H}*G, *, {ks.D}]")
+        if ks.code_dtype != vs.code_dtype or ks.dtype != vs.dtype:
+            raise NotImplementedError(
+                "QuantizedKVCache.attend: K and V must share code and scale dtypes")
+        for side in (ks, vs):
+            if side.code_dtype == torch.int16 and side.qz.n_bits > 10:
+                raise NotImplementedError(
+                    "QuantizedKVCache.attend: asymmetric codes of more than 10 bits")
+            if side.gran == "per_group" and side.qz.group_size % 16:
+                raise NotImplementedError(
+                    "QuantizedKVCache.attend: per-group sizes must be multiples of 16")
+        q = query.contiguous()
+        B, Hq, Sq, D = q.shape
+        sm = float(D ** -0.5 if scale is None else scale)
+        out = torch.empty_like(q)
+        if B * Hq * Sq == 0:
+            return out
+        nbytes = _C.lib().lq_kv_attention_workspace_bytes(B, Hq, ks.H, Sq, D, ks.T)
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device) if nbytes else None
+
+        def side_args(sd):
+            pitch = {"per_token": sd.cap, "per_channel": 1, "per_group": sd.gcap}[sd.gran]
+            return (sd.codes.data_ptr(), _GRAN_CODE[sd.gran], sd.qz.group_size,
+                    sd.scale.data_ptr(), sd.zp.data_ptr(), pitch)
+
+        _C.call("lq_kv_attention", q.data_ptr(), _C.dt(q), B, Hq, ks.H, Sq, D, ks.T, ks.cap,
+                _C.dt(ks.code_dtype), *side_args(ks), *side_args(vs), _C.dt(ks.dtype), sm,
+                int(bool(causal)), out.data_ptr(), _C.ptr(ws), nbytes, _C.stream_ptr(q))
+        return out
 
     def _cat_scales(self, old_scale: torch.Tensor, new_scale: torch.Tensor, seq_dim: int) -> torch.Tensor:
         """The reference's scale merge rule (kv_cache_quant.py:384-406), as a

@@ -551,3 +551,33 @@ class QuantizedKVCacheOracle:
         fv = kv_dequantize(c[3], c[4], self.dt, c[5], self.dt, self.vq["granularity"],
                            self.vq.get("group_size", 32))
         return fk, fv
+
+
+def kv_attention(q, k, v, sm_scale=None, causal=False):
+    """Decode attention over a layer's dequantized cache, in float64.
+
+    k, v: the fp32 [B, H, T, D] tensors QuantizedKVCache.update / get return
+    (kv_cache_quant.py:336-382, 408-415; ``QuantizedKVCacheOracle.get``).
+    q: [B, Hq, Sq, D], Hq a multiple of H; query head h reads kv head
+    h // (Hq // H).  out = softmax(q k^T * sm_scale) v, sm_scale defaulting to
+    D ** -0.5; causal: query i of Sq sees tokens t <= T - Sq + i.  The
+    reference stops at the dequantized K, V; this is the standard attention
+    its caller computes with them."""
+    q = np.asarray(q, np.float64)
+    k = np.asarray(k, np.float64)
+    v = np.asarray(v, np.float64)
+    B, Hq, Sq, D = q.shape
+    H, T = k.shape[1], k.shape[2]
+    G = Hq // H
+    sm = D ** -0.5 if sm_scale is None else float(sm_scale)
+    kk = np.repeat(k, G, axis=1)
+    vv = np.repeat(v, G, axis=1)
+    s = np.einsum("bhid,bhtd->bhit", q, kk) * sm
+    if causal:
+        t = np.arange(T)[None, :]
+        i = np.arange(Sq)[:, None]
+        s = np.where(t <= T - Sq + i, s, -np.inf)
+    m = s.max(axis=-1, keepdims=True)
+    p = np.exp(s - m)
+    p /= p.sum(axis=-1, keepdims=True)
+    return np.einsum("bhit,bhtd->bhid", p, vv)

@@ -81,6 +81,65 @@ def test_argument_validation_without_gpu(lib_path):
     assert lib.lq_group_quant(None, 0, 0, 8, 4, 4, 1, 1, None, 0, None, None, None) == 0
 
 
+def _attn(lib, **kw):
+    """lq_kv_attention with valid defaults (B=1, Hq=4, H=2, Sq=1, D=128,
+    T=20, cap=32, int8 per-token, fp16) overridden by kw; pointers fake."""
+    V, I, L = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
+    lib.lq_kv_attention.argtypes = [V, I, L, L, L, L, L, L, L, I, V, I, L, V, V, L, V, I, L, V, V, L,
+                                    I, ctypes.c_float, I, V, V, ctypes.c_size_t, V]
+    a = dict(q=None, q_dtype=1, B=1, Hq=4, H=2, Sq=1, D=128, T=20, cap=32, code_dtype=3,
+             k_codes=None, k_gran=0, k_group=32, k_scale=None, k_zp=None, k_pitch=32,
+             v_codes=None, v_gran=0, v_group=32, v_scale=None, v_zp=None, v_pitch=32,
+             s_dtype=1, sm_scale=0.1, causal=0, out=None, ws=None, ws_bytes=0, stream=None)
+    a.update(kw)
+    return lib.lq_kv_attention(*a.values())
+
+
+def test_kv_attention_validation_without_gpu(lib_path):
+    """lq_kv_attention rejects unsupported shapes / layouts on the host."""
+    lib = ctypes.CDLL(lib_path)
+    lib.lq_last_error.restype = ctypes.c_char_p
+    assert _attn(lib, D=96) == -1 and b"head dim" in lib.lq_last_error()
+    assert _attn(lib, Hq=3) == -1
+    assert _attn(lib, cap=40) == -1  # not whole 16-token tiles
+    assert _attn(lib, cap=16) == -1  # below T
+    assert _attn(lib, code_dtype=5) == -2
+    assert _attn(lib, k_gran=2, k_group=24, k_pitch=2) == -1
+    assert _attn(lib, v_gran=2, v_group=16, v_pitch=1) == -1  # 16 tokens of rows < T = 20
+    assert _attn(lib, k_pitch=16) == -1
+    assert _attn(lib) == -1 and b"NULL" in lib.lq_last_error()
+    fake = 4096
+    ptrs = dict(q=fake, k_codes=fake, v_codes=fake, k_scale=fake, k_zp=fake, v_scale=fake,
+                v_zp=fake, out=fake)
+    assert _attn(lib, **dict(ptrs, k_scale=fake + 8)) == -5  # 16-byte alignment
+    assert _attn(lib, B=0, **ptrs) == 0  # empty batch: no work
+    lib.lq_kv_attention_workspace_bytes.restype = ctypes.c_size_t
+    lib.lq_kv_attention_workspace_bytes.argtypes = [ctypes.c_int64] * 6
+    assert lib.lq_kv_attention_workspace_bytes(1, 4, 2, 1, 128, 20) == 0  # one split
+    # 8 x 8 kv heads, 4 rows each, 8192 tokens: split along the tokens
+    n = lib.lq_kv_attention_workspace_bytes(8, 32, 8, 1, 128, 8192)
+    assert n > 0 and n % (8 * 8 * 4 * 130 * 4) == 0
+    assert lib.lq_kv_attention_workspace_bytes(1, 3, 2, 1, 128, 20) == 0  # Hq % H: invalid
+
+
+def test_oracle_attention_matches_torch_sdpa():
+    """oracle.kv_attention (GQA head mapping, bottom-right causal mask) equals
+    torch's scaled_dot_product_attention in float64 on CPU."""
+    import torch
+    from oracle.lq_oracle import kv_attention
+    rng = np.random.default_rng(0)
+    q = rng.standard_normal((2, 6, 4, 32))
+    k = rng.standard_normal((2, 3, 40, 32))
+    v = rng.standard_normal((2, 3, 40, 32))
+    kt = torch.from_numpy(k).repeat_interleave(2, 1)
+    vt = torch.from_numpy(v).repeat_interleave(2, 1)
+    for causal in (False, True):
+        mask = torch.ones(4, 40, dtype=torch.bool).tril(40 - 4) if causal else None
+        ref = torch.nn.functional.scaled_dot_product_attention(torch.from_numpy(q), kt, vt,
+                                                               attn_mask=mask, scale=0.2)
+        assert np.abs(kv_attention(q, k, v, 0.2, causal) - ref.numpy()).max() < 1e-12
+
+
 def _oracle_thresholds(dtype="float32"):
     """Smallest fp32 quotient p at which the reference's code of round_dtype(p)
     reaches i, for i = 1..15 (bisection over fp32 bit patterns)."""
