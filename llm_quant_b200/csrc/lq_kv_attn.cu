@@ -29,7 +29,8 @@
 // multiplies S, a per-channel V scale multiplies O at the end, a per-group V
 // scale multiplies each tile's O contribution.  Where a scale has to enter an
 // f16 operand (per-channel / per-group K scale into q', per-token V scale
-// into P') the operand is normalised by the block's largest scale and split
+// into P') the operand is normalised (q' by the row's largest scale; P' by
+// folding log2 of the scale into the softmax exponent, so P' <= 1) and split
 // into hi + lo f16 halves (two MMAs), which keeps ~22 significant bits.
 // Online softmax in the exp2 domain; per-split partials (unnormalised O,
 // running max, running sum) are merged by kv_attn_combine_kernel.
@@ -100,6 +101,25 @@ __device__ __forceinline__ float ld_f(const uint8_t* p, int64_t i, int dt) {
   if (dt == LQ_F16) return __half2float(reinterpret_cast<const __half*>(p)[i]);
   return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
 }
+// scale / zero-point load: compile-time dtype STC (LQ_F32 / LQ_F16 / LQ_BF16),
+// or the runtime dtype dt when STC < 0
+template <int STC>
+__device__ __forceinline__ float lds(const uint8_t* p, int64_t i, int dt) {
+  if constexpr (STC == LQ_F32) return reinterpret_cast<const float*>(p)[i];
+  else if constexpr (STC == LQ_F16) return __half2float(reinterpret_cast<const __half*>(p)[i]);
+  else if constexpr (STC == LQ_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+  else return ld_f(p, i, dt);
+}
+__device__ __forceinline__ float ex2(float x) {  // 2^x (PTX ex2.approx; -inf -> 0)
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float lg2(float x) {  // log2 x (PTX lg2.approx; 0 -> -inf)
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ void st_f(uint8_t* p, int64_t i, int dt, float v) {
   if (dt == LQ_F32) reinterpret_cast<float*>(p)[i] = v;
   else if (dt == LQ_F16) reinterpret_cast<__half*>(p)[i] = __float2half_rn(v);
@@ -155,27 +175,26 @@ struct Codes<2> {
 
 __device__ __forceinline__ uint32_t zpair(float za, float zb, float bias) { return pack_h2(bias + za, bias + zb); }
 
-template <int D, int CES, int NQ, bool GEN>
+template <int D, int CES, int NQ, bool GEN, bool QLO, int STC>
 __global__ void __launch_bounds__(32 * kAttnWarps) kv_attn_kernel(AttnArgs a) {
   using C = AttnCfg<D, CES>;
   constexpr int NR = 8 * NQ;     // query rows of the block
   constexpr int NKB = C::NKB;
   extern __shared__ __align__(16) uint8_t sm[];
   float* qs = reinterpret_cast<float*>(sm);  // raw q rows [NR][QS]
-  float* red = qs + NR * C::QS;              // [8] block reduction scratch
-  uint8_t* ring = reinterpret_cast<uint8_t*>(red + 8);
+  uint8_t* ring = reinterpret_cast<uint8_t*>(qs + NR * C::QS + 8);  // warps' stage rings
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
   const int split = blockIdx.x, bh = blockIdx.y, zb = blockIdx.z;
   const int b = bh / a.H, h = bh % a.H;
   const int tile_lo = split * a.tiles_per_split;
   const int tile_hi = min(a.n_tiles, tile_lo + a.tiles_per_split);
-  const int t_lo = tile_lo * kTile, t_hi = min(a.T, tile_hi * kTile);
   const int dk0 = c * (D / 4);   // lane's d range in S = K q'^T
   const int dv0 = g * (D / 8);   // lane's d range in O
   const float bias = Codes<CES>::bias;
 
-  // ---- prologue: raw q rows, block-wide scale maxima --------------------
-  for (int idx = threadIdx.x; idx < NR * D; idx += blockDim.x) {
+  // ---- prologue: raw q rows ---------------------------------------------
+#pragma unroll
+  for (int idx = threadIdx.x; idx < NR * D; idx += 32 * kAttnWarps) {
     const int r = idx / D, d = idx % D, qr = zb * NR + r;
     float v = 0.0f;
     if (qr < a.rows) {
@@ -184,22 +203,7 @@ __global__ void __launch_bounds__(32 * kAttnWarps) kv_attn_kernel(AttnArgs a) {
     }
     qs[r * C::QS + (d / (D / 4)) * C::QC + d % (D / 4)] = v;
   }
-  // per-token V: P' = P * vs_t / sigma_v with sigma_v the largest scale of the split
-  float sigma_v = 1.0f;
-  if (a.v.gran == 0) {
-    float m = 0.0f;
-    for (int t = t_lo + threadIdx.x; t < t_hi; t += blockDim.x)
-      m = fmaxf(m, fabsf(ld_f(a.v.scale, (int64_t)bh * a.v.pitch + t, a.s_dtype)));
-#pragma unroll
-    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (lane == 0) red[warp] = m;
-  }
   __syncthreads();
-  if (a.v.gran == 0) {
-    float m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-    sigma_v = (m > 0.0f && m < INFINITY) ? m : 1.0f;
-  }
-  const float inv_sigma_v = 1.0f / sigma_v;
 
   // per-channel sides: the lane's scales / zero pairs, once
   uint32_t zkp[GEN ? NKB : 1][2];   // K zero pairs of (d0, d0+1), (d0+2, d0+3) of k block j
@@ -215,8 +219,8 @@ __global__ void __launch_bounds__(32 * kAttnWarps) kv_attn_kernel(AttnArgs a) {
       float z[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        z[u] = ld_f(zp, base + d0 + u, a.s_dtype);
-        m = fmaxf(m, fabsf(ld_f(sp, base + d0 + u, a.s_dtype)));
+        z[u] = lds<STC>(zp, base + d0 + u, a.s_dtype);
+        m = fmaxf(m, fabsf(lds<STC>(sp, base + d0 + u, a.s_dtype)));
       }
       zkp[j][0] = zpair(z[0], z[1], bias);
       zkp[j][1] = zpair(z[2], z[3], bias);
@@ -230,11 +234,11 @@ __global__ void __launch_bounds__(32 * kAttnWarps) kv_attn_kernel(AttnArgs a) {
 #pragma unroll
     for (int e = 0; e < (GEN ? NKB : 0); ++e) {
       const int d = dv0 + 2 * e;
-      const float z0 = ld_f(zp, base + d, a.s_dtype), z1 = ld_f(zp, base + d + 1, a.s_dtype);
+      const float z0 = lds<STC>(zp, base + d, a.s_dtype), z1 = lds<STC>(zp, base + d + 1, a.s_dtype);
       zvp[e][0] = zpair(z0, z0, bias);
       zvp[e][1] = zpair(z1, z1, bias);
-      vsd[e][0] = ld_f(sp, base + d, a.s_dtype);
-      vsd[e][1] = ld_f(sp, base + d + 1, a.s_dtype);
+      vsd[e][0] = lds<STC>(sp, base + d, a.s_dtype);
+      vsd[e][1] = lds<STC>(sp, base + d + 1, a.s_dtype);
     }
   };
   if constexpr (GEN) {
@@ -243,7 +247,7 @@ __global__ void __launch_bounds__(32 * kAttnWarps) kv_attn_kernel(AttnArgs a) {
   }
 
   // q' = q (* scale_d / sigma_k for a per-channel / per-group K) as f16 hi / lo
-  uint32_t bq[NQ][NKB][2], bql[NQ][NKB][2];
+  uint32_t bq[NQ][NKB][2], bql[QLO ? NQ : 1][QLO ? NKB : 1][2];
   auto make_q = [&](const uint8_t* sp, int64_t base, bool scaled) {
     const float inv = 1.0f / sigma_k;
 #pragma unroll
@@ -255,10 +259,15 @@ __global__ void __launch_bounds__(32 * kAttnWarps) kv_attn_kernel(AttnArgs a) {
         float x[4] = {v4.x, v4.y, v4.z, v4.w};
         if (GEN && scaled) {
 #pragma unroll
-          for (int u = 0; u < 4; ++u) x[u] *= ld_f(sp, base + dk0 + 4 * j + u, a.s_dtype) * inv;
+          for (int u = 0; u < 4; ++u) x[u] *= lds<STC>(sp, base + dk0 + 4 * j + u, a.s_dtype) * inv;
         }
-        split_h2(x[0], x[1], bq[nq][j][0], bql[nq][j][0]);
-        split_h2(x[2], x[3], bq[nq][j][1], bql[nq][j][1]);
+        if constexpr (QLO) {
+          split_h2(x[0], x[1], bq[nq][j][0], bql[nq][j][0]);
+          split_h2(x[2], x[3], bq[nq][j][1], bql[nq][j][1]);
+        } else {
+          bq[nq][j][0] = pack_h2(x[0], x[1]);
+          bq[nq][j][1] = pack_h2(x[2], x[3]);
+        }
       }
     }
   };
@@ -286,35 +295,39 @@ __global__ void __launch_bounds__(32 * kAttnWarps) kv_attn_kernel(AttnArgs a) {
   // ---- main loop over this warp's tiles ----------------------------------
   uint8_t* ring_w = ring + (size_t)warp * C::STAGES * a.stage_bytes;
   const int n_my = tile_hi > tile_lo + warp ? (tile_hi - tile_lo - warp + kAttnWarps - 1) / kAttnWarps : 0;
+  // per-(b, h) bases of the codes and scale rows; per tile only t0 moves
+  const uint8_t* kbase = a.k.codes + (int64_t)bh * a.cap * C::RB;
+  const uint8_t* vbase = a.v.codes + (int64_t)bh * a.cap * C::RB;
+  const int64_t ksrow = (int64_t)bh * a.k.pitch * (a.k.gran == 0 ? a.ses : D * a.ses);
+  const int64_t vsrow = (int64_t)bh * a.v.pitch * (a.v.gran == 0 ? a.ses : D * a.ses);
+  const int lr = lane / C::CPR, lj = lane % C::CPR;  // row / chunk of the lane's first chunk
   auto issue = [&](int tb, uint8_t* st) {
     const int t0 = tb * kTile;
-    const uint8_t* kc = a.k.codes + ((int64_t)bh * a.cap + t0) * C::RB;
-    const uint8_t* vc = a.v.codes + ((int64_t)bh * a.cap + t0) * C::RB;
+    const uint8_t* kc = kbase + t0 * C::RB + lane * 16;
+    const uint8_t* vc = vbase + t0 * C::RB + lane * 16;
 #pragma unroll
-    for (int qi = lane; qi < kTile * C::CPR; qi += 32) {
-      const int r = qi / C::CPR, j = qi % C::CPR;
-      const int off = r * C::RB + ((j ^ swz<C::CPR>(r)) << 4);
-      cp16(st + off, kc + qi * 16);
-      cp16(st + C::KB + off, vc + qi * 16);
+    for (int i = 0; i < kTile * C::CPR / 32; ++i) {  // chunk lane + 32 i: row lr + i (32 / CPR)
+      const int r = lr + i * (32 / C::CPR);
+      const int off = r * C::RB + ((lj ^ swz<C::CPR>(r)) << 4);
+      cp16(st + off, kc + 512 * i);
+      cp16(st + C::KB + off, vc + 512 * i);
     }
-    auto side = [&](const KvSide& s) {
+    auto side = [&](const KvSide& s, int64_t base) {
       if (s.bytes == 0) return;
-      const int64_t row = s.gran == 0 ? (int64_t)bh * s.pitch * a.ses + (int64_t)t0 * a.ses
-                                      : ((int64_t)bh * s.pitch + t0 / s.group) * D * a.ses;
-      for (int qi = lane; qi < s.bytes / 16; qi += 32) {
-        cp16(st + s.off_s + qi * 16, s.scale + row + qi * 16);
-        cp16(st + s.off_z + qi * 16, s.zp + row + qi * 16);
+      const int64_t row = base + (s.gran == 0 ? (int64_t)t0 * a.ses : (int64_t)(t0 / s.group) * D * a.ses);
+      if (lane < s.bytes / 16) {  // at most 32 chunks per row
+        cp16(st + s.off_s + lane * 16, s.scale + row + lane * 16);
+        cp16(st + s.off_z + lane * 16, s.zp + row + lane * 16);
       }
     };
-    side(a.k);
-    side(a.v);
+    side(a.k, ksrow);
+    side(a.v, vsrow);
   };
 #pragma unroll
   for (int s = 0; s < C::STAGES; ++s) {
     if (s < n_my) issue(tile_lo + warp + kAttnWarps * s, ring_w + s * a.stage_bytes);
     cp_commit();
   }
-  const bool qlo = a.qlo != 0;
   for (int it = 0; it < n_my; ++it) {
     const int tb = tile_lo + warp + kAttnWarps * it;
     const int t0 = tb * kTile;
@@ -330,10 +343,10 @@ __global__ void __launch_bounds__(32 * kAttnWarps) kv_attn_kernel(AttnArgs a) {
     if (!GEN || a.k.gran == 0) {
       const uint8_t* ksp = st + a.k.off_s;
       const uint8_t* kzp = st + a.k.off_z;
-      ks_g = ld_f(ksp, g, a.s_dtype);
-      ks_g8 = ld_f(ksp, g + 8, a.s_dtype);
-      const float z0 = tg < a.T ? ld_f(kzp, g, a.s_dtype) : 0.0f;
-      const float z1 = tg8 < a.T ? ld_f(kzp, g + 8, a.s_dtype) : 0.0f;
+      ks_g = lds<STC>(ksp, g, a.s_dtype);
+      ks_g8 = lds<STC>(ksp, g + 8, a.s_dtype);
+      const float z0 = tg < a.T ? lds<STC>(kzp, g, a.s_dtype) : 0.0f;
+      const float z1 = tg8 < a.T ? lds<STC>(kzp, g + 8, a.s_dtype) : 0.0f;
       zk_g = zpair(z0, z0, bias);
       zk_g8 = zpair(z1, z1, bias);
     } else if (GEN && a.k.gran == 2) {
@@ -343,11 +356,11 @@ __global__ void __launch_bounds__(32 * kAttnWarps) kv_attn_kernel(AttnArgs a) {
     if (GEN && a.v.gran == 2) fill_v_rows(st + a.v.off_s, st + a.v.off_z, 0);
 
     // ---- S = K q'^T ----
-    float S[NQ][4];
+    float S[NQ][4], S1[NQ][4];  // even / odd k blocks: two MMA chains
 #pragma unroll
     for (int nq = 0; nq < NQ; ++nq)
 #pragma unroll
-      for (int u = 0; u < 4; ++u) S[nq][u] = 0.0f;
+      for (int u = 0; u < 4; ++u) S[nq][u] = S1[nq][u] = 0.0f;
     uint32_t kw[2][C::LKC * 4];
 #pragma unroll
     for (int rr = 0; rr < 2; ++rr) {
@@ -387,10 +400,15 @@ __global__ void __launch_bounds__(32 * kAttnWarps) kv_attn_kernel(AttnArgs a) {
       }
 #pragma unroll
       for (int nq = 0; nq < NQ; ++nq) {
-        mma_f16(S[nq], ka, bq[nq][j][0], bq[nq][j][1]);
-        if (qlo) mma_f16(S[nq], ka, bql[nq][j][0], bql[nq][j][1]);
+        float* acc = (j & 1) ? S1[nq] : S[nq];
+        mma_f16(acc, ka, bq[nq][j][0], bq[nq][j][1]);
+        if constexpr (QLO) mma_f16(acc, ka, bql[nq][j][0], bql[nq][j][1]);
       }
     }
+#pragma unroll
+    for (int nq = 0; nq < NQ; ++nq)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) S[nq][u] += S1[nq][u];
 
     // ---- scale, mask, online softmax ----
     float fk0, fk1;
@@ -400,40 +418,51 @@ __global__ void __launch_bounds__(32 * kAttnWarps) kv_attn_kernel(AttnArgs a) {
     } else {
       fk0 = fk1 = sigma_k * a.sm_log2;
     }
-    float vf0 = 1.0f, vf1 = 1.0f;  // P' = P * vf (per-token V)
-    if (!GEN || a.v.gran == 0) {
-      vf0 = tg < a.T ? ld_f(st + a.v.off_s, g, a.s_dtype) * inv_sigma_v : 0.0f;
-      vf1 = tg8 < a.T ? ld_f(st + a.v.off_s, g + 8, a.s_dtype) * inv_sigma_v : 0.0f;
+    // per-token V: P' = P * vs_t, taken as exp2(s + log2(vs_t) - m') with the
+    // running max m' over s + log2(vs_t), so P' <= 1 fits the f16 operand;
+    // the softmax denominator sums exp2(s - m') separately
+    const bool vtok = !GEN || a.v.gran == 0;
+    float lv0 = 0.0f, lv1 = 0.0f;
+    if (vtok) {
+      lv0 = tg < a.T ? lg2(lds<STC>(st + a.v.off_s, g, a.s_dtype)) : 0.0f;
+      lv1 = tg8 < a.T ? lg2(lds<STC>(st + a.v.off_s, g + 8, a.s_dtype)) : 0.0f;
     }
     uint32_t pb[NQ][2], pbl[NQ][2];
 #pragma unroll
     for (int nq = 0; nq < NQ; ++nq) {
-      float p[4];
+      float p[4], alpha[2];
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const float s0 = tg <= lim[nq][e] ? S[nq][e] * fk0 : -INFINITY;
         const float s1 = tg8 <= lim[nq][e] ? S[nq][2 + e] * fk1 : -INFINITY;
-        float mt = fmaxf(s0, s1);
+        const float w0 = s0 + lv0, w1 = s1 + lv1;
+        float mt = fmaxf(w0, w1);
         mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
         mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
         mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
         const float mnew = fmaxf(mrun[nq][e], mt);
         const float mref = mnew == -INFINITY ? 0.0f : mnew;
-        const float alpha = exp2f(mrun[nq][e] - mref);
-        p[e] = exp2f(s0 - mref);
-        p[2 + e] = exp2f(s1 - mref);
-        lrun[nq][e] = lrun[nq][e] * alpha + p[e] + p[2 + e];
+        alpha[e] = mnew > mrun[nq][e] ? ex2(mrun[nq][e] - mref) : 1.0f;
+        p[e] = ex2(w0 - mref);
+        p[2 + e] = ex2(w1 - mref);
+        const float den = vtok ? ex2(s0 - mref) + ex2(s1 - mref) : p[e] + p[2 + e];
+        lrun[nq][e] = lrun[nq][e] * alpha[e] + den;
         mrun[nq][e] = mnew;
+      }
+      // rescale O only when a running max of the warp's columns grew
+      if (__any_sync(0xffffffffu, alpha[0] != 1.0f || alpha[1] != 1.0f)) {
 #pragma unroll
         for (int d = 0; d < NKB; ++d) {
-          O[nq][d][e] *= alpha;
-          O[nq][d][2 + e] *= alpha;
+          O[nq][d][0] *= alpha[0];
+          O[nq][d][1] *= alpha[1];
+          O[nq][d][2] *= alpha[0];
+          O[nq][d][3] *= alpha[1];
         }
       }
       // P' rows t = g (tokens 0-7 block) and t = g + 8, columns 2c, 2c+1
       uint32_t x0, x1, l0, l1;
-      split_h2(p[0] * vf0, p[1] * vf0, x0, l0);
-      split_h2(p[2] * vf1, p[3] * vf1, x1, l1);
+      split_h2(p[0], p[1], x0, l0);
+      split_h2(p[2], p[3], x1, l1);
       pb[nq][0] = trans8x8(x0);
       pb[nq][1] = trans8x8(x1);
       pbl[nq][0] = trans8x8(l0);
@@ -474,10 +503,10 @@ __global__ void __launch_bounds__(32 * kAttnWarps) kv_attn_kernel(AttnArgs a) {
     if (!GEN || a.v.gran == 0) {
       const uint8_t* vzp = st + a.v.off_z;
       const int ra = 2 * c, rb = 2 * c + 8;
-      const float z0 = t0 + ra < a.T ? ld_f(vzp, ra, a.s_dtype) : 0.0f;
-      const float z1 = t0 + ra + 1 < a.T ? ld_f(vzp, ra + 1, a.s_dtype) : 0.0f;
-      const float z2 = t0 + rb < a.T ? ld_f(vzp, rb, a.s_dtype) : 0.0f;
-      const float z3 = t0 + rb + 1 < a.T ? ld_f(vzp, rb + 1, a.s_dtype) : 0.0f;
+      const float z0 = t0 + ra < a.T ? lds<STC>(vzp, ra, a.s_dtype) : 0.0f;
+      const float z1 = t0 + ra + 1 < a.T ? lds<STC>(vzp, ra + 1, a.s_dtype) : 0.0f;
+      const float z2 = t0 + rb < a.T ? lds<STC>(vzp, rb, a.s_dtype) : 0.0f;
+      const float z3 = t0 + rb + 1 < a.T ? lds<STC>(vzp, rb + 1, a.s_dtype) : 0.0f;
       zv_a = zpair(z0, z1, bias);
       zv_b = zpair(z2, z3, bias);
     }
@@ -563,12 +592,10 @@ __global__ void __launch_bounds__(32 * kAttnWarps) kv_attn_kernel(AttnArgs a) {
     }
 #pragma unroll
     for (int e = 0; e < NKB; ++e) {
-      float f0 = sigma_v, f1 = sigma_v;
+      float f0 = 1.0f, f1 = 1.0f;
       if (GEN && a.v.gran == 1) {
         f0 = vsd[GEN ? e : 0][0];
         f1 = vsd[GEN ? e : 0][1];
-      } else if (GEN && a.v.gran == 2) {
-        f0 = f1 = 1.0f;
       }
       O[nq][e][0] *= f0;
       O[nq][e][1] *= f0;
@@ -612,7 +639,7 @@ __global__ void __launch_bounds__(32 * kAttnWarps) kv_attn_kernel(AttnArgs a) {
     if (M != -INFINITY) {
 #pragma unroll
       for (int w = 0; w < kAttnWarps; ++w) {
-        const float f = exp2f(mb[w * NR + r] - M);
+        const float f = ex2(mb[w * NR + r] - M);
         o = fmaf(f, ob[(w * NR + r) * D + d], o);
         L = fmaf(f, lb[w * NR + r], L);
       }
@@ -631,80 +658,119 @@ __global__ void __launch_bounds__(32 * kAttnWarps) kv_attn_kernel(AttnArgs a) {
   }
 }
 
-// One warp per (b, h, row): merge the splits' (O, max, sum) partials.
+// One thread per output element (b, h, row, d): merge the splits' (O, max,
+// sum) partials; the (max, sum) pairs of a row are read by all its threads
+// (L1 broadcast).
 __global__ void __launch_bounds__(128) kv_attn_combine_kernel(const float* __restrict__ ws, int n_split,
                                                               int rows, int D, int H, int Hq, int Sq,
                                                               int G, int64_t n_items, uint8_t* out,
                                                               int out_dtype) {
-  const int64_t item = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (item >= n_items) return;
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= n_items * D) return;
+  const int64_t item = e / D;
+  const int d = (int)(e % D);
   const int64_t bh = item / rows;
   const int qr = (int)(item % rows);
   const float* base = ws + (bh * n_split * rows + qr) * (int64_t)(D + 2);
   const int64_t sstride = (int64_t)rows * (D + 2);
   float M = -INFINITY;
-  for (int s = 0; s < n_split; ++s) M = fmaxf(M, base[s * sstride + D]);
+  for (int s = 0; s < n_split; ++s) M = fmaxf(M, __ldg(base + s * sstride + D));
+  float o = 0.0f, L = 0.0f;
+  if (M != -INFINITY) {
+#pragma unroll 4
+    for (int s = 0; s < n_split; ++s) {
+      const float* p = base + s * sstride;
+      const float f = ex2(__ldg(p + D) - M);
+      o = fmaf(f, __ldg(p + d), o);
+      L = fmaf(f, __ldg(p + D + 1), L);
+    }
+  }
   const int b = (int)(bh / H), h = (int)(bh % H);
   const int hq = h * G + qr / Sq, i = qr % Sq;
-  const int64_t obase = (((int64_t)b * Hq + hq) * Sq + i) * D;
-  for (int d = lane; d < D; d += 32) {
-    float o = 0.0f, L = 0.0f;
-    if (M != -INFINITY) {
-      for (int s = 0; s < n_split; ++s) {
-        const float* p = base + s * sstride;
-        const float f = exp2f(p[D] - M);
-        o = fmaf(f, p[d], o);
-        L = fmaf(f, p[D + 1], L);
-      }
-    }
-    st_f(out, obase + d, out_dtype, o / L);
-  }
+  st_f(out, (((int64_t)b * Hq + hq) * Sq + i) * D + d, out_dtype, o / L);
 }
 
-// Token splits: enough blocks for ~2 waves at 3 resident blocks per SM, at
-// least 4 tiles (one per warp) per split; tiles per split a multiple of 4.
+// SMs of the current device (148 on B200; 148 when there is none, for the
+// workspace query on a host without a GPU).
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return 148;
+  }
+  if (!cached[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = 148;
+    }
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+// Token splits: one wave of blocks (4 resident per SM for the per-token
+// variants), each as long as possible -- the pipeline fill, the q prologue
+// and the warp merge are paid once per block -- with at least 4 tiles (one
+// per warp) per split.
 struct SplitPlan {
   int n_tiles, n_split, tiles_per_split;
 };
 SplitPlan plan_split(int64_t BH, int64_t row_blocks, int64_t T) {
   SplitPlan p;
   p.n_tiles = (int)((T + kTile - 1) / kTile);
-  const int64_t want = (2 * 148 * 3 + BH * row_blocks - 1) / (BH * row_blocks);
-  int64_t ns = std::max<int64_t>(1, std::min<int64_t>(want, p.n_tiles / 4));
-  int tps = (int)((p.n_tiles + ns - 1) / ns);
-  tps = (tps + 3) / 4 * 4;
-  p.tiles_per_split = tps;
-  p.n_split = (p.n_tiles + tps - 1) / tps;
+  const int64_t slots = (int64_t)sm_count() * 4;
+  int64_t ns = std::max<int64_t>(1, slots / (BH * row_blocks));
+  ns = std::min<int64_t>(ns, std::max(1, p.n_tiles / kAttnWarps));
+  p.tiles_per_split = (int)((p.n_tiles + ns - 1) / ns);
+  p.n_split = (p.n_tiles + p.tiles_per_split - 1) / p.tiles_per_split;
   return p;
 }
 
-template <int D, int CES, int NQ, bool GEN>
+template <int D, int CES, int NQ, bool GEN, bool QLO, int STC>
 int launch_attn(const AttnArgs& a, int B, int row_blocks, int combine_items, cudaStream_t st) {
   using C = AttnCfg<D, CES>;
   constexpr int NR = 8 * NQ;
   const size_t ring = (size_t)kAttnWarps * C::STAGES * a.stage_bytes;
   const size_t merge = (size_t)kAttnWarps * NR * (D + 2) * 4;
   const size_t smem = (size_t)NR * C::QS * 4 + 32 + std::max(ring, merge);
-  auto kern = kv_attn_kernel<D, CES, NQ, GEN>;
+  auto kern = kv_attn_kernel<D, CES, NQ, GEN, QLO, STC>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return launched("kv_attn_kernel (attribute)");
   dim3 grid(a.n_split, B * a.H, row_blocks);
   kern<<<grid, 32 * kAttnWarps, smem, st>>>(a);
   int rc = launched("kv_attn_kernel");
   if (rc != LQ_OK || a.n_split == 1) return rc;
-  kv_attn_combine_kernel<<<(combine_items + 3) / 4, 128, 0, st>>>(a.ws, a.n_split, a.rows, D, a.H, a.Hq,
+  kv_attn_combine_kernel<<<(combine_items * D + 127) / 128, 128, 0, st>>>(a.ws, a.n_split, a.rows, D, a.H, a.Hq,
                                                                    a.Sq, a.G, combine_items, a.out,
                                                                    a.q_dtype);
   return launched("kv_attn_combine_kernel");
 }
 
+template <int D, int CES, int NQ>
+int attn_dispatch_nq(const AttnArgs& a, int B, bool gen, int row_blocks, int items, cudaStream_t st) {
+  // a per-token K with an f16 / bf16 query needs no lo half of q'
+  // the all-per-token path is compiled per scale dtype; the general one reads
+  // scales with a runtime dtype switch
+  if (gen) return launch_attn<D, CES, NQ, true, true, -1>(a, B, row_blocks, items, st);
+  switch (a.s_dtype) {
+    case LQ_F32:
+      return a.qlo ? launch_attn<D, CES, NQ, false, true, LQ_F32>(a, B, row_blocks, items, st)
+                   : launch_attn<D, CES, NQ, false, false, LQ_F32>(a, B, row_blocks, items, st);
+    case LQ_F16:
+      return a.qlo ? launch_attn<D, CES, NQ, false, true, LQ_F16>(a, B, row_blocks, items, st)
+                   : launch_attn<D, CES, NQ, false, false, LQ_F16>(a, B, row_blocks, items, st);
+    default:
+      return a.qlo ? launch_attn<D, CES, NQ, false, true, LQ_BF16>(a, B, row_blocks, items, st)
+                   : launch_attn<D, CES, NQ, false, false, LQ_BF16>(a, B, row_blocks, items, st);
+  }
+}
+
 template <int D, int CES>
 int attn_dispatch(const AttnArgs& a, int B, int nq, bool gen, int row_blocks, int items, cudaStream_t st) {
-  if (nq == 1) return gen ? launch_attn<D, CES, 1, true>(a, B, row_blocks, items, st)
-                          : launch_attn<D, CES, 1, false>(a, B, row_blocks, items, st);
-  return gen ? launch_attn<D, CES, 2, true>(a, B, row_blocks, items, st)
-             : launch_attn<D, CES, 2, false>(a, B, row_blocks, items, st);
+  return nq == 1 ? attn_dispatch_nq<D, CES, 1>(a, B, gen, row_blocks, items, st)
+                 : attn_dispatch_nq<D, CES, 2>(a, B, gen, row_blocks, items, st);
 }
 
 }  // namespace
