@@ -175,8 +175,9 @@ struct Codes<2> {
 
 __device__ __forceinline__ uint32_t zpair(float za, float zb, float bias) { return pack_h2(bias + za, bias + zb); }
 
+// the 8-row per-token variants are held to 128 registers (4 blocks per SM)
 template <int D, int CES, int NQ, bool GEN, bool QLO, int STC>
-__global__ void __launch_bounds__(32 * kAttnWarps) kv_attn_kernel(AttnArgs a) {
+__global__ void __launch_bounds__(32 * kAttnWarps, (NQ == 1 && !GEN) ? 4 : 1) kv_attn_kernel(AttnArgs a) {
   using C = AttnCfg<D, CES>;
   constexpr int NR = 8 * NQ;     // query rows of the block
   constexpr int NKB = C::NKB;
@@ -293,7 +294,27 @@ __global__ void __launch_bounds__(32 * kAttnWarps) kv_attn_kernel(AttnArgs a) {
       for (int u = 0; u < 4; ++u) O[nq][e][u] = 0.0f;
 
   // ---- main loop over this warp's tiles ----------------------------------
-  uint8_t* ring_w = ring + (size_t)warp * C::STAGES * a.stage_bytes;
+  // stage layout: K tile, V tile, then K scale / zero and V scale / zero rows;
+  // compile-time on the all-per-token path (16 tokens x the scale size each)
+  constexpr int SES = STC == LQ_F32 ? 4 : 2;
+  const int SB = GEN ? a.stage_bytes : 2 * C::KB + 64 * SES;
+  const int kso = GEN ? a.k.off_s : 2 * C::KB, kzo = GEN ? a.k.off_z : 2 * C::KB + 16 * SES;
+  const int vso = GEN ? a.v.off_s : 2 * C::KB + 32 * SES, vzo = GEN ? a.v.off_z : 2 * C::KB + 48 * SES;
+  uint8_t* ring_w = ring + (size_t)warp * C::STAGES * SB;
+  // lane-constant byte offsets inside a stage: K rows g (g + 8: + 8 rows,
+  // same swizzle), V rows 2c, 2c+1 (2c+8, 2c+9: + 8 rows)
+  int koff[C::LKC];
+#pragma unroll
+  for (int i = 0; i < C::LKC; ++i) koff[i] = g * C::RB + (((c * C::LKC + i) ^ swz<C::CPR>(g)) << 4);
+  constexpr int NVC = C::VB >= 16 ? C::VB / 16 : 1;
+  int voff[2][NVC];
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const int r = 2 * c + e, byte0 = dv0 * CES;
+#pragma unroll
+    for (int i = 0; i < NVC; ++i)
+      voff[e][i] = C::KB + r * C::RB + (((byte0 / 16 + i) ^ swz<C::CPR>(r)) << 4) + (C::VB >= 16 ? 0 : (byte0 & 15));
+  }
   const int n_my = tile_hi > tile_lo + warp ? (tile_hi - tile_lo - warp + kAttnWarps - 1) / kAttnWarps : 0;
   // per-(b, h) bases of the codes and scale rows; per tile only t0 moves
   const uint8_t* kbase = a.k.codes + (int64_t)bh * a.cap * C::RB;
@@ -301,37 +322,43 @@ __global__ void __launch_bounds__(32 * kAttnWarps) kv_attn_kernel(AttnArgs a) {
   const int64_t ksrow = (int64_t)bh * a.k.pitch * (a.k.gran == 0 ? a.ses : D * a.ses);
   const int64_t vsrow = (int64_t)bh * a.v.pitch * (a.v.gran == 0 ? a.ses : D * a.ses);
   const int lr = lane / C::CPR, lj = lane % C::CPR;  // row / chunk of the lane's first chunk
+  int ioff[kTile * C::CPR / 32];  // stage offsets of the lane's chunks lane + 32 i
+#pragma unroll
+  for (int i = 0; i < kTile * C::CPR / 32; ++i) {
+    const int r = lr + i * (32 / C::CPR);
+    ioff[i] = r * C::RB + ((lj ^ swz<C::CPR>(r)) << 4);
+  }
   auto issue = [&](int tb, uint8_t* st) {
     const int t0 = tb * kTile;
     const uint8_t* kc = kbase + t0 * C::RB + lane * 16;
     const uint8_t* vc = vbase + t0 * C::RB + lane * 16;
 #pragma unroll
-    for (int i = 0; i < kTile * C::CPR / 32; ++i) {  // chunk lane + 32 i: row lr + i (32 / CPR)
-      const int r = lr + i * (32 / C::CPR);
-      const int off = r * C::RB + ((lj ^ swz<C::CPR>(r)) << 4);
-      cp16(st + off, kc + 512 * i);
-      cp16(st + C::KB + off, vc + 512 * i);
+    for (int i = 0; i < kTile * C::CPR / 32; ++i) {
+      cp16(st + ioff[i], kc + 512 * i);
+      cp16(st + C::KB + ioff[i], vc + 512 * i);
     }
-    auto side = [&](const KvSide& s, int64_t base) {
+    auto side = [&](const KvSide& s, int64_t base, int so, int zo) {
       if (s.bytes == 0) return;
       const int64_t row = base + (s.gran == 0 ? (int64_t)t0 * a.ses : (int64_t)(t0 / s.group) * D * a.ses);
       if (lane < s.bytes / 16) {  // at most 32 chunks per row
-        cp16(st + s.off_s + lane * 16, s.scale + row + lane * 16);
-        cp16(st + s.off_z + lane * 16, s.zp + row + lane * 16);
+        cp16(st + so + lane * 16, s.scale + row + lane * 16);
+        cp16(st + zo + lane * 16, s.zp + row + lane * 16);
       }
     };
-    side(a.k, ksrow);
-    side(a.v, vsrow);
+    side(a.k, ksrow, kso, kzo);
+    side(a.v, vsrow, vso, vzo);
   };
 #pragma unroll
   for (int s = 0; s < C::STAGES; ++s) {
-    if (s < n_my) issue(tile_lo + warp + kAttnWarps * s, ring_w + s * a.stage_bytes);
+    if (s < n_my) issue(tile_lo + warp + kAttnWarps * s, ring_w + s * SB);
     cp_commit();
   }
+  int slot = 0;
   for (int it = 0; it < n_my; ++it) {
     const int tb = tile_lo + warp + kAttnWarps * it;
     const int t0 = tb * kTile;
-    uint8_t* st = ring_w + (it % C::STAGES) * a.stage_bytes;
+    uint8_t* st = ring_w + slot * SB;
+    slot = slot + 1 == C::STAGES ? 0 : slot + 1;
     cp_wait<C::STAGES - 1>();
     __syncwarp();
     const bool full_tile = t0 + kTile <= a.T;
@@ -341,8 +368,8 @@ __global__ void __launch_bounds__(32 * kAttnWarps) kv_attn_kernel(AttnArgs a) {
     float ks_g = 1.0f, ks_g8 = 1.0f;
     uint32_t zk_g = 0, zk_g8 = 0;
     if (!GEN || a.k.gran == 0) {
-      const uint8_t* ksp = st + a.k.off_s;
-      const uint8_t* kzp = st + a.k.off_z;
+      const uint8_t* ksp = st + kso;
+      const uint8_t* kzp = st + kzo;
       ks_g = lds<STC>(ksp, g, a.s_dtype);
       ks_g8 = lds<STC>(ksp, g + 8, a.s_dtype);
       const float z0 = tg < a.T ? lds<STC>(kzp, g, a.s_dtype) : 0.0f;
@@ -350,10 +377,10 @@ __global__ void __launch_bounds__(32 * kAttnWarps) kv_attn_kernel(AttnArgs a) {
       zk_g = zpair(z0, z0, bias);
       zk_g8 = zpair(z1, z1, bias);
     } else if (GEN && a.k.gran == 2) {
-      fill_k_rows(st + a.k.off_s, st + a.k.off_z, 0, true);
-      make_q(st + a.k.off_s, 0, true);
+      fill_k_rows(st + kso, st + kzo, 0, true);
+      make_q(st + kso, 0, true);
     }
-    if (GEN && a.v.gran == 2) fill_v_rows(st + a.v.off_s, st + a.v.off_z, 0);
+    if (GEN && a.v.gran == 2) fill_v_rows(st + vso, st + vzo, 0);
 
     // ---- S = K q'^T ----
     float S[NQ][4], S1[NQ][4];  // even / odd k blocks: two MMA chains
@@ -364,11 +391,9 @@ __global__ void __launch_bounds__(32 * kAttnWarps) kv_attn_kernel(AttnArgs a) {
     uint32_t kw[2][C::LKC * 4];
 #pragma unroll
     for (int rr = 0; rr < 2; ++rr) {
-      const int r = g + 8 * rr;
 #pragma unroll
       for (int i = 0; i < C::LKC; ++i) {
-        const int j = c * C::LKC + i;
-        const uint4 w = *reinterpret_cast<const uint4*>(st + r * C::RB + ((j ^ swz<C::CPR>(r)) << 4));
+        const uint4 w = *reinterpret_cast<const uint4*>(st + koff[i] + 8 * C::RB * rr);
         kw[rr][4 * i] = w.x;
         kw[rr][4 * i + 1] = w.y;
         kw[rr][4 * i + 2] = w.z;
@@ -424,8 +449,8 @@ __global__ void __launch_bounds__(32 * kAttnWarps) kv_attn_kernel(AttnArgs a) {
     const bool vtok = !GEN || a.v.gran == 0;
     float lv0 = 0.0f, lv1 = 0.0f;
     if (vtok) {
-      lv0 = tg < a.T ? lg2(lds<STC>(st + a.v.off_s, g, a.s_dtype)) : 0.0f;
-      lv1 = tg8 < a.T ? lg2(lds<STC>(st + a.v.off_s, g + 8, a.s_dtype)) : 0.0f;
+      lv0 = tg < a.T ? lg2(lds<STC>(st + vso, g, a.s_dtype)) : 0.0f;
+      lv1 = tg8 < a.T ? lg2(lds<STC>(st + vso, g + 8, a.s_dtype)) : 0.0f;
     }
     uint32_t pb[NQ][2], pbl[NQ][2];
 #pragma unroll
@@ -476,32 +501,29 @@ __global__ void __launch_bounds__(32 * kAttnWarps) kv_attn_kernel(AttnArgs a) {
 #pragma unroll
     for (int q4 = 0; q4 < 4; ++q4) {
       const int r = 2 * c + (q4 & 1) + 8 * (q4 >> 1);
-      const int byte0 = dv0 * CES;
+      const uint8_t* vp = st + 8 * C::RB * (q4 >> 1);
       if constexpr (C::VB >= 16) {
 #pragma unroll
         for (int i = 0; i < C::VB / 16; ++i) {
-          const int j = byte0 / 16 + i;
-          const uint4 w = *reinterpret_cast<const uint4*>(st + C::KB + r * C::RB + ((j ^ swz<C::CPR>(r)) << 4));
+          const uint4 w = *reinterpret_cast<const uint4*>(vp + voff[q4 & 1][i]);
           vw[q4][4 * i] = w.x;
           vw[q4][4 * i + 1] = w.y;
           vw[q4][4 * i + 2] = w.z;
           vw[q4][4 * i + 3] = w.w;
         }
-      } else {  // 8 bytes: half of chunk byte0 / 16
-        const int j = byte0 / 16;
-        const uint2 w = *reinterpret_cast<const uint2*>(st + C::KB + r * C::RB + ((j ^ swz<C::CPR>(r)) << 4) +
-                                                        (byte0 & 15));
+      } else {  // 8 bytes: half of a chunk
+        const uint2 w = *reinterpret_cast<const uint2*>(vp + voff[q4 & 1][0]);
         vw[q4][0] = w.x;
         vw[q4][1] = w.y;
       }
       if (!full_tile && t0 + r >= a.T) {  // past the end: unwritten codes -> 0
 #pragma unroll
-        for (int i = 0; i < VWORDS; ++i) vw[q4][i] = CES == 1 ? 0u : 0u;
+        for (int i = 0; i < VWORDS; ++i) vw[q4][i] = 0u;
       }
     }
     uint32_t zv_a = 0, zv_b = 0;  // per-token V zero pairs of rows (2c, 2c+1), (2c+8, 2c+9)
     if (!GEN || a.v.gran == 0) {
-      const uint8_t* vzp = st + a.v.off_z;
+      const uint8_t* vzp = st + vzo;
       const int ra = 2 * c, rb = 2 * c + 8;
       const float z0 = t0 + ra < a.T ? lds<STC>(vzp, ra, a.s_dtype) : 0.0f;
       const float z1 = t0 + ra + 1 < a.T ? lds<STC>(vzp, ra + 1, a.s_dtype) : 0.0f;
