@@ -696,10 +696,11 @@ __global__ void __launch_bounds__(128) kv_attn_combine_kernel(const float* __res
   const float* base = ws + (bh * n_split * rows + qr) * (int64_t)(D + 2);
   const int64_t sstride = (int64_t)rows * (D + 2);
   float M = -INFINITY;
+#pragma unroll 8
   for (int s = 0; s < n_split; ++s) M = fmaxf(M, __ldg(base + s * sstride + D));
   float o = 0.0f, L = 0.0f;
   if (M != -INFINITY) {
-#pragma unroll 4
+#pragma unroll 8
     for (int s = 0; s < n_split; ++s) {
       const float* p = base + s * sstride;
       const float f = ex2(__ldg(p + D) - M);
