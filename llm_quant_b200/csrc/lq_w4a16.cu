@@ -7,17 +7,19 @@
 // Tile = 128 weight rows x BT tokens ("swap AB"): the dequantized weights are
 // the MMA's A operand and live in tensor memory, the activations are the B
 // operand (TMA, 128-byte swizzle, K-major), the fp32 accumulator D[128, BT]
-// is in tensor memory.  Warp roles (192 threads):
+// is in tensor memory.  Warp roles (320 threads):
 //   warp 0      TMA producer: activation tile + packed 4-bit weight tile +
 //               (zero, scale) pairs per stage, one mbarrier per stage each;
 //   warp 1      allocates tensor memory, one lane issues tcgen05.mma
 //               (4 x K=16 per 64-wide K step) and tcgen05.commit;
-//   warps 2..5  dequantize: thread = one weight row, 64 codes per stage ->
-//               32 packed fp16/bf16 pairs -> tcgen05.st into the A slot of
-//               the stage; afterwards they are the epilogue (tcgen05.ld of
-//               the accumulator, + bias, convert, store y).
-// Warp w may only touch tensor-memory lanes 32*(w%4)..+31, so warps 2,3,4,5
-// own weight rows 64..95, 96..127, 0..31, 32..63 of the tile.
+//   warps 2..9  dequantize: thread = one weight row and half of the K step,
+//               32 codes per stage -> 16 packed fp16/bf16 pairs ->
+//               tcgen05.st into its half of the stage's A slot; afterwards
+//               they are the epilogue (tcgen05.ld of the accumulator, + bias,
+//               convert, store y).  Two warps per tensor-memory lane quarter
+//               keep one converting while the other waits on its store.
+// Warp w may only touch tensor-memory lanes 32*(w%4)..+31, so warps 2..5 and
+// 6..9 own weight rows 64..95, 96..127, 0..31, 32..63 of the tile.
 //
 // Every mbarrier wait is bounded; on timeout the kernel records an error
 // code in *err (when given), drains its outstanding copies (bounded), frees
@@ -56,15 +58,12 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint32_t a_tmem, uint64_
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
       : "memory");
 }
-__device__ __forceinline__ void tmem_st32(uint32_t addr, const uint32_t* r) {
+__device__ __forceinline__ void tmem_st16(uint32_t addr, const uint32_t* r) {
   asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
-      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
-      "%29, %30, %31, %32};" ::"r"(addr),
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16};" ::"r"(addr),
       "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
-      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
-      "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
-      "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
       : "memory");
 }
 __device__ __forceinline__ void tmem_ld32(uint32_t addr, uint32_t* r) {
@@ -176,6 +175,8 @@ __device__ __forceinline__ uint32_t pair_lut_off(uint32_t w, int b, uint32_t lan
   return off | lane4;
 }
 
+constexpr int kW4Threads = 320;  // producer, MMA, 8 dequant / epilogue warps
+
 template <typename T, int BT, int S, bool NF>
 struct Smem {
   static constexpr int kX = BT * kBK * 2;  // activation tile bytes per stage
@@ -192,7 +193,7 @@ struct Smem {
 };
 
 template <typename T, int BT, int S, bool NF>
-__global__ void __launch_bounds__(192, 1) w4a16_kernel(const __grid_constant__ CUtensorMap tmap_x,
+__global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_constant__ CUtensorMap tmap_x,
                                                        const uint8_t* __restrict__ packed,
                                                        const float* __restrict__ bias,
                                                        T* __restrict__ y, W4Args a,
@@ -224,7 +225,7 @@ __global__ void __launch_bounds__(192, 1) w4a16_kernel(const __grid_constant__ C
     for (int i = 0; i < S; ++i) {
       mbar_init(&full_x[i], 1);
       mbar_init(&full_w[i], 1);
-      mbar_init(&a_full[i], 128);
+      mbar_init(&a_full[i], 256);
       mbar_init(&empty[i], 1);
     }
     mbar_init(acc_full, 1);
@@ -297,6 +298,7 @@ __global__ void __launch_bounds__(192, 1) w4a16_kernel(const __grid_constant__ C
   } else {
     // ---------------- dequantization (warps 2..5), then epilogue ----------------
     const int q = warp & 3;          // tensor-memory lane quarter
+    const int h = (warp - 2) >> 2;   // half of the K step (A slot columns 16h..16h+15)
     const int row = q * 32 + lane;   // weight row within the tile
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
     bool ok = true;
@@ -305,26 +307,26 @@ __global__ void __launch_bounds__(192, 1) w4a16_kernel(const __grid_constant__ C
       const uint32_t ph = (i / S) & 1;
       if (!mbar_wait_warp(&full_w[s], ph)) { ok = false; break; }
       if (i >= S && !mbar_wait_warp(&empty[s], ph ^ 1)) { ok = false; break; }
-      const uint4* src = reinterpret_cast<const uint4*>(smem + L::off_w + s * kWStage + row * 32);
-      const uint4 c0 = src[0], c1 = src[1];
+      // this warp's half of the row's codes: words 4h..4h+3 (k = 32h..32h+31)
+      const uint4 cw = reinterpret_cast<const uint4*>(smem + L::off_w + s * kWStage + row * 32)[h];
       const uint32_t zs = *reinterpret_cast<const uint32_t*>(smem + L::off_s + s * kSStage + row * 4);
       // zs = (zero_b, scale) as a T pair; broadcast each half to both halves
       const uint32_t zb = __byte_perm(zs, zs, 0x1010);
       const uint32_t sc = __byte_perm(zs, zs, 0x3232);
-      const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-      uint32_t r[32];
+      const uint32_t w[4] = {cw.x, cw.y, cw.z, cw.w};
+      uint32_t r[16];
       if constexpr (NF) {
         // byte c = k pair (2c, 2c+1) -> table pair * scale = round_T(NF4 * scale)
         const char* lb = reinterpret_cast<const char*>(smem + L::off_lut);
         const uint32_t l4 = (uint32_t)lane << 2;
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
+        for (int c = 0; c < 16; ++c) {
           const uint32_t pv = *reinterpret_cast<const uint32_t*>(lb + pair_lut_off(w[c >> 2], c & 3, l4));
           r[c] = Act<T>::mul2(pv, sc);
         }
       } else {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
+        for (int j = 0; j < 4; ++j) {
 #pragma unroll
           for (int p = 0; p < 4; ++p) {
             // nibbles (4p, 16+4p) of word j are k = 8j+2p (low half), 8j+2p+1 (high half)
@@ -333,7 +335,7 @@ __global__ void __launch_bounds__(192, 1) w4a16_kernel(const __grid_constant__ C
           }
         }
       }
-      tmem_st32(lane_base + kAcol + s * (kBK / 2), r);
+      tmem_st16(lane_base + kAcol + s * (kBK / 2) + 16 * h, r);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&a_full[s]);
@@ -345,7 +347,7 @@ __global__ void __launch_bounds__(192, 1) w4a16_kernel(const __grid_constant__ C
       const int n = nt * kRows + row;
       const float b = bias ? bias[n] : 0.0f;
 #pragma unroll 1
-      for (int c = 0; c < BT; c += 32) {
+      for (int c = 32 * h; c < BT; c += 64) {
         uint32_t v[32];
         tmem_ld32(lane_base + c, v);
         tmem_wait_ld();
@@ -747,14 +749,14 @@ int launch_w4(const void* x, int M, int N, int K, int group, const void* packed,
     attr_done.fetch_or(bit);
   }
   dim3 grid(N / kRows, (M + BT - 1) / BT);
-  kern<<<grid, 192, smem_bytes, st>>>(map, static_cast<const uint8_t*>(packed), bias,
+  kern<<<grid, kW4Threads, smem_bytes, st>>>(map, static_cast<const uint8_t*>(packed), bias,
                                     static_cast<T*>(y), a, err);
   return launched("w4a16_kernel");
 }
 
 // Token-tile width for M > 128: one CTA per SM runs one 128 x BT tile at a
 // time and a tile's time is dominated by its 64-wide K steps, whose cost
-// hardly depends on BT (measured: 1.1k cycles per step at BT = 256 and 192),
+// hardly depends on BT (measured with 4 dequant warps: 1.1k cycles per step at BT = 256 and 192),
 // so a launch costs about ceil(tiles / SMs) waves; take the widest tile
 // among those with the fewest waves.
 inline int pick_bt(int M, int N) {
