@@ -444,12 +444,11 @@ struct G64Out {
   float lo;
 };
 
-// One super-group (256 groups, one per thread of the block): scale, codes,
-// and with DQ the second-level quantization of the 256 scales.
-template <bool DQ>
-__device__ __forceinline__ void g64_group(const uint4 (&w)[8], int64_t sg, const G64Out& o,
-                                          const char* lutb, uint32_t rep, uint32_t* red) {
-  using T = __nv_bfloat16;
+// One super-group (256 groups, one per thread of the block), first half:
+// scale and codes of the thread's group, and (DQ) the warp's largest scale in
+// wmax[warp].  Returns the group's scale.
+__device__ __forceinline__ float g64_group(const uint4 (&w)[8], int64_t sg, const G64Out& o,
+                                           const char* lutb, uint32_t rep, uint32_t* wmax) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t g = sg * 256 + threadIdx.x;
   const bool live = g < o.n_groups;
@@ -471,23 +470,29 @@ __device__ __forceinline__ void g64_group(const uint4 (&w)[8], int64_t sg, const
     o.codes[2 * g] = make_uint4(out[0], out[1], out[2], out[3]);
     o.codes[2 * g + 1] = make_uint4(out[4], out[5], out[6], out[7]);
   }
-  if constexpr (DQ) {
-    // absmax of the super-group's scales (s >= 0 or +NaN: integer order is float order)
+  if (wmax) {
+    // absmax of the warp's scales (s >= 0 or +NaN: integer order is float order)
     const uint32_t mb = __reduce_max_sync(0xffffffffu, live ? __float_as_uint(s) : 0u);
-    if (lane == 0) red[warp] = mb;
-    __syncthreads();
-    uint32_t tot = red[0];
+    if (lane == 0) wmax[warp] = mb;
+  }
+  return s;
+}
+
+// Second half (DQ), after a block barrier has made the 8 warp maxima
+// visible: the super-group's dq scale and the thread's quantized scale.
+__device__ __forceinline__ void g64_double_quant(float s, int64_t sg, const G64Out& o, const uint32_t* wmax) {
+  using T = __nv_bfloat16;
+  const int64_t g = sg * 256 + threadIdx.x;
+  uint32_t tot = wmax[0];
 #pragma unroll
-    for (int i = 1; i < 8; ++i) tot = max(tot, red[i]);
-    __syncthreads();
-    float dq = __uint_as_float(tot);
-    dq = (dq < o.lo) ? o.lo : dq;
-    if (threadIdx.x == 0) o.dq_scales[sg] = __float2bfloat16_rn(dq);
-    if (live) {
-      const float sn = tdiv<T>(s, dq);
-      const float q = tclamp(trint(tmul<T>(sn, 127.0f)), -127.0f, 127.0f);
-      o.q_scales[g] = __float2bfloat16_rn(q);
-    }
+  for (int i = 1; i < 8; ++i) tot = max(tot, wmax[i]);
+  float dq = __uint_as_float(tot);
+  dq = (dq < o.lo) ? o.lo : dq;
+  if (threadIdx.x == 0) o.dq_scales[sg] = __float2bfloat16_rn(dq);
+  if (g < o.n_groups) {
+    const float sn = tdiv<T>(s, dq);
+    const float q = tclamp(trint(tmul<T>(sn, 127.0f)), -127.0f, 127.0f);
+    o.q_scales[g] = __float2bfloat16_rn(q);
   }
 }
 
@@ -512,7 +517,7 @@ __global__ void __launch_bounds__(256, 2) nf4_pack_g64_kernel(const __grid_const
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   int2* lut = reinterpret_cast<int2*>(smem + kG64Stages * kG64StageBytes);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kG64Stages * kG64StageBytes + kG64LutBytes);
-  __shared__ uint32_t red[8];
+  __shared__ uint32_t red[2][8];  // warp maxima, by iteration parity
   __shared__ int s_fail;
   const int t = threadIdx.x;
   const int64_t step = gridDim.x;
@@ -545,7 +550,11 @@ __global__ void __launch_bounds__(256, 2) nf4_pack_g64_kernel(const __grid_const
     const uint8_t* row = smem + s * kG64StageBytes + t * 128;
 #pragma unroll
     for (int k = 0; k < 8; ++k) w[k] = *reinterpret_cast<const uint4*>(row + ((k ^ (t & 7)) << 4));
-    __syncthreads();  // stage s has been read by every thread
+    const float sc = g64_group(w, sg, o, lutb, rep, DQ ? red[it & 1] : nullptr);
+    // one barrier per super-group: stage s has been read by every thread and
+    // the warp maxima of this super-group are visible (red is double-buffered
+    // by iteration parity, so the next super-group cannot overwrite them)
+    __syncthreads();
     if (s_fail) break;
     if (t == 0) {
       const int64_t nsg = sg + kG64Stages * step;
@@ -554,7 +563,7 @@ __global__ void __launch_bounds__(256, 2) nf4_pack_g64_kernel(const __grid_const
         tma_load_2d(smem + s * kG64StageBytes, &tmap, 0, (int)(nsg * 256), &bars[s]);
       }
     }
-    g64_group<DQ>(w, sg, o, lutb, rep, red);
+    if constexpr (DQ) g64_double_quant(sc, sg, o, red[it & 1]);
   }
   if (sg < n_super) {  // a copy timed out: mark this super-group, wait out the copies still in flight
     const int64_t g = sg * 256 + t;
