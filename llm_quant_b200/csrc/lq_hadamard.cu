@@ -25,6 +25,7 @@ struct FhtArgs {
   // fused quantization
   float qmin, qmax, lo;
   int sym;
+  int al32;  // x is 32-byte aligned: rows are read with whole-sector loads
 };
 
 template <typename T, int E>
@@ -338,10 +339,20 @@ __global__ void __launch_bounds__((1 << L) / 32) fht3_kernel(const T* __restrict
   // this thread's 32 input elements of the current row; the next row's are
   // loaded as soon as these are in registers, so the load overlaps the row
   uint4 raw[32 / V];
-  if (blockIdx.x < a.rows) {
+  // a thread's 32 elements are 64 (bf16) or 128 (fp32) contiguous bytes:
+  // 32-byte loads take whole sectors (16-byte loads at a 64-byte lane stride
+  // would fetch every sector twice)
+  auto load_row = [&](int64_t r) {
+    const T* src = x + r * D + (int64_t)t * 32;
+    if (a.al32) {
 #pragma unroll
-    for (int k = 0; k < 32 / V; ++k) raw[k] = ld_nc_v4(x + (int64_t)blockIdx.x * D + (int64_t)t * 32 + k * V);
-  }
+      for (int k = 0; k < 32 / V; k += 2) ld_nc_v8(src + k * V, raw[k], raw[k + 1]);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 32 / V; ++k) raw[k] = ld_nc_v4(src + k * V);
+    }
+  };
+  if (blockIdx.x < a.rows) load_row(blockIdx.x);
   for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
     float2 v[16];
     {  // phase 1
@@ -354,10 +365,7 @@ __global__ void __launch_bounds__((1 << L) / 32) fht3_kernel(const T* __restrict
           v[(k * V + i) / 2] = make_float2(Ty<T>::to_f(u.v[i]), Ty<T>::to_f(u.v[i + 1]));
       }
       const int64_t nrow = row + gridDim.x;
-      if (nrow < a.rows) {
-#pragma unroll
-        for (int k = 0; k < 32 / V; ++k) raw[k] = ld_nc_v4(x + nrow * D + (int64_t)t * 32 + k * V);
-      }
+      if (nrow < a.rows) load_row(nrow);
     }
 #pragma unroll
     for (int m = 0; m < 16; ++m) {
@@ -539,7 +547,9 @@ int fht_launch(const T* x, FhtArgs a, T* out, T* s, T* z, cudaStream_t st) {
     LQ_REQUIRE(e == cudaSuccess && per_sm > 0, LQ_ECUDA, "occupancy query: %s", cudaGetErrorString(e));
     const int64_t cap = (int64_t)num_sms() * per_sm;
     const int grid = (int)(a.rows < cap ? a.rows : cap);
-    k3<<<grid, d / 32, 0, st>>>(x, a, out, s, z);
+    FhtArgs a3 = a;
+    a3.al32 = (reinterpret_cast<uintptr_t>(x) & 31) == 0;
+    k3<<<grid, d / 32, 0, st>>>(x, a3, out, s, z);
     return launched("fht3_kernel");
   }
   int E = (d <= 8192) ? 16 : 32;
@@ -571,6 +581,7 @@ int fht_t(const void* x, int64_t rows, int64_t d, int n_bits, int sym, void* out
   a.rows = rows;
   a.d = (int)d;
   a.E = 0;
+  a.al32 = 0;
   a.log2d = 0;
   while ((1 << a.log2d) < d) ++a.log2d;
   a.entry = entry_of<T>((int)d);
