@@ -55,11 +55,12 @@ NUM_LAYERS = 32
 # the bench).  Writes still held in L2 when a launch ends are not counted,
 # which is why some ratios sit below the algorithmic bytes.
 NCU_TRAFFIC = {
-    "nf4": 279.9e6 / (28672 * 4096),     # nf4_pack_g64_kernel, 2.38 B per weight
+    "nf4": 281.4e6 / (28672 * 4096),     # nf4_pack_g64_kernel, 2.40 B per weight
     "group": 212.4e6 / (8192 * 4096),    # group_warp_kernel, 6.33 B per element
-    "rotquant": 209.7e6 / (16384 * 4096),  # fht3_kernel, 3.13 B per element
+    "rotquant": 222.0e6 / (16384 * 4096),  # fht3_kernel, 3.31 B per element
     "kv": 277.2e6 / (8 * 8 * 8192 * 128),  # kv_dequant_seg_kernel, 4.13 B per element
     "w4a16": 42.6e6,                     # w4a16_kernel at M = 1024, bytes per launch
+    "kv_attention": 70.2e6 / (8 * 8 * 4096),  # kv_attn_kernel, 268 B per cached token
 }
 
 
