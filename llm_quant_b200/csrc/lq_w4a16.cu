@@ -27,6 +27,8 @@
 #include "lq_common.cuh"
 #include "lq_tma.cuh"
 
+#include <initializer_list>
+
 namespace lq {
 namespace {
 
@@ -177,13 +179,17 @@ __device__ __forceinline__ uint32_t pair_lut_off(uint32_t w, int b, uint32_t lan
 
 constexpr int kW4Threads = 320;  // producer, MMA, 8 dequant / epilogue warps
 
-template <typename T, int BT, int S, bool NF>
+// A stage holds WK 64-wide K halves (WK = 2: 128 K per stage), so the
+// per-stage barrier round trips and MMA-thread bookkeeping -- which pace the
+// pipeline, not the tensor cores -- are paid once per 128 K.
+template <typename T, int BT, int S, bool NF, int WK>
 struct Smem {
-  static constexpr int kX = BT * kBK * 2;  // activation tile bytes per stage
+  static constexpr int kXh = BT * kBK * 2;  // activation bytes of one 64-wide half
+  static constexpr int kX = WK * kXh;       // activation tile bytes per stage
   static constexpr int off_x = 0;
-  static constexpr int off_w = off_x + S * kX;
-  static constexpr int off_s = off_w + S * kWStage;
-  static constexpr int off_lut = off_s + S * kSStage;             // NF4 pair table (NF only)
+  static constexpr int off_w = off_x + S * kX;                  // [S][WK] weight halves
+  static constexpr int off_s = off_w + S * WK * kWStage;        // [S][WK] pair halves
+  static constexpr int off_lut = off_s + S * WK * kSStage;      // NF4 pair table (NF only)
   static constexpr int off_tmp = off_lut + (NF ? kPairLutWords * 4 : 0);
   static constexpr int off_bar = off_tmp + (NF ? 1024 : 0);
   // barriers: full_x[S], full_w[S], a_full[S], empty[S], acc_full
@@ -192,14 +198,15 @@ struct Smem {
   static constexpr int bytes = off_tmem + 16 + 1024;  // + alignment slack
 };
 
-template <typename T, int BT, int S, bool NF>
+template <typename T, int BT, int S, bool NF, int WK>
 __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_constant__ CUtensorMap tmap_x,
                                                        const uint8_t* __restrict__ packed,
                                                        const float* __restrict__ bias,
                                                        T* __restrict__ y, W4Args a,
                                                        int* __restrict__ err) {
-  using L = Smem<T, BT, S, NF>;
-  static_assert(BT % 16 == 0 && BT <= kAcol && kAcol + S * (kBK / 2) <= (int)kTmemCols,
+  using L = Smem<T, BT, S, NF, WK>;
+  constexpr int SC = WK * (kBK / 2);  // tensor-memory columns of one stage's A slot
+  static_assert(BT % 16 == 0 && BT <= kAcol && kAcol + S * SC <= (int)kTmemCols,
                 "accumulator and A slots must fit tensor memory without overlap");
   static_assert(L::bytes <= 227 * 1024, "shared memory per CTA");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -216,6 +223,7 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nt = blockIdx.x;       // weight-row tile
   const int m0 = blockIdx.y * BT;  // first token of the tile
+  const int n_steps = a.n_kb / WK;
   const uint8_t* wtile = packed + (size_t)nt * a.n_kb * kWStage;
   const uint8_t* stile = packed + (size_t)(a.N / kRows) * a.n_kb * kWStage +
                          (size_t)nt * a.n_groups * kSStage;
@@ -225,7 +233,7 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
     for (int i = 0; i < S; ++i) {
       mbar_init(&full_x[i], 1);
       mbar_init(&full_w[i], 1);
-      mbar_init(&a_full[i], 256);
+      mbar_init(&a_full[i], 8);  // one arrival per dequant warp
       mbar_init(&empty[i], 1);
     }
     mbar_init(acc_full, 1);
@@ -251,16 +259,22 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_x)) : "memory");
       int issued = 0;
-      for (int i = 0; i < a.n_kb; ++i) {
+      for (int i = 0; i < n_steps; ++i) {
         const int s = i % S;
         if (i >= S && !mbar_wait(&empty[s], ((i / S) - 1) & 1)) { s_err = 1; break; }
         if (s_err) break;
         mbar_expect_tx(&full_x[s], L::kX);
-        tma_load_2d(smem + L::off_x + s * L::kX, &tmap_x, i * kBK, m0, &full_x[s]);
-        mbar_expect_tx(&full_w[s], kWStage + kSStage);
-        bulk_load(smem + L::off_w + s * kWStage, wtile + (size_t)i * kWStage, kWStage, &full_w[s]);
-        const int g = group_of(a, i);
-        bulk_load(smem + L::off_s + s * kSStage, stile + (size_t)g * kSStage, kSStage, &full_w[s]);
+#pragma unroll
+        for (int hk = 0; hk < WK; ++hk)
+          tma_load_2d(smem + L::off_x + s * L::kX + hk * L::kXh, &tmap_x, (i * WK + hk) * kBK, m0, &full_x[s]);
+        mbar_expect_tx(&full_w[s], WK * (kWStage + kSStage));
+        // the WK weight halves of a step are adjacent in the packed layout
+        bulk_load(smem + L::off_w + s * WK * kWStage, wtile + (size_t)i * WK * kWStage, WK * kWStage, &full_w[s]);
+#pragma unroll
+        for (int hk = 0; hk < WK; ++hk) {
+          const int g = group_of(a, i * WK + hk);
+          bulk_load(smem + L::off_s + (s * WK + hk) * kSStage, stile + (size_t)g * kSStage, kSStage, &full_w[s]);
+        }
         issued = i + 1;
       }
       if (s_err) {
@@ -273,20 +287,23 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
+    // 128-wide stages: one wait per stage, a_full completes only after the
+    // dequant warps have written the A slot AND (warp 2 waits on it first) the
+    // activations landed; 64-wide stages wait on the activations directly
     bool issued_any = false;
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc(Act<T>::fmt, BT);
-      for (int i = 0; i < a.n_kb; ++i) {
+      for (int i = 0; i < n_steps; ++i) {
         const int s = i % S;
         const uint32_t ph = (i / S) & 1;
-        if (!mbar_wait(&full_x[s], ph) || !mbar_wait(&a_full[s], ph)) { s_err = 2; break; }
+        if ((WK == 1 && !mbar_wait(&full_x[s], ph)) || !mbar_wait(&a_full[s], ph)) { s_err = 2; break; }
         tc_fence_after();
         const uint32_t xs = smem_u32(smem + L::off_x + s * L::kX);
+        const uint32_t acol0 = tmem + kAcol + s * SC;
 #pragma unroll
-        for (int kk = 0; kk < kBK / 16; ++kk) {
-          const uint64_t bdesc = sw128_desc(xs + kk * 32);
-          const uint32_t acol = tmem + kAcol + s * (kBK / 2) + kk * 8;
-          tc_mma(tmem, acol, bdesc, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < WK * (kBK / 16); ++kk) {
+          const uint64_t bdesc = sw128_desc(xs + (kk >> 2) * L::kXh + (kk & 3) * 32);
+          tc_mma(tmem, acol0 + kk * 8, bdesc, idesc, (i > 0 || kk > 0) ? 1u : 0u);
         }
         tc_commit(&empty[s]);  // frees the activation stage and the A slot
         issued_any = true;
@@ -296,49 +313,57 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
     }
     __syncwarp();
   } else {
-    // ---------------- dequantization (warps 2..5), then epilogue ----------------
+    // ---------------- dequantization (warps 2..9), then epilogue ----------------
     const int q = warp & 3;          // tensor-memory lane quarter
-    const int h = (warp - 2) >> 2;   // half of the K step (A slot columns 16h..16h+15)
+    const int h = (warp - 2) >> 2;   // half of each 64-wide K half (A slot columns 16h..16h+15)
     const int row = q * 32 + lane;   // weight row within the tile
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
     bool ok = true;
-    for (int i = 0; i < a.n_kb && ok; ++i) {
+    for (int i = 0; i < n_steps && ok; ++i) {
       const int s = i % S;
       const uint32_t ph = (i / S) & 1;
       if (!mbar_wait_warp(&full_w[s], ph)) { ok = false; break; }
       if (i >= S && !mbar_wait_warp(&empty[s], ph ^ 1)) { ok = false; break; }
-      // this warp's half of the row's codes: words 4h..4h+3 (k = 32h..32h+31)
-      const uint4 cw = reinterpret_cast<const uint4*>(smem + L::off_w + s * kWStage + row * 32)[h];
-      const uint32_t zs = *reinterpret_cast<const uint32_t*>(smem + L::off_s + s * kSStage + row * 4);
-      // zs = (zero_b, scale) as a T pair; broadcast each half to both halves
-      const uint32_t zb = __byte_perm(zs, zs, 0x1010);
-      const uint32_t sc = __byte_perm(zs, zs, 0x3232);
-      const uint32_t w[4] = {cw.x, cw.y, cw.z, cw.w};
-      uint32_t r[16];
-      if constexpr (NF) {
-        // byte c = k pair (2c, 2c+1) -> table pair * scale = round_T(NF4 * scale)
-        const char* lb = reinterpret_cast<const char*>(smem + L::off_lut);
-        const uint32_t l4 = (uint32_t)lane << 2;
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          const uint32_t pv = *reinterpret_cast<const uint32_t*>(lb + pair_lut_off(w[c >> 2], c & 3, l4));
-          r[c] = Act<T>::mul2(pv, sc);
-        }
-      } else {
+      for (int hk = 0; hk < WK; ++hk) {
+        // this warp's half of the row's codes: words 4h..4h+3 (k = 32h..32h+31)
+        const uint4 cw = reinterpret_cast<const uint4*>(smem + L::off_w + (s * WK + hk) * kWStage + row * 32)[h];
+        const uint32_t zs = *reinterpret_cast<const uint32_t*>(smem + L::off_s + (s * WK + hk) * kSStage + row * 4);
+        // zs = (zero_b, scale) as a T pair; broadcast each half to both halves
+        const uint32_t zb = __byte_perm(zs, zs, 0x1010);
+        const uint32_t sc = __byte_perm(zs, zs, 0x3232);
+        const uint32_t w[4] = {cw.x, cw.y, cw.z, cw.w};
+        uint32_t r[16];
+        if constexpr (NF) {
+          // byte c = k pair (2c, 2c+1) -> table pair * scale = round_T(NF4 * scale)
+          const char* lb = reinterpret_cast<const char*>(smem + L::off_lut);
+          const uint32_t l4 = (uint32_t)lane << 2;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
+          for (int c = 0; c < 16; ++c) {
+            const uint32_t pv = *reinterpret_cast<const uint32_t*>(lb + pair_lut_off(w[c >> 2], c & 3, l4));
+            r[c] = Act<T>::mul2(pv, sc);
+          }
+        } else {
 #pragma unroll
-          for (int p = 0; p < 4; ++p) {
-            // nibbles (4p, 16+4p) of word j are k = 8j+2p (low half), 8j+2p+1 (high half)
-            const uint32_t v = ((w[j] >> (4 * p)) & 0x000F000Fu) | Act<T>::magic;
-            r[j * 4 + p] = Act<T>::sub_mul(v, zb, sc);
+          for (int j = 0; j < 4; ++j) {
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {
+              // nibbles (4p, 16+4p) of word j are k = 8j+2p (low half), 8j+2p+1 (high half)
+              const uint32_t v = ((w[j] >> (4 * p)) & 0x000F000Fu) | Act<T>::magic;
+              r[j * 4 + p] = Act<T>::sub_mul(v, zb, sc);
+            }
           }
         }
+        tmem_st16(lane_base + kAcol + s * SC + hk * (kBK / 2) + 16 * h, r);
       }
-      tmem_st16(lane_base + kAcol + s * (kBK / 2) + 16 * h, r);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&a_full[s]);
+      // 128-wide stages: warp 2 also waits for the stage's activations, so
+      // a_full stands for both and the MMA thread waits once per stage
+      if (WK == 2 && warp == 2 && !mbar_wait_warp(&full_x[s], ph)) { ok = false; break; }
+      // one elected arrival per warp once every lane's store has landed
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&a_full[s]);
     }
     if (!ok) s_err = 3;
     // epilogue: accumulator rows = weight rows (this thread's row), columns = tokens
@@ -711,10 +736,10 @@ __global__ void __launch_bounds__(256) nf4lin_pack_kernel(const uint32_t* __rest
 }
 
 // ---- host side ---------------------------------------------------------------
-template <typename T, int BT, int S, bool NF>
+template <typename T, int BT, int S, bool NF, int WK>
 int launch_w4(const void* x, int M, int N, int K, int group, const void* packed, const float* bias,
               void* y, int* err, cudaStream_t st) {
-  using L = Smem<T, BT, S, NF>;
+  using L = Smem<T, BT, S, NF, WK>;
   EncodeTiledFn enc = encode_fn();
   LQ_REQUIRE(enc != nullptr, LQ_ECUDA, "cuTensorMapEncodeTiled unavailable");
   CUtensorMap map;
@@ -735,7 +760,7 @@ int launch_w4(const void* x, int M, int N, int K, int group, const void* packed,
   a.n_kb = K / kBK;
   a.n_groups = K / group;
   a.kb_shift = kb_shift_of(group);
-  auto kern = w4a16_kernel<T, BT, S, NF>;
+  auto kern = w4a16_kernel<T, BT, S, NF, WK>;
   // every CTA allocates all 512 tensor-memory columns: request enough shared
   // memory that only one CTA fits on an SM, so none waits in tcgen05.alloc
   const int smem_bytes = L::bytes > 117 * 1024 ? L::bytes : 117 * 1024;
@@ -755,37 +780,58 @@ int launch_w4(const void* x, int M, int N, int K, int group, const void* packed,
 }
 
 // Token-tile width for M > 128: one CTA per SM runs one 128 x BT tile at a
-// time and a tile's time is dominated by its 64-wide K steps, whose cost
-// hardly depends on BT (measured with 4 dequant warps: 1.1k cycles per step at BT = 256 and 192),
-// so a launch costs about ceil(tiles / SMs) waves; take the widest tile
-// among those with the fewest waves.
-inline int pick_bt(int M, int N) {
+// time, so a launch costs ceil(tiles / SMs) waves of one tile's time.  With
+// 128-wide stages the main loop is tensor-bound, so a tile's time grows with
+// BT (plus a fixed prologue / epilogue worth about 32 columns): take the
+// candidate with the least waves x (BT + 32).  With 64-wide stages a step's
+// cost hardly depends on BT (the MMA thread's bookkeeping paces it): take the
+// widest tile among those with the fewest waves.
+inline int pick_bt(int M, int N, std::initializer_list<int> cands, bool tensor_bound) {
   const int sms = num_sms();
-  int best = 256;
-  int64_t best_waves = INT64_MAX;
-  for (int bt : {256, 224, 192}) {
+  int best = *cands.begin();
+  int64_t best_cost = INT64_MAX;
+  for (int bt : cands) {
     const int64_t tiles = (int64_t)(N / kRows) * ((M + bt - 1) / bt);
     const int64_t waves = (tiles + sms - 1) / sms;
-    if (waves < best_waves) { best_waves = waves; best = bt; }
+    const int64_t cost = tensor_bound ? waves * (bt + 32) : waves;
+    if (cost < best_cost) { best_cost = cost; best = bt; }
   }
   return best;
 }
 
-// Stages: as many 64-wide K steps in flight as shared memory allows (the
-// NF4 variant also holds its 33 KB pair table).
+// K multiple of 128: 128-wide stages (WK = 2), as many as shared and tensor
+// memory allow (3 for the wide tiles, 4 up to BT = 128).  Otherwise, and for
+// NF4 past M = 128, 64-wide stages.
 template <typename T, bool NF>
 int w4_dispatch(const void* x, int M, int N, int K, int group, const void* packed,
                 const float* bias, void* y, int* err, cudaStream_t st) {
   if (M <= 8) return launch_gemv<T, NF>(x, M, N, K, group, packed, bias, y, st);
-  if (M <= 16) return launch_w4<T, 16, 8, NF>(x, M, N, K, group, packed, bias, y, err, st);
-  if (M <= 32) return launch_w4<T, 32, 8, NF>(x, M, N, K, group, packed, bias, y, err, st);
-  if (M <= 64) return launch_w4<T, 64, 8, NF>(x, M, N, K, group, packed, bias, y, err, st);
-  if (M <= 128) return launch_w4<T, 128, 8, NF>(x, M, N, K, group, packed, bias, y, err, st);
+  if (K % (2 * kBK) == 0) {
+    if (M <= 16) return launch_w4<T, 16, 4, NF, 2>(x, M, N, K, group, packed, bias, y, err, st);
+    if (M <= 32) return launch_w4<T, 32, 4, NF, 2>(x, M, N, K, group, packed, bias, y, err, st);
+    if (M <= 64) return launch_w4<T, 64, 4, NF, 2>(x, M, N, K, group, packed, bias, y, err, st);
+    if (M <= 128) return launch_w4<T, 128, 4, NF, 2>(x, M, N, K, group, packed, bias, y, err, st);
+    if constexpr (!NF) {
+      switch (pick_bt(M, N, {256, 224, 192, 160}, true)) {
+        case 224: return launch_w4<T, 224, 3, NF, 2>(x, M, N, K, group, packed, bias, y, err, st);
+        case 192: return launch_w4<T, 192, 3, NF, 2>(x, M, N, K, group, packed, bias, y, err, st);
+        case 160: return launch_w4<T, 160, 3, NF, 2>(x, M, N, K, group, packed, bias, y, err, st);
+        default: return launch_w4<T, 256, 3, NF, 2>(x, M, N, K, group, packed, bias, y, err, st);
+      }
+    }
+    // NF4 past M = 128: its 33 KB table leaves room for three 128-wide
+    // stages only up to BT = 192, which measured slower than five 64-wide
+    // stages at BT = 224 -- fall through
+  }
+  if (M <= 16) return launch_w4<T, 16, 8, NF, 1>(x, M, N, K, group, packed, bias, y, err, st);
+  if (M <= 32) return launch_w4<T, 32, 8, NF, 1>(x, M, N, K, group, packed, bias, y, err, st);
+  if (M <= 64) return launch_w4<T, 64, 8, NF, 1>(x, M, N, K, group, packed, bias, y, err, st);
+  if (M <= 128) return launch_w4<T, 128, 8, NF, 1>(x, M, N, K, group, packed, bias, y, err, st);
   constexpr int S = NF ? 5 : 6;
-  switch (pick_bt(M, N)) {
-    case 224: return launch_w4<T, 224, S, NF>(x, M, N, K, group, packed, bias, y, err, st);
-    case 192: return launch_w4<T, 192, S, NF>(x, M, N, K, group, packed, bias, y, err, st);
-    default: return launch_w4<T, 256, S, NF>(x, M, N, K, group, packed, bias, y, err, st);
+  switch (pick_bt(M, N, {256, 224, 192}, false)) {
+    case 224: return launch_w4<T, 224, S, NF, 1>(x, M, N, K, group, packed, bias, y, err, st);
+    case 192: return launch_w4<T, 192, S, NF, 1>(x, M, N, K, group, packed, bias, y, err, st);
+    default: return launch_w4<T, 256, S, NF, 1>(x, M, N, K, group, packed, bias, y, err, st);
   }
 }
 
