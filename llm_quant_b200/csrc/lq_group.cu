@@ -303,9 +303,9 @@ int dispatch(const T* x, const GroupArgs& a, OutT* out, T* s, T* z, bool vec_ok,
   const int64_t G = a.G;
   if (vec_ok) {
     const int64_t nv = G / V;  // vectors per group
-    // up to 4 vectors (64 bytes) in flight per lane, teams of <= 32 lanes
+    // up to 8 vectors (128 bytes) in flight per lane, teams of <= 32 lanes
     int nvt = 1;
-    while (nvt < 4 && nvt * 2 <= nv) nvt *= 2;
+    while (nvt < 8 && nvt * 2 <= nv) nvt *= 2;
     int64_t need = (nv + nvt - 1) / nvt;
     if (need > 32) {
       nvt = 8;
