@@ -79,7 +79,8 @@ __global__ void __launch_bounds__(256) token_group_kernel(const T* __restrict__ 
 #pragma unroll
     for (int i = 0; i < V; ++i) r[i].init();
     if (col_ok) {
-      for (int64_t t = t0 + ty; t < t1; t += TY) {
+#pragma unroll 8
+      for (int64_t t = t0 + ty; t < t1; t += TY) {  // unrolled: 8 token rows' loads in flight
         const T* src = xb + t * a.D + c0;
         if constexpr (VEC) {
           Vec16<T> u;
@@ -138,6 +139,7 @@ __global__ void __launch_bounds__(256) token_group_kernel(const T* __restrict__ 
           zz[i] = sm[tx * V + i].mx;
         }
         OutT* ob = out + (p * a.out_pitch_t + a.out_t_off) * a.D;
+#pragma unroll 4
         for (int64_t t = t0 + ty; t < t1; t += TY) {
           const T* src = xb + t * a.D + c0;
           float v[V];
@@ -194,8 +196,13 @@ int launch_tok(const T* x, TokArgs a, OutT* out, T* s, T* z, bool vec, cudaStrea
   const int threads = 256;
   a.CW = (int)(a.D < 256 ? a.D : 256);
   if (vec) {
-    // column tile: a multiple of V, at most 256 elements (32 vector threads for fp32)
-    a.CW = (int)((a.D < 256 ? a.D : 256));
+    // column tile: a multiple of V, at most 256 elements (32 vector threads
+    // for fp32), narrowed (down to 4 vector threads) until there are slabs
+    // for two per SM -- a per-channel chunk of few (batch, head) pairs would
+    // otherwise leave most SMs idle
+    while (a.P * a.ngt * ((a.D + a.CW - 1) / a.CW) < 2 * (int64_t)num_sms() && a.CW / V > 4 &&
+           (a.CW / 2) % V == 0)
+      a.CW /= 2;
   }
   a.ntile = (a.D + a.CW - 1) / a.CW;
   const int TX = vec ? a.CW / V : a.CW;
