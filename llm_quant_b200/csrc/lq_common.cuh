@@ -264,4 +264,19 @@ inline int num_sms() {
   return n;
 }
 
+// Grid of at most one wave of resident blocks of `kernel` (grid-stride
+// kernels then share their work evenly; a second, partly filled wave would run
+// at lower occupancy), and at most `want` blocks.
+template <typename K>
+inline int resident_grid(K kernel, int threads, size_t smem, int64_t want) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess ||
+      per_sm < 1) {
+    cudaGetLastError();
+    per_sm = 1;
+  }
+  const int64_t cap = (int64_t)num_sms() * per_sm;
+  return (int)(want < 1 ? 1 : (want < cap ? want : cap));
+}
+
 }  // namespace lq

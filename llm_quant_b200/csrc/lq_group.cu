@@ -282,7 +282,8 @@ int grid_for(int64_t units, int per_block) {
 template <typename T, int MODE, typename OutT, int NVT, bool VEC>
 int launch_warp(const T* x, const GroupArgs& a, int tps, OutT* out, T* s, T* z, cudaStream_t st) {
   const int threads = 256;
-  int grid = grid_for(a.total_groups * tps, threads);
+  const int grid = resident_grid(group_warp_kernel<T, MODE, OutT, NVT, VEC>, threads, 0,
+                                 (a.total_groups * tps + threads - 1) / threads);
   group_warp_kernel<T, MODE, OutT, NVT, VEC><<<grid, threads, 0, st>>>(x, a, tps, out, s, z);
   return launched("group_warp_kernel");
 }

@@ -379,8 +379,7 @@ int kv_dequant_t(const void* codes, const DqArgs& a, const void* s, const void* 
   if (a.D % 4 == 0 && aligned16(out) && reinterpret_cast<uintptr_t>(codes) % (4 * sizeof(CT)) == 0) {
     const int64_t segs_per_p = (a.T * a.D + 511) / 512;
     const int64_t warps_needed = a.P * segs_per_p;
-    const int64_t want = (warps_needed + 7) / 8;
-    const int grid = (int)(want < (int64_t)num_sms() * 8 ? (want > 0 ? want : 1) : (int64_t)num_sms() * 8);
+    const int grid = resident_grid(kv_dequant_seg_kernel<CT, ST>, 256, 0, (warps_needed + 7) / 8);
     int d_shift = -1;
     if ((a.D & (a.D - 1)) == 0) {
       d_shift = 0;

@@ -1012,7 +1012,8 @@ int nf4_dequant_t(const void* codes, int cdt, int64_t n, int64_t G, int64_t DG, 
       aligned16(out)) {
     const int64_t nchunk = n / 8;
     if (nchunk > 0) {
-      nf4_unpack_vec_kernel<T><<<grid_cap((nchunk + 256 * kUnpackK - 1) / (256 * kUnpackK), 6), 256, 0, st>>>(
+      const int grid = resident_grid(nf4_unpack_vec_kernel<T>, 256, 0, (nchunk + 256 * kUnpackK - 1) / (256 * kUnpackK));
+      nf4_unpack_vec_kernel<T><<<grid, 256, 0, st>>>(
           static_cast<const uint32_t*>(codes), a, sp, q, d, reinterpret_cast<uint4*>(o), nchunk);
       int rc = launched("nf4_unpack_vec_kernel");
       if (rc) return rc;
