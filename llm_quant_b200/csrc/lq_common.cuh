@@ -48,6 +48,13 @@ inline int launched(const char* what) {
     }                               \
   } while (0)
 
+// Return the status of a helper that failed (it has already set the error).
+#define LQ_TRY(expr)                  \
+  do {                                \
+    const int lq_rc_ = (expr);        \
+    if (lq_rc_ != LQ_OK) return lq_rc_; \
+  } while (0)
+
 inline bool is_float_dtype(int dt) { return dt == LQ_F32 || dt == LQ_F16 || dt == LQ_BF16; }
 inline int dtype_size(int dt) {
   switch (dt) {

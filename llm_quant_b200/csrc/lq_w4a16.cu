@@ -7,19 +7,20 @@
 // Tile = 128 weight rows x BT tokens ("swap AB"): the dequantized weights are
 // the MMA's A operand and live in tensor memory, the activations are the B
 // operand (TMA, 128-byte swizzle, K-major), the fp32 accumulator D[128, BT]
-// is in tensor memory.  Warp roles (320 threads):
-//   warp 0      TMA producer: activation tile + packed 4-bit weight tile +
-//               (zero, scale) pairs per stage, one mbarrier per stage each;
-//   warp 1      allocates tensor memory, one lane issues tcgen05.mma
-//               (4 x K=16 per 64-wide K step) and tcgen05.commit;
-//   warps 2..9  dequantize: thread = one weight row and half of the K step,
-//               32 codes per stage -> 16 packed fp16/bf16 pairs ->
-//               tcgen05.st into its half of the stage's A slot; afterwards
-//               they are the epilogue (tcgen05.ld of the accumulator, + bias,
-//               convert, store y).  Two warps per tensor-memory lane quarter
-//               keep one converting while the other waits on its store.
-// Warp w may only touch tensor-memory lanes 32*(w%4)..+31, so warps 2..5 and
-// 6..9 own weight rows 64..95, 96..127, 0..31, 32..63 of the tile.
+// is in tensor memory.  Warp roles (576 threads):
+//   warp 0       TMA producer: activation tile + packed 4-bit weight tile +
+//                (zero, scale) pairs per stage, one mbarrier per stage each;
+//   warp 1       allocates tensor memory, one lane issues tcgen05.mma
+//                (4 x K=16 per 64-wide K step) and tcgen05.commit;
+//   warps 2..17  dequantize, in two groups of eight taking alternate stages:
+//                thread = one weight row and half of the K step, 32 codes
+//                per 64-wide half -> 16 packed fp16/bf16 pairs -> tcgen05.st
+//                into its half of the stage's A slot; afterwards all sixteen
+//                are the epilogue (tcgen05.ld of the accumulator, + bias,
+//                convert, store y).
+// Warp w may only touch tensor-memory lanes 32*(w%4)..+31, so in each group
+// warps 2..5 (10..13) and 6..9 (14..17) own weight rows 64..95, 96..127,
+// 0..31, 32..63 of the tile.
 //
 // Every mbarrier wait is bounded; on timeout the kernel records an error
 // code in *err (when given), drains its outstanding copies (bounded), frees
@@ -177,7 +178,12 @@ __device__ __forceinline__ uint32_t pair_lut_off(uint32_t w, int b, uint32_t lan
   return off | lane4;
 }
 
-constexpr int kW4Threads = 320;  // producer, MMA, 8 dequant / epilogue warps
+// Block: producer warp, MMA warp, kDG groups of 8 dequant / epilogue warps.
+// Group g dequantizes the stages g, g + kDG, ...: one warp's per-stage chain
+// (barrier waits, shared loads, conversion, tcgen05.st and its wait, arrive)
+// is latency- not issue-bound, so two groups keep two stages in flight.
+constexpr int kDG = 2;
+constexpr int kW4Threads = 64 + 256 * kDG;
 
 // A stage holds WK 64-wide K halves (WK = 2: 128 K per stage), so the
 // per-stage barrier round trips and MMA-thread bookkeeping -- which pace the
@@ -313,13 +319,16 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
     }
     __syncwarp();
   } else {
-    // ---------------- dequantization (warps 2..9), then epilogue ----------------
+    // ---------------- dequantization (warps 2..), then epilogue ----------------
+    // kDG groups of 8 warps; group grp takes the stages grp, grp + kDG, ...
+    const int dw = warp - 2;
+    const int grp = dw >> 3, wi = dw & 7;
     const int q = warp & 3;          // tensor-memory lane quarter
-    const int h = (warp - 2) >> 2;   // half of each 64-wide K half (A slot columns 16h..16h+15)
+    const int h = wi >> 2;           // half of each 64-wide K half (A slot columns 16h..16h+15)
     const int row = q * 32 + lane;   // weight row within the tile
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
     bool ok = true;
-    for (int i = 0; i < n_steps && ok; ++i) {
+    for (int i = grp; i < n_steps && ok; i += kDG) {
       const int s = i % S;
       const uint32_t ph = (i / S) & 1;
       if (!mbar_wait_warp(&full_w[s], ph)) { ok = false; break; }
@@ -360,7 +369,7 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
       tc_fence_before();
       // 128-wide stages: warp 2 also waits for the stage's activations, so
       // a_full stands for both and the MMA thread waits once per stage
-      if (WK == 2 && warp == 2 && !mbar_wait_warp(&full_x[s], ph)) { ok = false; break; }
+      if (WK == 2 && wi == 0 && !mbar_wait_warp(&full_x[s], ph)) { ok = false; break; }
       // one elected arrival per warp once every lane's store has landed
       __syncwarp();
       if (lane == 0) mbar_arrive(&a_full[s]);
@@ -372,7 +381,7 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
       const int n = nt * kRows + row;
       const float b = bias ? bias[n] : 0.0f;
 #pragma unroll 1
-      for (int c = 32 * h; c < BT; c += 64) {
+      for (int c = 32 * (dw >> 2); c < BT; c += 64 * kDG) {
         uint32_t v[32];
         tmem_ld32(lane_base + c, v);
         tmem_wait_ld();
@@ -736,22 +745,24 @@ __global__ void __launch_bounds__(256) nf4lin_pack_kernel(const uint32_t* __rest
 }
 
 // ---- host side ---------------------------------------------------------------
-template <typename T, int BT, int S, bool NF, int WK>
-int launch_w4(const void* x, int M, int N, int K, int group, const void* packed, const float* bias,
-              void* y, int* err, cudaStream_t st) {
-  using L = Smem<T, BT, S, NF, WK>;
+// Activation tensor map: [M, K] row-major, box kBK x BT, 128-byte swizzle.
+template <typename T>
+int encode_x_map(CUtensorMap* map, const void* x, int M, int K, int BT) {
   EncodeTiledFn enc = encode_fn();
   LQ_REQUIRE(enc != nullptr, LQ_ECUDA, "cuTensorMapEncodeTiled unavailable");
-  CUtensorMap map;
   cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
   cuuint64_t strides[1] = {(cuuint64_t)K * 2};
   cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)BT};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(&map, Act<T>::fmt == 0 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+  CUresult r = enc(map, Act<T>::fmt == 0 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                    2, const_cast<void*>(x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   LQ_REQUIRE(r == CUDA_SUCCESS, LQ_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return LQ_OK;
+}
+
+inline W4Args w4_args(int M, int N, int K, int group) {
   W4Args a;
   a.M = M;
   a.N = N;
@@ -760,19 +771,35 @@ int launch_w4(const void* x, int M, int N, int K, int group, const void* packed,
   a.n_kb = K / kBK;
   a.n_groups = K / group;
   a.kb_shift = kb_shift_of(group);
-  auto kern = w4a16_kernel<T, BT, S, NF, WK>;
-  // every CTA allocates all 512 tensor-memory columns: request enough shared
-  // memory that only one CTA fits on an SM, so none waits in tcgen05.alloc
-  const int smem_bytes = L::bytes > 117 * 1024 ? L::bytes : 117 * 1024;
-  static std::atomic<uint64_t> attr_done{0};  // one bit per device
+  return a;
+}
+
+// Every CTA allocates all 512 tensor-memory columns: request enough shared
+// memory that only one CTA fits on an SM, so none waits in tcgen05.alloc.
+template <typename Kern>
+int set_smem_once(Kern kern, int smem_bytes, std::atomic<uint64_t>& done) {
   int dev = 0;
   cudaGetDevice(&dev);
-  const uint64_t bit = 1ull << (dev & 63);
-  if (!(attr_done.load() & bit)) {
+  const uint64_t bit = 1ull << (dev & 63);  // one bit per device
+  if (!(done.load() & bit)) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
     LQ_REQUIRE(e == cudaSuccess, LQ_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    attr_done.fetch_or(bit);
+    done.fetch_or(bit);
   }
+  return LQ_OK;
+}
+
+template <typename T, int BT, int S, bool NF, int WK>
+int launch_w4(const void* x, int M, int N, int K, int group, const void* packed, const float* bias,
+              void* y, int* err, cudaStream_t st) {
+  using L = Smem<T, BT, S, NF, WK>;
+  CUtensorMap map;
+  LQ_TRY(encode_x_map<T>(&map, x, M, K, BT));
+  const W4Args a = w4_args(M, N, K, group);
+  auto kern = w4a16_kernel<T, BT, S, NF, WK>;
+  const int smem_bytes = L::bytes > 117 * 1024 ? L::bytes : 117 * 1024;
+  static std::atomic<uint64_t> attr_done{0};
+  LQ_TRY(set_smem_once(kern, smem_bytes, attr_done));
   dim3 grid(N / kRows, (M + BT - 1) / BT);
   kern<<<grid, kW4Threads, smem_bytes, st>>>(map, static_cast<const uint8_t*>(packed), bias,
                                     static_cast<T*>(y), a, err);
@@ -781,11 +808,13 @@ int launch_w4(const void* x, int M, int N, int K, int group, const void* packed,
 
 // Token-tile width for M > 128: one CTA per SM runs one 128 x BT tile at a
 // time, so a launch costs ceil(tiles / SMs) waves of one tile's time.  With
-// 128-wide stages the main loop is tensor-bound, so a tile's time grows with
-// BT (plus a fixed prologue / epilogue worth about 32 columns): take the
-// candidate with the least waves x (BT + 32).  With 64-wide stages a step's
-// cost hardly depends on BT (the MMA thread's bookkeeping paces it): take the
-// widest tile among those with the fewest waves.
+// 128-wide stages a tile's time grows with BT plus a part that does not (the
+// weight side: loads, dequantization, pipeline fill and epilogue), measured at
+// about 170 columns' worth for K = 4096 (M = 2048, N = 14336: 24.8, 26.4,
+// 29.4, 32.0 us per wave at BT = 160, 192, 224, 256): take the candidate with
+// the least waves x (BT + 170).  With 64-wide stages a step's cost hardly
+// depends on BT (the MMA thread's bookkeeping paces it): take the widest tile
+// among those with the fewest waves.
 inline int pick_bt(int M, int N, std::initializer_list<int> cands, bool tensor_bound) {
   const int sms = num_sms();
   int best = *cands.begin();
@@ -793,7 +822,7 @@ inline int pick_bt(int M, int N, std::initializer_list<int> cands, bool tensor_b
   for (int bt : cands) {
     const int64_t tiles = (int64_t)(N / kRows) * ((M + bt - 1) / bt);
     const int64_t waves = (tiles + sms - 1) / sms;
-    const int64_t cost = tensor_bound ? waves * (bt + 32) : waves;
+    const int64_t cost = tensor_bound ? waves * (bt + 170) : waves;
     if (cost < best_cost) { best_cost = cost; best = bt; }
   }
   return best;

@@ -59,6 +59,16 @@ def test_fused_forward_matches_fp32_reference(L, dtype, N, K, gs, dq, M):
     _check(y, _reference(ql, x))
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("M", [300, 1000])
+def test_fused_forward_many_tiles_per_sm(L, dtype, M):
+    """N = 8192: more 128 x BT tiles than SMs (several waves), the last
+    token tile partial."""
+    ql, g = _module(L, 8192, 1024, dtype, 64, True, seed=M)
+    x = torch.randn(M, 1024, generator=g).to(dtype).cuda()
+    _check(ql(x), _reference(ql, x))
+
+
 def test_fused_forward_3d_input_and_no_bias(L):
     g = torch.Generator().manual_seed(5)
     w = (torch.randn(256, 256, generator=g) * 0.02).to(torch.bfloat16).cuda()

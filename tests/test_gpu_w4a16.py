@@ -99,6 +99,23 @@ def test_w4a16_packed_cache_invalidated(L):
     _check(y1, _ref(ql, x))
 
 
+@pytest.mark.parametrize("K,group", [(1024, 128), (960, 64), (1536, 192)])
+@pytest.mark.parametrize("M", [300, 777, 1500])
+def test_w4a16_many_tiles_per_sm(L, K, group, M):
+    """N = 8192 (64 weight-row tiles) and M > 128: more tiles than SMs (the
+    grid runs in several waves), the last token tile partial; K = 960 takes
+    the 64-wide stages, group 192 the non-power-of-two group index; a single
+    64-wide stage (K = 960 has 15) leaves one dequant group a stage fewer."""
+    ql = _make(L, 8192, K, group, False, torch.float16, M + K)
+    x = torch.randn(M, K, generator=torch.Generator().manual_seed(M)).half().cuda()
+    y = ql(x)
+    _check(y, _ref(ql, x))
+    y2 = ql(x)  # a second launch reuses the pipeline barriers from scratch
+    assert torch.equal(y, y2)
+    from llm_quant_b200.core import w4a16
+    assert w4a16.check_error_flag(x.device) == 0
+
+
 @pytest.mark.parametrize("M", [1, 16, 128, 1024, 4096])
 def test_config5_full_size(L, M):
     """Linear(4096, 14336) int4 g128 asym with fp16 scales/zeros, fp16 x."""
