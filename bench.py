@@ -301,27 +301,41 @@ class NF4Workload:
         }
 
     def e2e(self, steps, graph):
-        """The step's public-API calls (pack_base / _dequantize_base, replayed
-        from the step's CUDA graph) with every weight copied in from pinned
-        host memory first and the packed codes + scales copied back to pinned
-        host memory after, every step.  One layer's seven host weights are
-        reused as the source of every layer."""
+        """The step's public-API calls (pack_base / _dequantize_base) with every
+        weight copied in from pinned host memory and the packed codes + scales
+        copied back to pinned host memory, every step, through HostPipeline:
+        the upload of weight i+1 and the download of weight i-1's results
+        overlap weight i's kernels.  One layer's seven host weights are reused
+        as the source of every layer."""
         torch = self.ctx.torch
+        from llm_quant_b200.streaming import HostPipeline
         host_in = [torch.empty(w.shape, dtype=w.dtype).pin_memory() for w in self.weights[:7]]
         for h, w in zip(host_in, self.weights[:7]):
             h.copy_(w.cpu())
-        res = [t for m in self.mods for t in
-               (m.nf4_codes_packed, m.nf4_scales, m.dq_q_scales, m.dq_scales)]
-        outs = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in res]
+
+        def results(m):
+            return (m.nf4_codes_packed, m.nf4_scales, m.dq_q_scales, m.dq_scales)
+        outs = [[torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in results(m)] for m in self.mods]
         h2d = sum(w.numel() * w.element_size() for w in self.weights)
-        d2h = sum(t.numel() * t.element_size() for t in res)
+        d2h = sum(o.numel() * o.element_size() for os_ in outs for o in os_)
+        n = len(self.weights)
+        pipe = HostPipeline(self.ctx.dev, buffers=n)  # every weight has its own device buffer
+
+        def up(i, _):
+            self.weights[i].copy_(host_in[i % 7], non_blocking=True)
+
+        def work(i, _):
+            self.mods[i].pack_base(self.weights[i])
+            self.mods[i]._dequantize_base()
+
+        def down(i, _):
+            cur = torch.cuda.current_stream()
+            for o, t in zip(outs[i], results(self.mods[i])):
+                t.record_stream(cur)
+                o.copy_(t, non_blocking=True)
 
         def one_step():
-            for i, w in enumerate(self.weights):
-                w.copy_(host_in[i % 7], non_blocking=True)
-            graph.replay()
-            for o, t in zip(outs, res):
-                o.copy_(t, non_blocking=True)
+            pipe.run(n, up, work, down)
 
         one_step()
         torch.cuda.synchronize()
@@ -414,18 +428,29 @@ class GroupWorkload:
 
     def e2e(self, steps, graph):
         """fake_quantize through the public API on matrices copied in from
-        pinned host memory, results copied back, every step."""
+        pinned host memory, results copied back, every step (HostPipeline:
+        uploads, kernels and downloads of consecutive matrices overlap)."""
         torch = self.ctx.torch
+        from llm_quant_b200.streaming import HostPipeline
         host = torch.empty(4096, 4096).pin_memory()
         host.copy_(self.ws[0].cpu())
         out = torch.empty(4096, 4096).pin_memory()
-        dev = torch.empty_like(self.ws[0])
+        devs = [torch.empty_like(self.ws[0]) for _ in range(2)]
+        ys = [None, None]
+        pipe = HostPipeline(self.ctx.dev, buffers=2)
+
+        def up(i, b):
+            devs[b].copy_(host, non_blocking=True)
+
+        def work(i, b):
+            ys[b] = self.L.fake_quantize(devs[b], 4, False, self.L.QScheme.PER_GROUP, 128)
+
+        def down(i, b):
+            ys[b].record_stream(torch.cuda.current_stream())
+            out.copy_(ys[b], non_blocking=True)
 
         def one():
-            for _ in self.ws:
-                dev.copy_(host, non_blocking=True)
-                y = self.L.fake_quantize(dev, 4, False, self.L.QScheme.PER_GROUP, 128)
-                out.copy_(y, non_blocking=True)
+            pipe.run(len(self.ws), up, work, down)
 
         one()
         torch.cuda.synchronize()
@@ -497,16 +522,30 @@ class RotQuantWorkload:
         return {"fht3_kernel (hadamard_fake_quantize)": (4.0 * n, t, n, "elements")}
 
     def e2e(self, steps, graph):
+        """hadamard_fake_quantize through the public API on batches copied in
+        from pinned host memory, results copied back, every step
+        (HostPipeline)."""
         torch = self.ctx.torch
+        from llm_quant_b200.streaming import HostPipeline
         host = torch.empty(8192, 4096, dtype=torch.bfloat16).pin_memory()
         host.copy_(self.xs[0].cpu())
         out = torch.empty_like(host).pin_memory()
-        dev = torch.empty_like(self.xs[0])
+        devs = [torch.empty_like(self.xs[0]) for _ in range(2)]
+        ys = [None, None]
+        pipe = HostPipeline(self.ctx.dev, buffers=2)
+
+        def up(i, b):
+            devs[b].copy_(host, non_blocking=True)
+
+        def work(i, b):
+            ys[b] = self.L.hadamard_fake_quantize(devs[b], 4, True)
+
+        def down(i, b):
+            ys[b].record_stream(torch.cuda.current_stream())
+            out.copy_(ys[b], non_blocking=True)
 
         def one():
-            for _ in self.xs:
-                dev.copy_(host, non_blocking=True)
-                out.copy_(self.L.hadamard_fake_quantize(dev, 4, True), non_blocking=True)
+            pipe.run(len(self.xs), up, work, down)
 
         one()
         torch.cuda.synchronize()
@@ -607,25 +646,43 @@ class KVWorkload:
         return {"kv_dequant_seg_kernel (full-cache fp32 read-out)": (5.0 * n, t, n, "elements")}
 
     def e2e(self, steps, graph):
+        """Every layer's 16 update() calls through the public API with the new
+        K, V chunks copied in from pinned host memory and the layer's final
+        fp32 K, V copied back, every step; HostPipeline overlaps the chunk
+        uploads, the kernels and the layer downloads."""
         torch = self.ctx.torch
+        from llm_quant_b200.streaming import HostPipeline
         L = self.L
         hk = [k.cpu().pin_memory() for k in self.k]
         hv = [v.cpu().pin_memory() for v in self.v]
-        dk, dv = torch.empty_like(self.k[0]), torch.empty_like(self.v[0])
+        dks = [torch.empty_like(self.k[0]) for _ in range(2)]
+        dvs = [torch.empty_like(self.v[0]) for _ in range(2)]
         outk = torch.empty(self.B, self.H, self.C * self.U, self.D).pin_memory()
         outv = torch.empty_like(outk).pin_memory()
+        st = {}
+        pipe = HostPipeline(self.ctx.dev, buffers=2)
+
+        def up(i, b):
+            j = i % self.U
+            dks[b].copy_(hk[j], non_blocking=True)
+            dvs[b].copy_(hv[j], non_blocking=True)
+
+        def work(i, b):
+            if i % self.U == 0:
+                st["cache"] = L.QuantizedKVCache(1, L.PerChannelKVCacheQuantizer(8),
+                                                 value_quantizer=L.PerTokenKVCacheQuantizer(4),
+                                                 max_seq_len=self.C * self.U)
+            st["out"] = st["cache"].update(0, dks[b], dvs[b])
+
+        def down(i, b):
+            if i % self.U == self.U - 1:  # the layer's full cache after its last update
+                cur = torch.cuda.current_stream()
+                for o, t in zip((outk, outv), st["out"]):
+                    t.record_stream(cur)
+                    o.copy_(t, non_blocking=True)
 
         def one():
-            for _ in self.layers:
-                cache = L.QuantizedKVCache(1, L.PerChannelKVCacheQuantizer(8),
-                                           value_quantizer=L.PerTokenKVCacheQuantizer(4),
-                                           max_seq_len=self.C * self.U)
-                for j in range(self.U):
-                    dk.copy_(hk[j], non_blocking=True)
-                    dv.copy_(hv[j], non_blocking=True)
-                    fk, fv = cache.update(0, dk, dv)
-                outk.copy_(fk, non_blocking=True)
-                outv.copy_(fv, non_blocking=True)
+            pipe.run(len(self.layers) * self.U, up, work, down)
 
         one()
         torch.cuda.synchronize()
@@ -732,26 +789,37 @@ class W4A16Workload:
         return out
 
     def e2e(self, steps, graph):
-        """Forward through the public API (captured in a CUDA graph) with x
-        copied in from pinned host memory and y copied back, every step."""
+        """Forward through the public API (each layer captured in a CUDA
+        graph) with x copied in from pinned host memory and y copied back,
+        every step; HostPipeline overlaps layer l+1's upload and layer l-1's
+        download with layer l's forward."""
         torch = self.ctx.torch
+        from llm_quant_b200.streaming import HostPipeline
         host = self.x[1024].cpu().pin_memory()
         out = torch.empty(1024, self.N, dtype=self.x[1024].dtype).pin_memory()
-        dev = self.x[1024]
+        devs = [torch.empty_like(self.x[1024]) for _ in self.qls]
         torch.cuda.synchronize()
         graphs, ys = [], []
-        for ql in self.qls:
+        for ql, dev in zip(self.qls, devs):
+            dev.copy_(self.x[1024])
             ql(dev)
             g2 = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g2):
                 ys.append(ql(dev))
             graphs.append(g2)
+        pipe = HostPipeline(self.ctx.dev, buffers=len(self.qls))  # a graph's input is its own buffer
+
+        def up(i, b):
+            devs[i].copy_(host, non_blocking=True)
+
+        def work(i, b):
+            graphs[i].replay()
+
+        def down(i, b):
+            out.copy_(ys[i], non_blocking=True)
 
         def one():
-            for g2, y in zip(graphs, ys):
-                dev.copy_(host, non_blocking=True)
-                g2.replay()
-                out.copy_(y, non_blocking=True)
+            pipe.run(len(self.qls), up, work, down, outputs_reused=True)
 
         one()
         torch.cuda.synchronize()
@@ -917,7 +985,10 @@ class KVAttentionWorkload:
 
     def e2e(self, steps, graph):
         """attend() through the public API for every layer, with the query
-        copied in from pinned host memory and the output copied back."""
+        copied in from pinned host memory and the output copied back.  One
+        stream: with 256 KB of transfers per step, HostPipeline's per-item
+        stream and event handling cost more host time than the overlap saves
+        (measured 1326 against 1759 GB/s)."""
         torch = self.ctx.torch
         hq = self.q.cpu().pin_memory()
         dq = torch.empty_like(self.q)
