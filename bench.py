@@ -988,7 +988,8 @@ class KVAttentionWorkload:
         copied in from pinned host memory and the output copied back.  One
         stream: with 256 KB of transfers per step, HostPipeline's per-item
         stream and event handling cost more host time than the overlap saves
-        (measured 1326 against 1759 GB/s)."""
+        (measured 1326 against 1759 GB/s before the combine kernel became a
+        programmatic dependent launch)."""
         torch = self.ctx.torch
         hq = self.q.cpu().pin_memory()
         dq = torch.empty_like(self.q)

@@ -36,10 +36,38 @@
 // running max, running sum) are merged by kv_attn_combine_kernel.
 #include "lq_common.cuh"
 
+#include <utility>
+
 namespace lq {
 namespace {
 
 constexpr int kAttnWarps = 4;
+
+// Programmatic dependent launch: the combine kernel is launched with
+// programmatic stream serialization, so its blocks may be scheduled once
+// every attention block has passed pdl_trigger() (after its token loop), and
+// pdl_wait() (its first statement) blocks until the attention kernel has
+// completed and its writes are visible -- a no-op for an ordinary launch.
+// The combine's launch and block scheduling overlap the attention kernel's
+// merge and tail instead of following them.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 constexpr int kTile = 16;  // tokens per tile
 
 struct KvSide {
@@ -627,6 +655,7 @@ __global__ void __launch_bounds__(32 * kAttnWarps, (NQ == 1 && !GEN) ? 4 : 1) kv
   }
 
   // ---- merge the 4 warps in shared memory (the ring is free now) ----
+  if (threadIdx.x == 0) pdl_trigger();  // token loop done: the combine's blocks may launch
   __syncthreads();
   float* mb = reinterpret_cast<float*>(ring);  // [warps][NR]
   float* lb = mb + kAttnWarps * NR;            // [warps][NR]
@@ -687,6 +716,7 @@ __global__ void __launch_bounds__(128) kv_attn_combine_kernel(const float* __res
                                                               int rows, int D, int H, int Hq, int Sq,
                                                               int G, int64_t n_items, uint8_t* out,
                                                               int out_dtype) {
+  pdl_wait();  // the attention kernel's partials are complete and visible
   const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (e >= n_items * D) return;
   const int64_t item = e / D;
@@ -765,9 +795,9 @@ int launch_attn(const AttnArgs& a, int B, int row_blocks, int combine_items, cud
   kern<<<grid, 32 * kAttnWarps, smem, st>>>(a);
   int rc = launched("kv_attn_kernel");
   if (rc != LQ_OK || a.n_split == 1) return rc;
-  kv_attn_combine_kernel<<<(combine_items * D + 127) / 128, 128, 0, st>>>(a.ws, a.n_split, a.rows, D, a.H, a.Hq,
-                                                                   a.Sq, a.G, combine_items, a.out,
-                                                                   a.q_dtype);
+  launch_pdl(kv_attn_combine_kernel, dim3((unsigned)((combine_items * D + 127) / 128)), dim3(128), 0, st,
+             (const float*)a.ws, a.n_split, a.rows, D, a.H, a.Hq, a.Sq, a.G, (int64_t)combine_items, a.out,
+             a.q_dtype);
   return launched("kv_attn_combine_kernel");
 }
 
