@@ -16,6 +16,7 @@
 #include <atomic>
 #include <cstdio>
 #include <string>
+#include <utility>
 
 #include "../../include/lq_sm100.h"
 
@@ -47,6 +48,32 @@ inline int launched(const char* what) {
       return (code);                \
     }                               \
   } while (0)
+
+// Programmatic dependent launch.  A kernel launched with launch_pdl() may be
+// scheduled before the kernel ahead of it in the stream has finished;
+// pdl_wait() blocks until that kernel has completed and its memory writes are
+// visible (a no-op after an ordinary launch), so a kernel calls it before its
+// first global-memory access -- the stream-ordered allocator may have handed
+// it memory the previous kernel still uses.  pdl_trigger() lets the next
+// kernel's blocks launch before this one has finished.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 // Return the status of a helper that failed (it has already set the error).
 #define LQ_TRY(expr)                  \

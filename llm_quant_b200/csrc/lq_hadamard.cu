@@ -139,6 +139,8 @@ __global__ void __launch_bounds__(256) fht_warp_kernel(const T* __restrict__ x, 
                                                        T* __restrict__ out,
                                                        T* __restrict__ scale_out,
                                                        T* __restrict__ zp_out, int vec) {
+  pdl_wait();  // launched as a programmatic dependent: the previous kernel is done
+  pdl_trigger();
   const int tps = a.d / E;
   const int lane = threadIdx.x & 31;
   const int t = lane & (tps - 1);
@@ -178,6 +180,8 @@ __global__ void __launch_bounds__(1024) fht_block_kernel(const T* __restrict__ x
                                                          T* __restrict__ out,
                                                          T* __restrict__ scale_out,
                                                          T* __restrict__ zp_out, int vec) {
+  pdl_wait();  // launched as a programmatic dependent: the previous kernel is done
+  pdl_trigger();
   extern __shared__ float sm[];  // [d]
   __shared__ MinMax red[32];
   const int t = threadIdx.x, lane = t & 31;
@@ -328,6 +332,8 @@ __global__ void __launch_bounds__((1 << L) / 32) fht3_kernel(const T* __restrict
                                                             T* __restrict__ out,
                                                             T* __restrict__ scale_out,
                                                             T* __restrict__ zp_out) {
+  pdl_wait();  // launched as a programmatic dependent: the previous kernel is done
+  pdl_trigger();
   constexpr int D = 1 << L, NT = D / 32, C3 = L - 9, NF = 1 << (4 - C3), NK3 = 1 << C3;
   constexpr bool kBf16 = Ty<T>::code == LQ_BF16;
   __shared__ float2 sm[(D / 2) + (D / 32)];
@@ -529,12 +535,12 @@ int fht_launch(const T* x, FhtArgs a, T* out, T* s, T* z, cudaStream_t st) {
     grid = grid < 1 ? 1 : (grid > cap ? cap : grid);
     int vec = vec_for(E);
     switch (E) {
-      case 1: fht_warp_kernel<T, 1, QUANT><<<grid, 256, 0, st>>>(x, a, out, s, z, 0); break;
-      case 2: fht_warp_kernel<T, 2, QUANT><<<grid, 256, 0, st>>>(x, a, out, s, z, 0); break;
-      case 4: fht_warp_kernel<T, 4, QUANT><<<grid, 256, 0, st>>>(x, a, out, s, z, vec); break;
-      case 8: fht_warp_kernel<T, 8, QUANT><<<grid, 256, 0, st>>>(x, a, out, s, z, vec); break;
-      case 16: fht_warp_kernel<T, 16, QUANT><<<grid, 256, 0, st>>>(x, a, out, s, z, vec); break;
-      case 32: fht_warp_kernel<T, 32, QUANT><<<grid, 256, 0, st>>>(x, a, out, s, z, vec); break;
+      case 1: launch_pdl(fht_warp_kernel<T, 1, QUANT>, dim3((unsigned)(grid)), dim3((unsigned)(256)), 0, st, x, a, out, s, z, 0); break;
+      case 2: launch_pdl(fht_warp_kernel<T, 2, QUANT>, dim3((unsigned)(grid)), dim3((unsigned)(256)), 0, st, x, a, out, s, z, 0); break;
+      case 4: launch_pdl(fht_warp_kernel<T, 4, QUANT>, dim3((unsigned)(grid)), dim3((unsigned)(256)), 0, st, x, a, out, s, z, vec); break;
+      case 8: launch_pdl(fht_warp_kernel<T, 8, QUANT>, dim3((unsigned)(grid)), dim3((unsigned)(256)), 0, st, x, a, out, s, z, vec); break;
+      case 16: launch_pdl(fht_warp_kernel<T, 16, QUANT>, dim3((unsigned)(grid)), dim3((unsigned)(256)), 0, st, x, a, out, s, z, vec); break;
+      case 32: launch_pdl(fht_warp_kernel<T, 32, QUANT>, dim3((unsigned)(grid)), dim3((unsigned)(256)), 0, st, x, a, out, s, z, vec); break;
       default: set_error("internal: bad E %d", E); return LQ_EINVAL;
     }
     return launched("fht_warp_kernel");
@@ -549,7 +555,7 @@ int fht_launch(const T* x, FhtArgs a, T* out, T* s, T* z, cudaStream_t st) {
     const int grid = (int)(a.rows < cap ? a.rows : cap);
     FhtArgs a3 = a;
     a3.al32 = (reinterpret_cast<uintptr_t>(x) & 31) == 0;
-    k3<<<grid, d / 32, 0, st>>>(x, a3, out, s, z);
+    launch_pdl(k3, dim3((unsigned)(grid)), dim3((unsigned)(d / 32)), 0, st, x, a3, out, s, z);
     return launched("fht3_kernel");
   }
   int E = (d <= 8192) ? 16 : 32;
@@ -570,7 +576,7 @@ int fht_launch(const T* x, FhtArgs a, T* out, T* s, T* z, cudaStream_t st) {
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     LQ_REQUIRE(e == cudaSuccess, LQ_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   }
-  k<<<grid, NT, smem, st>>>(x, a, out, s, z, vec);
+  launch_pdl(k, dim3((unsigned)(grid)), dim3((unsigned)(NT)), smem, st, x, a, out, s, z, vec);
   return launched("fht_block_kernel");
 }
 

@@ -36,38 +36,17 @@
 // running max, running sum) are merged by kv_attn_combine_kernel.
 #include "lq_common.cuh"
 
-#include <utility>
-
 namespace lq {
 namespace {
 
 constexpr int kAttnWarps = 4;
 
-// Programmatic dependent launch: the combine kernel is launched with
-// programmatic stream serialization, so its blocks may be scheduled once
-// every attention block has passed pdl_trigger() (after its token loop), and
-// pdl_wait() (its first statement) blocks until the attention kernel has
-// completed and its writes are visible -- a no-op for an ordinary launch.
-// The combine's launch and block scheduling overlap the attention kernel's
-// merge and tail instead of following them.
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-
-template <typename... KArgs, typename... Args>
-cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
-                       Args&&... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
-}
+// The combine kernel is a programmatic dependent launch (launch_pdl): its
+// blocks may be scheduled once every attention block has passed
+// pdl_trigger() (after its token loop), and its first statement, pdl_wait(),
+// blocks until the attention kernel's partials are complete and visible.  The
+// combine's launch and block scheduling overlap the attention kernel's merge
+// and tail instead of following them.
 constexpr int kTile = 16;  // tokens per tile
 
 struct KvSide {

@@ -529,6 +529,8 @@ __global__ void __launch_bounds__(256, 2) nf4_pack_g64_kernel(const __grid_const
   }
   build_lut_g64(lut);
   __syncthreads();
+  pdl_wait();     // the previous kernel in the stream is done (its memory may be reused here)
+  pdl_trigger();  // the next kernel may launch (it waits for this one the same way)
   if (t == 0) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap)) : "memory");
     for (int j = 0; j < kG64Stages; ++j) {
@@ -743,6 +745,8 @@ __global__ void __launch_bounds__(256) nf4_unpack_vec_kernel(const uint32_t* __r
     reinterpret_cast<uint4*>(pair)[threadIdx.x + 256 * j] = make_uint4(v, v, v, v);
   }
   __syncthreads();
+  pdl_wait();     // the previous kernel in the stream (the packing) is done
+  pdl_trigger();
   const char* pb = reinterpret_cast<const char*>(pair);
   const int lane = threadIdx.x & 31;
   const uint32_t lane4 = (uint32_t)lane * 4;
@@ -944,7 +948,7 @@ int nf4_quant_launch(const T* x, NfArgs a, void* codes, T* scales, T* qs, T* dqs
           LQ_REQUIRE(e == cudaSuccess, LQ_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
           attr_done.fetch_or(bit);
         }
-        kern<<<grid_cap(n_chunks, 2), 256, kG64SmemBytes, st>>>(map, n_chunks, o);
+        launch_pdl(kern, dim3((unsigned)grid_cap(n_chunks, 2)), dim3(256), kG64SmemBytes, st, map, n_chunks, o);
         return launched("nf4_pack_g64_kernel");
       }
     }
@@ -1013,8 +1017,8 @@ int nf4_dequant_t(const void* codes, int cdt, int64_t n, int64_t G, int64_t DG, 
     const int64_t nchunk = n / 8;
     if (nchunk > 0) {
       const int grid = resident_grid(nf4_unpack_vec_kernel<T>, 256, 0, (nchunk + 256 * kUnpackK - 1) / (256 * kUnpackK));
-      nf4_unpack_vec_kernel<T><<<grid, 256, 0, st>>>(
-          static_cast<const uint32_t*>(codes), a, sp, q, d, reinterpret_cast<uint4*>(o), nchunk);
+      launch_pdl(nf4_unpack_vec_kernel<T>, dim3(grid), dim3(256), 0, st, static_cast<const uint32_t*>(codes), a,
+                 sp, q, d, reinterpret_cast<uint4*>(o), nchunk);
       int rc = launched("nf4_unpack_vec_kernel");
       if (rc) return rc;
       done = nchunk * 8;
