@@ -43,6 +43,53 @@ def test_fake_quantize_stream_matches_direct(L):
             assert torch.equal(o, ref)
 
 
+def test_nf4_pack_stream_matches_direct(L):
+    """QLoRALinear.pack_base + _dequantize_base of host weights through the
+    pipeline (the packing kernels are programmatic dependent launches that
+    follow a cross-stream wait on the upload): codes, scales and the
+    dequantized base equal a direct call on the same weights."""
+    from llm_quant_b200.streaming import HostPipeline
+    g = torch.Generator().manual_seed(2)
+    shapes = [(256, 1024), (1024, 512), (128, 4096), (512, 2048), (256, 1024)]
+    hosts = [(torch.randn(o, k, generator=g) * 0.02).to(torch.bfloat16).pin_memory() for o, k in shapes]
+    mods = [L.QLoRALinear(k, o, rank=4, group_size=64).cuda() for o, k in shapes]
+    devs = [torch.empty(o, k, dtype=torch.bfloat16, device="cuda") for o, k in shapes]
+
+    def res(m):
+        return (m.nf4_codes_packed, m.nf4_scales, m.dq_q_scales, m.dq_scales)
+
+    outs = [None] * len(shapes)
+    deq = [torch.empty(o, k, dtype=torch.bfloat16).pin_memory() for o, k in shapes]
+    last = [None] * len(shapes)
+    pipe = HostPipeline(buffers=len(shapes))
+
+    def up(i, b):
+        devs[i].copy_(hosts[i], non_blocking=True)
+
+    def work(i, b):
+        mods[i].pack_base(devs[i])
+        last[i] = mods[i]._dequantize_base()
+
+    def down(i, b):
+        cur = torch.cuda.current_stream()
+        if outs[i] is None:
+            outs[i] = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in res(mods[i])]
+        for o, t in zip(outs[i], res(mods[i])):
+            t.record_stream(cur)
+            o.copy_(t, non_blocking=True)
+        last[i].record_stream(cur)
+        deq[i].copy_(last[i], non_blocking=True)
+
+    pipe.run(len(shapes), up, work, down)
+    torch.cuda.current_stream().synchronize()
+    for i, (o, k) in enumerate(shapes):
+        ref = L.QLoRALinear(k, o, rank=4, group_size=64).cuda()
+        ref.pack_base(hosts[i].cuda())
+        for got, want in zip(outs[i], res(ref)):
+            assert torch.equal(got, want.cpu())
+        assert torch.equal(deq[i], ref._dequantize_base().cpu())
+
+
 def test_graph_outputs_reused(L):
     """Work that replays a CUDA graph rewrites the same output buffer every
     run: outputs_reused orders it after the previous run's download."""
