@@ -7,9 +7,13 @@
 // Tile = 128 weight rows x BT tokens ("swap AB"): the dequantized weights are
 // the MMA's A operand and live in tensor memory, the activations are the B
 // operand (TMA, 128-byte swizzle, K-major), the fp32 accumulator D[128, BT]
-// is in tensor memory.  Warp roles (576 threads):
-//   warp 0       TMA producer: activation tile + packed 4-bit weight tile +
-//                (zero, scale) pairs per stage, one mbarrier per stage each;
+// is in tensor memory.  Warp roles (608 threads):
+//   warp 0       activation producer: one TMA tile per stage into the
+//                activation ring (S stages, refilled when the stage's MMAs
+//                have completed);
+//   warp 18      weight producer: packed 4-bit weight tile + (zero, scale)
+//                pairs per stage into the weight ring (SW >= S stages,
+//                refilled once the dequant warps have read the slot);
 //   warp 1       allocates tensor memory, one lane issues tcgen05.mma
 //                (4 x K=16 per 64-wide K step) and tcgen05.commit;
 //   warps 2..17  dequantize, in two groups of eight taking alternate stages:
@@ -178,28 +182,43 @@ __device__ __forceinline__ uint32_t pair_lut_off(uint32_t w, int b, uint32_t lan
   return off | lane4;
 }
 
-// Block: producer warp, MMA warp, kDG groups of 8 dequant / epilogue warps.
-// Group g dequantizes the stages g, g + kDG, ...: one warp's per-stage chain
-// (barrier waits, shared loads, conversion, tcgen05.st and its wait, arrive)
-// is latency- not issue-bound, so two groups keep two stages in flight.
+// Block: activation producer warp, MMA warp, kDG groups of 8 dequant /
+// epilogue warps, weight producer warp.  Group g dequantizes the stages g,
+// g + kDG, ...: one warp's per-stage chain (barrier waits, shared loads,
+// conversion, tcgen05.st and its wait, arrive) is latency- not issue-bound,
+// so two groups keep two stages in flight.
 constexpr int kDG = 2;
-constexpr int kW4Threads = 64 + 256 * kDG;
+constexpr int kW4Threads = 64 + 256 * kDG + 32;
+constexpr int kWProdWarp = kW4Threads / 32 - 1;
 
 // A stage holds WK 64-wide K halves (WK = 2: 128 K per stage), so the
 // per-stage barrier round trips and MMA-thread bookkeeping -- which pace the
 // pipeline, not the tensor cores -- are paid once per 128 K.
+// The weights (packed codes + (zero, scale) pairs) have a ring of their own,
+// SW stages deep (what shared memory leaves, at most 8): a slot is refilled
+// once the dequant warps are done with it, not when the MMA that used the
+// stage completes, so a stage's weights are requested up to SW stages before
+// its dequantization instead of S - 1 MMA steps before (with the weights
+// arriving late, the dequant warps waited on them: 17 % of the kernel time).
 template <typename T, int BT, int S, bool NF, int WK>
 struct Smem {
   static constexpr int kXh = BT * kBK * 2;  // activation bytes of one 64-wide half
   static constexpr int kX = WK * kXh;       // activation tile bytes per stage
+  static constexpr int kWS = WK * (kWStage + kSStage);  // weight + pair bytes per stage
+  static constexpr int kRest = (NF ? kPairLutWords * 4 + 1024 : 0) + 2048;  // table, barriers, slack
+  // 226 KB: a block's opt-in limit is 1 KB under the SM's 227 KB (a
+  // 231648-byte layout failed cudaFuncSetAttribute, 231168 bytes launched)
+  static constexpr int kBudget = 226 * 1024;
+  static constexpr int kFit = (kBudget - S * kX - kRest) / kWS;
+  static constexpr int SW = kFit > 8 ? 8 : kFit;
   static constexpr int off_x = 0;
-  static constexpr int off_w = off_x + S * kX;                  // [S][WK] weight halves
-  static constexpr int off_s = off_w + S * WK * kWStage;        // [S][WK] pair halves
-  static constexpr int off_lut = off_s + S * WK * kSStage;      // NF4 pair table (NF only)
+  static constexpr int off_w = off_x + S * kX;                  // [SW][WK] weight halves
+  static constexpr int off_s = off_w + SW * WK * kWStage;       // [SW][WK] pair halves
+  static constexpr int off_lut = off_s + SW * WK * kSStage;     // NF4 pair table (NF only)
   static constexpr int off_tmp = off_lut + (NF ? kPairLutWords * 4 : 0);
   static constexpr int off_bar = off_tmp + (NF ? 1024 : 0);
-  // barriers: full_x[S], full_w[S], a_full[S], empty[S], acc_full
-  static constexpr int n_bar = 4 * S + 1;
+  // barriers: full_x[S], a_full[S], empty[S], full_w[SW], w_empty[SW], acc_full
+  static constexpr int n_bar = 3 * S + 2 * SW + 1;
   static constexpr int off_tmem = off_bar + n_bar * 8;
   static constexpr int bytes = off_tmem + 16 + 1024;  // + alignment slack
 };
@@ -212,17 +231,20 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
                                                        int* __restrict__ err) {
   using L = Smem<T, BT, S, NF, WK>;
   constexpr int SC = WK * (kBK / 2);  // tensor-memory columns of one stage's A slot
+  constexpr int SW = L::SW;           // weight-ring stages
   static_assert(BT % 16 == 0 && BT <= kAcol && kAcol + S * SC <= (int)kTmemCols,
                 "accumulator and A slots must fit tensor memory without overlap");
-  static_assert(L::bytes <= 227 * 1024, "shared memory per CTA");
+  static_assert(L::bytes <= L::kBudget, "shared memory per CTA");
+  static_assert(SW >= S, "the weight ring is at least as deep as the activation ring");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::off_bar);
   uint64_t* full_x = bars;
-  uint64_t* full_w = bars + S;
-  uint64_t* a_full = bars + 2 * S;
-  uint64_t* empty = bars + 3 * S;
-  uint64_t* acc_full = bars + 4 * S;
+  uint64_t* a_full = bars + S;
+  uint64_t* empty = bars + 2 * S;
+  uint64_t* full_w = bars + 3 * S;
+  uint64_t* w_empty = bars + 3 * S + SW;
+  uint64_t* acc_full = bars + 3 * S + 2 * SW;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::off_tmem);
   __shared__ int s_err;
 
@@ -238,9 +260,12 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
     s_err = 0;
     for (int i = 0; i < S; ++i) {
       mbar_init(&full_x[i], 1);
-      mbar_init(&full_w[i], 1);
       mbar_init(&a_full[i], 8);  // one arrival per dequant warp
       mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < SW; ++i) {
+      mbar_init(&full_w[i], 1);
+      mbar_init(&w_empty[i], 8);  // one arrival per dequant warp, once it has read the slot
     }
     mbar_init(acc_full, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -261,7 +286,7 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ---------------- producer ----------------
+    // ---------------- activation producer ----------------
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_x)) : "memory");
       int issued = 0;
@@ -273,22 +298,33 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
 #pragma unroll
         for (int hk = 0; hk < WK; ++hk)
           tma_load_2d(smem + L::off_x + s * L::kX + hk * L::kXh, &tmap_x, (i * WK + hk) * kBK, m0, &full_x[s]);
-        mbar_expect_tx(&full_w[s], WK * (kWStage + kSStage));
-        // the WK weight halves of a step are adjacent in the packed layout
-        bulk_load(smem + L::off_w + s * WK * kWStage, wtile + (size_t)i * WK * kWStage, WK * kWStage, &full_w[s]);
-#pragma unroll
-        for (int hk = 0; hk < WK; ++hk) {
-          const int g = group_of(a, i * WK + hk);
-          bulk_load(smem + L::off_s + (s * WK + hk) * kSStage, stile + (size_t)g * kSStage, kSStage, &full_w[s]);
-        }
         issued = i + 1;
       }
       if (s_err) {
         // drain: wait (bounded) for every stage this thread may still have in flight
-        for (int i = (issued > S ? issued - S : 0); i < issued; ++i) {
-          mbar_wait(&full_x[i % S], (i / S) & 1);
-          mbar_wait(&full_w[i % S], (i / S) & 1);
+        for (int i = (issued > S ? issued - S : 0); i < issued; ++i) mbar_wait(&full_x[i % S], (i / S) & 1);
+      }
+    }
+  } else if (warp == kWProdWarp) {
+    // ---------------- weight producer ----------------
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0; i < n_steps; ++i) {
+        const int sw = i % SW;
+        if (i >= SW && !mbar_wait(&w_empty[sw], ((i / SW) - 1) & 1)) { s_err = 5; break; }
+        if (s_err) break;
+        mbar_expect_tx(&full_w[sw], WK * (kWStage + kSStage));
+        // the WK weight halves of a step are adjacent in the packed layout
+        bulk_load(smem + L::off_w + sw * WK * kWStage, wtile + (size_t)i * WK * kWStage, WK * kWStage, &full_w[sw]);
+#pragma unroll
+        for (int hk = 0; hk < WK; ++hk) {
+          const int g = group_of(a, i * WK + hk);
+          bulk_load(smem + L::off_s + (sw * WK + hk) * kSStage, stile + (size_t)g * kSStage, kSStage, &full_w[sw]);
         }
+        issued = i + 1;
+      }
+      if (s_err) {
+        for (int i = (issued > SW ? issued - SW : 0); i < issued; ++i) mbar_wait(&full_w[i % SW], (i / SW) & 1);
       }
     }
   } else if (warp == 1) {
@@ -331,13 +367,14 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
     for (int i = grp; i < n_steps && ok; i += kDG) {
       const int s = i % S;
       const uint32_t ph = (i / S) & 1;
-      if (!mbar_wait_warp(&full_w[s], ph)) { ok = false; break; }
+      const int sw = i % SW;
+      if (!mbar_wait_warp(&full_w[sw], (i / SW) & 1)) { ok = false; break; }
       if (i >= S && !mbar_wait_warp(&empty[s], ph ^ 1)) { ok = false; break; }
 #pragma unroll
       for (int hk = 0; hk < WK; ++hk) {
         // this warp's half of the row's codes: words 4h..4h+3 (k = 32h..32h+31)
-        const uint4 cw = reinterpret_cast<const uint4*>(smem + L::off_w + (s * WK + hk) * kWStage + row * 32)[h];
-        const uint32_t zs = *reinterpret_cast<const uint32_t*>(smem + L::off_s + (s * WK + hk) * kSStage + row * 4);
+        const uint4 cw = reinterpret_cast<const uint4*>(smem + L::off_w + (sw * WK + hk) * kWStage + row * 32)[h];
+        const uint32_t zs = *reinterpret_cast<const uint32_t*>(smem + L::off_s + (sw * WK + hk) * kSStage + row * 4);
         // zs = (zero_b, scale) as a T pair; broadcast each half to both halves
         const uint32_t zb = __byte_perm(zs, zs, 0x1010);
         const uint32_t sc = __byte_perm(zs, zs, 0x3232);
@@ -370,9 +407,14 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
       // 128-wide stages: warp 2 also waits for the stage's activations, so
       // a_full stands for both and the MMA thread waits once per stage
       if (WK == 2 && wi == 0 && !mbar_wait_warp(&full_x[s], ph)) { ok = false; break; }
-      // one elected arrival per warp once every lane's store has landed
+      // one elected arrival per warp once every lane's store has landed; the
+      // warp has read its weights too, so the weight slot (needed again SW >= S
+      // stages later) is released in the same step
       __syncwarp();
-      if (lane == 0) mbar_arrive(&a_full[s]);
+      if (lane == 0) {
+        mbar_arrive(&w_empty[sw]);
+        mbar_arrive(&a_full[s]);
+      }
     }
     if (!ok) s_err = 3;
     // epilogue: accumulator rows = weight rows (this thread's row), columns = tokens
