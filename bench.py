@@ -59,7 +59,7 @@ NCU_TRAFFIC = {
     "group": 212.4e6 / (8192 * 4096),    # group_warp_kernel, 6.33 B per element
     "rotquant": 222.0e6 / (16384 * 4096),  # fht3_kernel, 3.31 B per element
     "kv": 277.2e6 / (8 * 8 * 8192 * 128),  # kv_dequant_seg_kernel, 4.13 B per element
-    "w4a16": 45.3e6,                     # w4a16_kernel at M = 1024, bytes per launch
+    "w4a16": 44.7e6,                     # w4a16_kernel at M = 1024, bytes per launch
     "kv_attention": 70.2e6 / (8 * 8 * 4096),  # kv_attn_kernel, 268 B per cached token
 }
 
