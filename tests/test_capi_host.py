@@ -316,3 +316,11 @@ def test_fp16_code_range_overflow_raises_like_reference():
         L._C.check_clamp_bounds(torch.float16, 16, False)
     L._C.check_clamp_bounds(torch.float16, 16, True)    # qmax 32767 fits
     L._C.check_clamp_bounds(torch.bfloat16, 16, False)  # 65535 -> 65536 fits in bf16
+
+
+def test_host_pipeline_arguments_without_gpu():
+    """streaming.HostPipeline imports without a GPU and rejects a pipeline with
+    no device buffers before touching CUDA."""
+    from llm_quant_b200.streaming import HostPipeline
+    with pytest.raises(ValueError):
+        HostPipeline(device="cuda:0", buffers=0)
