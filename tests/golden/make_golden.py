@@ -12,7 +12,7 @@ copied).  Every case stores its seeded inputs and the reference outputs in
 patterns.  Case parameters live in the JSON string ``<case>/params``.
 
 These fixtures pin the oracle (``oracle/lq_oracle.py``) and are the reference
-side of the GPU parity tests; nothing on the GPU box needs the reference.
+side of the GPU parity tests; the tests read only the fixtures, never the reference.
 """
 
 from __future__ import annotations
