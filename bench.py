@@ -60,7 +60,7 @@ NCU_TRAFFIC = {
     "rotquant": 222.0e6 / (16384 * 4096),  # fht3_kernel, 3.31 B per element
     "kv": 277.2e6 / (8 * 8 * 8192 * 128),  # kv_dequant_seg_kernel, 4.13 B per element
     "w4a16": 44.7e6,                     # w4a16_kernel at M = 1024, bytes per launch
-    "kv_attention": 70.2e6 / (8 * 8 * 4096),  # kv_attn_kernel, 268 B per cached token
+    "kv_attention": 70.5e6 / (8 * 8 * 4096),  # kv_attn_kernel, 269 B per cached token
 }
 
 
