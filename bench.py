@@ -228,6 +228,44 @@ def cpu_time(fn_chunk, chunks, reps=3):
     return statistics.median(ts), n
 
 
+REF_INSTALL = os.path.join(ROOT, "baseline", "_ref")
+
+
+def reference_package():
+    """The reference package itself (its torch CPU code), from the installed
+    copy in baseline/_ref (written by oracle/install_ref.py; not part of the
+    product), or None with the reason when it is absent."""
+    if not os.path.exists(os.path.join(REF_INSTALL, "llm_quant", "qlora.py")):
+        return None, "the reference is not installed (python oracle/install_ref.py)"
+    if REF_INSTALL not in sys.path:
+        sys.path.insert(0, REF_INSTALL)
+    import importlib
+    mod = importlib.import_module("llm_quant")
+    if not os.path.abspath(mod.__file__).startswith(REF_INSTALL):
+        return None, f"llm_quant resolves to {mod.__file__}, not the installed reference"
+    return mod, None
+
+
+def reference_torch_leg(fn, nbytes, sample, reps=3):
+    """Median wall time of the reference's own torch CPU call fn() (after one
+    warm-up) with torch's intra-op threads on every host core."""
+    import torch
+    threads = torch.get_num_threads()
+    torch.set_num_threads(_threads())
+    try:
+        fn()
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+    finally:
+        torch.set_num_threads(threads)
+    t = statistics.median(ts)
+    return {"value": nbytes / t / 1e9, "unit": "GB/s", "cores": _threads(),
+            "kind": "reference_torch", "sample": f"{sample}, median of {reps}"}
+
+
 # ─────────────────────────────────────────────────────────────────────────────
 # workloads
 # ─────────────────────────────────────────────────────────────────────────────
@@ -299,6 +337,25 @@ class NF4Workload:
             "nf4_pack_g64_kernel (pack_base)": (b_pack, t_pack, n, "weights"),
             "nf4_unpack_vec_kernel (_dequantize_base)": (b_unpack, t_unpack, n, "weights"),
         }
+
+    def api_int64_kernels(self):
+        """nf4_quantize + nf4_dequantize through the functional API with int64
+        codes (qlora.py:66-157), on the largest weights of the rank (each
+        117 MB of bf16 and 470 MB of codes, more than L2): 2 + 8 + 8 + 2 +
+        2 x 2/64 = 20.06 algorithmic bytes per weight."""
+        torch = self.ctx.torch
+        n = max(w.numel() for w in self.weights)
+        idx = [j for j, w in enumerate(self.weights) if w.numel() == n][:2]
+        c = [0]
+
+        def f():
+            w = self.weights[idx[c[0] % len(idx)]]
+            codes, s = self.L.nf4_quantize(w, 64)
+            self.L.nf4_dequantize(codes, s, 64, tuple(w.shape))
+            c[0] += 1
+        t = cuda_time_ms(torch, f, 2 * len(idx))
+        b = (2 + 8 + 8 + 2) * n + 2 * 2 * (n / 64)
+        return {"nf4_quant_kernel + nf4_dequant (API int64 codes)": (b, t, n, "weights")}
 
     def e2e(self, steps, graph):
         """The step's public-API calls (pack_base / _dequantize_base) with every
@@ -383,9 +440,31 @@ class NF4Workload:
 
         t, n = cpu_time(run, chunks)
         b = NF4Workload.bytes_for(w.size)
-        return {"value": b / t / 1e9, "unit": "GB/s", "cores": n, "kind": "port",
-                "sample": f"oracle NF4 pack+dequant of {w.size} bf16 weights ({len(chunks)} chunks "
-                          f"on {n} threads), median of 3"}
+        out = {"value": b / t / 1e9, "unit": "GB/s", "cores": n, "kind": "port",
+               "sample": f"oracle NF4 pack+dequant of {w.size} bf16 weights ({len(chunks)} chunks "
+                         f"on {n} threads), median of 3"}
+        out["reference_torch"] = NF4Workload.reference_torch(w)
+        return out
+
+    @staticmethod
+    def reference_torch(w):
+        """The reference's own torch CPU path on the same sample:
+        nf4_quantize + double_quantize + double_dequantize + nf4_dequantize
+        (qlora.py:66-223), the calls pack_base / _dequantize_base make."""
+        ref, why = reference_package()
+        if ref is None:
+            return {"unavailable": why}
+        import torch
+        from llm_quant import qlora as RQ
+        x = torch.from_numpy(np.array(w, np.float32)).to(torch.bfloat16)
+
+        def run():
+            codes, s = RQ.nf4_quantize(x, 64)
+            q, dq = RQ.double_quantize(s, 256)
+            RQ.nf4_dequantize(codes, RQ.double_dequantize(q, dq, 256), 64, tuple(x.shape))
+        return reference_torch_leg(run, NF4Workload.bytes_for(x.numel()),
+                                   f"reference torch NF4 pack+dequant of {x.numel()} bf16 weights "
+                                   "(packed-path bytes)")
 
 
 class GroupWorkload:
@@ -473,9 +552,20 @@ class GroupWorkload:
         w = (rng.standard_normal((1024, 4096)) * 0.02).astype(np.float32)
         chunks = [w[i:i + 32] for i in range(0, 1024, 32)]
         t, n = cpu_time(lambda c: O.fake_quantize(c, "float32", 4, False, "per_group", 128), chunks)
-        return {"value": 8.0 * w.size / t / 1e9, "unit": "GB/s", "cores": n, "kind": "port",
-                "sample": f"oracle fake_quantize of fp32 [1024, 4096] ({len(chunks)} chunks on "
-                          f"{n} threads), median of 3"}
+        out = {"value": 8.0 * w.size / t / 1e9, "unit": "GB/s", "cores": n, "kind": "port",
+               "sample": f"oracle fake_quantize of fp32 [1024, 4096] ({len(chunks)} chunks on "
+                         f"{n} threads), median of 3"}
+        ref, why = reference_package()
+        if ref is None:
+            out["reference_torch"] = {"unavailable": why}
+        else:
+            import torch
+            from llm_quant.core import quantizer as RQ
+            x = torch.from_numpy(w)
+            out["reference_torch"] = reference_torch_leg(
+                lambda: RQ.fake_quantize(x, 4, False, RQ.QScheme.PER_GROUP, 128), 8.0 * w.size,
+                "reference torch fake_quantize of fp32 [1024, 4096]")
+        return out
 
 
 class RotQuantWorkload:
@@ -1139,6 +1229,35 @@ def run_reference(args):
     return 0
 
 
+def other_kernels(ctx, nf4, hbm, tflops):
+    """The rest of the metric beside the NF4 line, each kernel timed alone
+    with CUDA events on its stream over inputs larger than L2: the NF4
+    functional API with int64 codes, group fake-quant (fp32 4096 x 4096,
+    INT4 asym g128), Hadamard + per-token INT4 (bf16 8192 x 4096) and the
+    QuantizedLinear W4A16 forward (K 4096, N 14336, g128) at every M."""
+    torch = ctx.torch
+
+    def hbm_entry(b, t):
+        gbs = b / (t * 1e-3) / 1e9
+        return {"ms": t, "GB/s": gbs, "frac_of_peak": gbs / hbm}
+
+    out = {k: hbm_entry(b, t) for k, (b, t, _, _) in nf4.api_int64_kernels().items()}
+    for cls in (GroupWorkload, RotQuantWorkload):
+        w = cls(ctx)
+        out.update({k: hbm_entry(b, t) for k, (b, t, _, _) in w.kernels().items()})
+        del w
+    w = W4A16Workload(ctx)
+    for k, (fl, t, m, wb) in w.kernels().items():
+        tf = fl / (t * 1e-3) / 1e12
+        gbs = wb / (t * 1e-3) / 1e9
+        out[k] = {"ms": t, "TFLOP/s": tf, "frac_of_tensor_peak": tf / tflops, "GB/s": gbs,
+                  "frac_of_hbm_peak": gbs / hbm, "bound": "hbm" if m <= 16 else "tensor"}
+    del w
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args):
     ctx = Ctx(args.gpus)
     torch = ctx.torch
@@ -1202,6 +1321,8 @@ def run_ours(args):
                     "units_per_launch": f"{units} {unit_name}"}
         kernels = {k: {"ms": v[1], "GB/s": v[0] / (v[1] * 1e-3) / 1e9,
                        "frac_of_peak": v[0] / (v[1] * 1e-3) / 1e9 / hbm} for k, v in kern.items()}
+    if W.name == "nf4" and ctx.world == 1 and not args.no_extra:
+        kernels.update(other_kernels(ctx, W, hbm, tflops))
 
     e2e_ms, h2d, d2h = W.e2e(max(1, args.e2e_steps), graph)
     e2e_ms = ctx.max(e2e_ms)
@@ -1227,7 +1348,10 @@ def run_ours(args):
                        if W.name in ("nf4", "kv") else f"independent x{ctx.world}",
                        "l2": "inputs larger than L2 (no flush)",
                        "launch": "one CUDA graph per step",
-                       "algorithmic_bytes_per_step": total_bytes},
+                       "algorithmic_bytes_per_step": total_bytes,
+                       **({"algorithmic_bytes_per_weight": {
+                           "packed_path (value)": total_bytes / W.n_total,
+                           "api_int64_codes": 20.0 + 4.0 / 64}} if W.name == "nf4" else {})},
             "roofline": roofline,
             "kernels": kernels,
             "cpu_baseline": cpu,
@@ -1250,6 +1374,8 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="nf4")
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="default line: skip the other workloads' kernel timings")
     ap.add_argument("--profile", action="store_true",
                     help="only run a small case of the workload's dominant kernel (for ncu)")
     args = ap.parse_args()

@@ -11,6 +11,22 @@ from .quantizer import (
 )
 from .rotation import (
     hadamard_matrix,
+    random_hadamard_matrix,
+    random_orthogonal,
+    cayley_transform,
+    CayleyRotation,
+    rotate_weight_right,
+    rotate_weight_left,
+    apply_rotation_to_linear,
     fast_hadamard_transform,
     hadamard_fake_quantize,
+)
+from .utils import (
+    MinMaxObserver,
+    ActivationCollector,
+    quantization_mse,
+    quantization_snr,
+    kurtosis,
+    make_dummy_linear,
+    make_calibration_data,
 )

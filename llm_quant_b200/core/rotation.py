@@ -74,3 +74,96 @@ def hadamard_fake_quantize(x: torch.Tensor, n_bits: int = 4, symmetric: bool = T
     Not part of the reference's API (it has no fused op); values equal the
     two-call composition applied to this module's transform."""
     return _fht(x, n_bits, symmetric, return_qparams)
+
+
+# ──────────────────────────────────────────────────────────────────────────────
+# Rotation construction and weight-rotation helpers (core/rotation.py:46-207).
+# One-off weight preparation for QuaRot / SpinQuant / FlatQuant, off the
+# data-parallel hot path: plain eager PyTorch on the inputs' device (CPU
+# included), with the reference's names, signatures, defaults and results.
+# ──────────────────────────────────────────────────────────────────────────────
+
+def _gen_device(generator):
+    return None if generator is None else generator.device
+
+
+def random_hadamard_matrix(n: int, dtype: torch.dtype = torch.float32,
+                           generator: torch.Generator | None = None) -> torch.Tensor:
+    """``hadamard_matrix(n) @ diag(s)`` with s_j = +-1 drawn by
+    ``torch.randint(0, 2, (n,))`` from ``generator`` (core/rotation.py:46-55):
+    column j of the normalised Sylvester matrix is negated when its draw is 0.
+    The draw runs on the generator's device, so a seeded CPU generator gives
+    the reference's signs wherever the matrix is placed."""
+    H = hadamard_matrix(n, dtype)
+    draw = torch.randint(0, 2, (n,), generator=generator, dtype=dtype,
+                         device=_gen_device(generator))
+    return H * (draw.to(H.device) * 2 - 1)
+
+
+def random_orthogonal(n: int, dtype: torch.dtype = torch.float32,
+                      generator: torch.Generator | None = None) -> torch.Tensor:
+    """Haar-distributed orthogonal matrix (core/rotation.py:58-66): the Q of
+    a QR factorisation of an n x n standard normal matrix, its columns
+    signed so that R's diagonal would be non-negative (a zero diagonal entry
+    keeps its column)."""
+    g = torch.randn(n, n, dtype=dtype, generator=generator, device=_gen_device(generator))
+    q, r = torch.linalg.qr(g)
+    sign = torch.diagonal(r).sign()
+    sign = torch.where(sign == 0, torch.ones_like(sign), sign)
+    return q * sign
+
+
+def cayley_transform(A: torch.Tensor) -> torch.Tensor:
+    """Orthogonal ``(I + A)^-1 (I - A)`` of a skew-symmetric A
+    (core/rotation.py:73-81), by one linear solve; the two factors commute
+    because both are polynomials in A."""
+    eye = torch.eye(A.shape[0], dtype=A.dtype, device=A.device)
+    return torch.linalg.solve(eye + A, eye - A)
+
+
+class CayleyRotation(torch.nn.Module):
+    """Learnable rotation Q = cayley_transform(A) (core/rotation.py:84-123).
+
+    The free parameters ``params`` (dim (dim - 1) / 2 of them, zero at
+    construction, so Q starts at the identity for either ``init``) fill the
+    strict upper triangle of A row by row; A = U - U^T is skew-symmetric and
+    Q is orthogonal for every value of the parameters."""
+
+    def __init__(self, dim: int, init: str = "identity"):
+        super().__init__()
+        self.dim = dim
+        self.init = init
+        self.params = torch.nn.Parameter(torch.zeros(dim * (dim - 1) // 2))
+
+    def _build_skew(self) -> torch.Tensor:
+        rows, cols = torch.triu_indices(self.dim, self.dim, offset=1, device=self.params.device)
+        upper = torch.zeros(self.dim, self.dim, dtype=self.params.dtype, device=self.params.device)
+        upper = upper.index_put((rows, cols), self.params)
+        return upper - upper.t()
+
+    def forward(self) -> torch.Tensor:
+        return cayley_transform(self._build_skew())
+
+    def extra_repr(self) -> str:
+        return f"dim={self.dim}"
+
+
+def rotate_weight_right(weight: torch.Tensor, R: torch.Tensor) -> torch.Tensor:
+    """``weight @ R``: the rotation absorbed into the input dimension."""
+    return torch.matmul(weight, R)
+
+
+def rotate_weight_left(weight: torch.Tensor, R: torch.Tensor) -> torch.Tensor:
+    """``R^T @ weight``: the rotation absorbed into the output dimension."""
+    return torch.matmul(R.t(), weight)
+
+
+@torch.no_grad()
+def apply_rotation_to_linear(linear: torch.nn.Linear, R: torch.Tensor, side: str = "right") -> None:
+    """Replace ``linear.weight.data`` by its rotation (core/rotation.py:189-207):
+    ``side='right'`` W R, ``side='left'`` R^T W; any other side raises
+    ``ValueError``."""
+    rotate = {"right": rotate_weight_right, "left": rotate_weight_left}.get(side)
+    if rotate is None:
+        raise ValueError(f"side must be 'right' or 'left', got {side!r}")
+    linear.weight.data = rotate(linear.weight.data, R)

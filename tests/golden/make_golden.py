@@ -1,9 +1,10 @@
 """Generate golden input/output vectors by running the reference llm_quant itself.
 
-Run in a container that has the reference source tree (read-only) at
-/root/reference:
+Run where the reference source tree (read-only) is available:
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py [--ref DIR] [quantizer rotation ...]
+
+DIR defaults to $LQ_REFERENCE_SRC, else /root/reference.
 
 The reference is pure PyTorch with relative imports; it is made importable as
 ``llm_quant`` through a symlink in a temporary directory (its files are never
@@ -26,7 +27,7 @@ import tempfile
 import numpy as np
 import torch
 
-REF_SRC = "/root/reference"
+REF_SRC = os.environ.get("LQ_REFERENCE_SRC", "/root/reference")
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
@@ -486,9 +487,62 @@ def gen_layers(ref):
     st.save("layers.npz")
 
 
+def gen_helpers(ref):
+    """The reference's rotation-construction helpers and core.utils (off the
+    hot path; eager torch on the CPU in both packages)."""
+    from llm_quant.core import rotation as R
+    from llm_quant.core import utils as U
+    st = Store()
+    for n, dtn, seed in [(16, "float32", 123), (64, "float32", 7), (32, "bfloat16", 8)]:
+        st.add(f"rhad_{n}_{dtn}", dict(fn="random_hadamard_matrix", n=n, dtype=dtn, seed=seed),
+               H=R.random_hadamard_matrix(n, DT[dtn], generator=torch.Generator().manual_seed(seed)))
+    for n, seed in [(8, 1), (32, 2)]:
+        st.add(f"rorth_{n}", dict(fn="random_orthogonal", n=n, seed=seed),
+               Q=R.random_orthogonal(n, generator=torch.Generator().manual_seed(seed)))
+    g = torch.Generator().manual_seed(11)
+    a = torch.randn(12, 12, generator=g)
+    a = a - a.t()
+    st.add("cayley", dict(fn="cayley_transform"), A=a, Q=R.cayley_transform(a))
+    cr = R.CayleyRotation(6)
+    with torch.no_grad():
+        cr.params.copy_(torch.randn(cr.params.shape, generator=g) * 0.3)
+    st.add("cayley_rot", dict(fn="CayleyRotation", dim=6), p=cr.params.data, Q=cr().detach())
+    w = torch.randn(6, 10, generator=g)
+    r10 = R.random_orthogonal(10, generator=torch.Generator().manual_seed(3))
+    r6 = R.random_orthogonal(6, generator=torch.Generator().manual_seed(4))
+    st.add("rotate", dict(fn="rotate_weight"), W=w, R10=r10, R6=r6,
+           right=R.rotate_weight_right(w, r10), left=R.rotate_weight_left(w, r6))
+    batches = [torch.randn(3, 5, 4, generator=g) * (i + 1) for i in range(3)]
+    obs = {}
+    for key, kw in [("tensor", dict()), ("ch_last", dict(per_channel=True, channel_dim=-1)),
+                    ("ch0", dict(per_channel=True, channel_dim=0)),
+                    ("ch1", dict(per_channel=True, channel_dim=1))]:
+        o = U.MinMaxObserver(**kw)
+        for b in batches:
+            o.update(b)
+        obs[f"{key}_min"], obs[f"{key}_max"] = o.get_range()
+    st.add("observer", dict(fn="MinMaxObserver"), b0=batches[0], b1=batches[1], b2=batches[2], **obs)
+    x = torch.randn(64, 8, generator=g)
+    y = x + torch.randn(64, 8, generator=g) * 0.05
+    st.add("metrics", dict(fn="metrics"), x=x, y=y, mse=U.quantization_mse(x, y),
+           snr=U.quantization_snr(x, y), kurt0=U.kurtosis(x, dim=0), kurt1=U.kurtosis(x))
+    lin = U.make_dummy_linear(64, 32)
+    lin_nb = U.make_dummy_linear(16, 8, bias=False)
+    st.add("dummy_linear", dict(fn="make_dummy_linear"), w=lin.weight.data, b=lin.bias.data,
+           w_nb=lin_nb.weight.data)
+    cal = U.make_calibration_data(2, 4, 8, 3, seed=5)
+    st.add("calib", dict(fn="make_calibration_data"), d0=cal[0], d1=cal[1], d2=cal[2])
+    st.save("helpers.npz")
+
+
 if __name__ == "__main__":
     torch.set_num_threads(max(1, os.cpu_count() or 1))
+    args = sys.argv[1:]
+    if "--ref" in args:
+        i = args.index("--ref")
+        REF_SRC = args[i + 1]
+        del args[i:i + 2]
     ref = _import_reference()
-    which = sys.argv[1:] or ["quantizer", "rotation", "nf4", "kv", "grad", "layers"]
+    which = args or ["quantizer", "rotation", "nf4", "kv", "grad", "layers", "helpers"]
     for name in which:
         globals()[f"gen_{name}"](ref)
