@@ -6,8 +6,9 @@
  *   - Every pointer is a device pointer (or a host pointer where named
  *     "host_"), every size is in elements unless the name says bytes.
  *   - The caller allocates every output and every workspace; the library
- *     never allocates device memory and keeps no mutable global state, so it
- *     is re-entrant.
+ *     never allocates device memory.  Its only mutable global state is the
+ *     launch counter (lq_launch_count, atomic) and the fixed scratch array of
+ *     lq_tensor_qparams_noalloc; every other entry point is re-entrant.
  *   - All work is enqueued on `stream` (a cudaStream_t, NULL = legacy default
  *     stream); no call synchronizes the host.
  *   - Every entry point returns an lq_status (0 = success).  On failure
@@ -190,7 +191,9 @@ int lq_tensor_qparams(const void* x, int x_dtype, int64_t n, int n_bits, int sym
  * which limits n to 64 Mi elements (larger n: LQ_ERANGE).  All calls share
  * that array: calls whose kernels overlap on the GPU race.  The first call on
  * a device looks up the array's address (cudaGetSymbolAddress), so make it
- * before any stream capture.  Allocates nothing. */
+ * before any stream capture.  The address is kept for the life of the
+ * process: after a cudaDeviceReset of that device the array may move, so do
+ * not call this entry point again in that process.  Allocates nothing. */
 int lq_tensor_qparams_noalloc(const void* x, int x_dtype, int64_t n, int n_bits, int symmetric,
                               void* scale, void* zero_point, void* stream);
 

@@ -329,6 +329,49 @@ def int_weight_fp32(m, what: str) -> torch.Tensor:
     return out
 
 
+def bind_int_qparams(m, scale: torch.Tensor, zp: torch.Tensor) -> None:
+    """Store [out, n_groups] qparams on an int-weight layer.  The layer's
+    buffers are replaced when the shape changes (its constructor makes them
+    [out, 1]; the reference rebinds them then, so state_dicts carry the
+    grouped shape) and copied into otherwise.  Drops the packed W4A16
+    operand."""
+    if scale.shape != m.scale.shape:
+        m.scale, m.zero_point = scale, zp
+    else:
+        m.scale.copy_(scale)
+        m.zero_point.copy_(zp)
+    m._w4 = None
+
+
+def row_group_quantize(m, weight: torch.Tensor, symmetric: bool, what: str,
+                       codes: bool = True) -> None:
+    """One pass of lq_group_quant over a 2-D weight [out, in]: qparams of
+    every group of ``m.group_size`` columns (the last group zero-padded; one
+    group per row when group_size <= 0) and, with ``codes``, the int8 codes
+    written straight into ``m.weight_int``.  Values equal compute_qparams
+    PER_GROUP / PER_CHANNEL followed by quantize_tensor on the padded groups
+    (core/quantizer.py:231-260)."""
+    _C.require_cuda(weight, what=what)
+    _C.require_float(weight, what)
+    _C.check_clamp_bounds(weight.dtype, m.n_bits, symmetric)
+    w = weight.detach().contiguous()
+    N, K = w.shape
+    G = m.group_size if m.group_size > 0 else K
+    scale = torch.empty(N, math.ceil(K / G), dtype=w.dtype, device=w.device)
+    zp = torch.empty_like(scale)
+    out = None
+    if codes:
+        direct = (m.weight_int.device == w.device and m.weight_int.is_contiguous()
+                  and m.weight_int.shape == (N, K))
+        out = m.weight_int if direct else torch.empty(N, K, dtype=torch.int8, device=w.device)
+    _C.call("lq_group_quant", w.data_ptr(), _C.dt(w), N, K, G, m.n_bits, int(symmetric),
+            _C.MODE_CODES if codes else _C.MODE_QPARAMS, _C.ptr(out), _C.I8, scale.data_ptr(),
+            zp.data_ptr(), _C.stream_ptr(w))
+    if codes and out is not m.weight_int:
+        m.weight_int.copy_(out.reshape_as(m.weight_int))
+    bind_int_qparams(m, scale, zp)
+
+
 def int_linear_forward(m, x: torch.Tensor) -> torch.Tensor:
     """Forward of an int-weight linear: the fused W4A16 kernel for fp16 / bf16
     activations when the layout allows it, else the reference's fp32
@@ -382,29 +425,7 @@ class QuantizedLinear(nn.Module):
     def quantize_weights(self, weight: torch.Tensor) -> None:
         """Quantize a float weight and store INT codes + scale / zero point
         (core/quantizer.py:231-260), one fused pass over the weight."""
-        _C.require_cuda(weight, what="QuantizedLinear.quantize_weights")
-        _C.require_float(weight, "QuantizedLinear.quantize_weights")
-        w = weight.detach().contiguous()
-        N, K = w.shape
-        G = self.group_size if self.group_size > 0 else K
-        ng = math.ceil(K / G)
-        direct = (self.weight_int.device == w.device and self.weight_int.is_contiguous()
-                  and self.weight_int.shape == (N, K))
-        codes = self.weight_int if direct else torch.empty(N, K, dtype=torch.int8, device=w.device)
-        scale = torch.empty(N, ng, dtype=w.dtype, device=w.device)
-        zp = torch.empty_like(scale)
-        _C.call("lq_group_quant", w.data_ptr(), _C.dt(w), N, K, G, self.n_bits,
-                int(self.symmetric), _C.MODE_CODES, codes.data_ptr(), _C.I8, scale.data_ptr(),
-                zp.data_ptr(), _C.stream_ptr(w))
-        if not direct:
-            self.weight_int.copy_(codes.reshape_as(self.weight_int))
-        if scale.shape != self.scale.shape:
-            self.scale = scale
-            self.zero_point = zp
-        else:
-            self.scale.copy_(scale)
-            self.zero_point.copy_(zp)
-        self._w4 = None
+        row_group_quantize(self, weight, self.symmetric, "QuantizedLinear.quantize_weights")
 
     def _load_from_state_dict(self, *args, **kwargs):
         self._w4 = None

@@ -383,7 +383,9 @@ extern "C" int lq_ste_round(const void* x, int dtype, int64_t n, void* out, void
 //     partial it later reads, so nothing has to be cleared between calls;
 //   * the first call on a device looks up the array's device address with
 //     cudaGetSymbolAddress (once per device, with that device current), so
-//     make that first call before any stream capture;
+//     make that first call before any stream capture.  The address is cached
+//     for the life of the process; a cudaDeviceReset of the device may move
+//     the array, so the entry point must not be called after one;
 //   * the call allocates nothing: no cudaMalloc, no cudaFree, no library
 //     routine that allocates.
 // ---------------------------------------------------------------------------

@@ -16,6 +16,20 @@ constexpr uint64_t kWaitNs = 2000000000ull;  // bounded waits give up after 2 s
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
+// Shared-window loads by 32-bit address.  A pointer into the dynamic area
+// that was aligned through an integer is generic to the compiler, and a
+// generic load costs 64-bit address arithmetic and the long scoreboard; these
+// compile to plain shared loads.  volatile keeps them after the barrier waits.
+__device__ __forceinline__ uint32_t lds_b32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint4 lds_v4(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
 __device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count));
 }

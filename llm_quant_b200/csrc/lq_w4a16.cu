@@ -363,6 +363,7 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
     const int h = wi >> 2;           // half of each 64-wide K half (A slot columns 16h..16h+15)
     const int row = q * 32 + lane;   // weight row within the tile
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+    const uint32_t sbase = smem_u32(smem);
     bool ok = true;
     for (int i = grp; i < n_steps && ok; i += kDG) {
       const int s = i % S;
@@ -373,8 +374,8 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
 #pragma unroll
       for (int hk = 0; hk < WK; ++hk) {
         // this warp's half of the row's codes: words 4h..4h+3 (k = 32h..32h+31)
-        const uint4 cw = reinterpret_cast<const uint4*>(smem + L::off_w + (sw * WK + hk) * kWStage + row * 32)[h];
-        const uint32_t zs = *reinterpret_cast<const uint32_t*>(smem + L::off_s + (sw * WK + hk) * kSStage + row * 4);
+        const uint4 cw = lds_v4(sbase + L::off_w + (sw * WK + hk) * kWStage + row * 32 + 16 * h);
+        const uint32_t zs = lds_b32(sbase + L::off_s + (sw * WK + hk) * kSStage + row * 4);
         // zs = (zero_b, scale) as a T pair; broadcast each half to both halves
         const uint32_t zb = __byte_perm(zs, zs, 0x1010);
         const uint32_t sc = __byte_perm(zs, zs, 0x3232);
@@ -382,11 +383,11 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
         uint32_t r[16];
         if constexpr (NF) {
           // byte c = k pair (2c, 2c+1) -> table pair * scale = round_T(NF4 * scale)
-          const char* lb = reinterpret_cast<const char*>(smem + L::off_lut);
+          const uint32_t lb = sbase + L::off_lut;
           const uint32_t l4 = (uint32_t)lane << 2;
 #pragma unroll
           for (int c = 0; c < 16; ++c) {
-            const uint32_t pv = *reinterpret_cast<const uint32_t*>(lb + pair_lut_off(w[c >> 2], c & 3, l4));
+            const uint32_t pv = lds_b32(lb + pair_lut_off(w[c >> 2], c & 3, l4));
             r[c] = Act<T>::mul2(pv, sc);
           }
         } else {

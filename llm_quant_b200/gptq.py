@@ -18,7 +18,7 @@ from __future__ import annotations
 import torch
 import torch.nn as nn
 
-from .core.quantizer import QScheme, compute_qparams, int_linear_forward, int_weight_fp32
+from .core.quantizer import int_linear_forward, int_weight_fp32, row_group_quantize
 
 
 class GPTQLinear(nn.Module):
@@ -51,19 +51,12 @@ class GPTQLinear(nn.Module):
 
     @torch.no_grad()
     def pack(self, w_q: torch.Tensor, weight_orig: torch.Tensor) -> None:
-        """Store the GPTQ codes and the qparams of the original weight (gptq.py:285-299)."""
-        scheme = QScheme.PER_GROUP if self.group_size > 0 else QScheme.PER_CHANNEL
-        scale, zp = compute_qparams(weight_orig, self.n_bits, self.symmetric, scheme, self.group_size)
+        """Keep GPTQ's integer codes ``w_q`` as int8 and take the scale / zero
+        point from the weight they were solved for (gptq.py:285-299): one
+        qparams-only pass of the row-group kernel over ``weight_orig``, groups
+        of ``group_size`` columns (one per row when group_size <= 0)."""
+        row_group_quantize(self, weight_orig, self.symmetric, "GPTQLinear.pack", codes=False)
         self.weight_int.copy_(w_q.to(torch.int8).reshape_as(self.weight_int))
-        scale_flat = scale.reshape(self.out_features, -1)
-        zp_flat = zp.reshape(self.out_features, -1)
-        if scale_flat.shape != self.scale.shape:
-            self.scale = scale_flat.clone()
-            self.zero_point = zp_flat.clone()
-        else:
-            self.scale.copy_(scale_flat)
-            self.zero_point.copy_(zp_flat)
-        self._w4 = None
 
     def _load_from_state_dict(self, state_dict, prefix, *args, **kwargs):
         self._w4 = None

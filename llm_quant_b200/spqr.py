@@ -19,14 +19,12 @@ the mask, the values or the int weight change.
 
 from __future__ import annotations
 
-import math
-
 import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
 from . import _C
-from .core.quantizer import (QScheme, compute_qparams, int_weight_fp32, quantize_tensor)
+from .core.quantizer import int_weight_fp32, row_group_quantize
 
 
 class SpQRLinear(nn.Module):
@@ -56,35 +54,16 @@ class SpQRLinear(nn.Module):
 
     @torch.no_grad()
     def pack(self, weight: torch.Tensor, outlier_mask: torch.Tensor) -> None:
-        """Int part of the weight with the outliers zeroed, plus the outliers
-        in fp (spqr.py:128-170)."""
+        """Split the weight into fp outliers and a symmetric int part
+        (spqr.py:128-170).  ``outlier_vals`` takes the masked weights in
+        row-major mask order; the int part is the weight with those positions
+        set to zero, quantized (qparams and int8 codes) by one pass of the
+        row-group kernel."""
         self.outlier_mask.copy_(outlier_mask)
         self.outlier_vals = weight[outlier_mask].clone()
-        w_for_quant = weight.clone()
-        w_for_quant[outlier_mask] = 0.0
-
-        scheme = QScheme.PER_GROUP if self.group_size > 0 else QScheme.PER_CHANNEL
-        scale, zp = compute_qparams(w_for_quant, self.n_bits, True, scheme, self.group_size)
-        if scheme == QScheme.PER_GROUP:
-            out_f, in_f = w_for_quant.shape
-            n_groups = math.ceil(in_f / self.group_size)
-            padded = in_f % self.group_size
-            w_pad = F.pad(w_for_quant, (0, self.group_size - padded)) if padded else w_for_quant
-            q = quantize_tensor(w_pad.reshape(out_f, n_groups, self.group_size), scale, zp, self.n_bits, True)
-            q = q.reshape(out_f, -1)[:, :in_f]
-        else:
-            q = quantize_tensor(w_for_quant, scale, zp, self.n_bits, True)
-
-        self.weight_int.copy_(q.to(torch.int8).reshape_as(self.weight_int))
-        scale_flat = scale.reshape(self.out_features, -1)
-        zp_flat = zp.reshape(self.out_features, -1)
-        if scale_flat.shape != self.scale.shape:
-            self.scale = scale_flat.clone()
-            self.zero_point = zp_flat.clone()
-        else:
-            self.scale.copy_(scale_flat)
-            self.zero_point.copy_(zp_flat)
-        self._w4 = None
+        inliers = torch.where(outlier_mask, torch.zeros((), dtype=weight.dtype, device=weight.device),
+                              weight)
+        row_group_quantize(self, inliers, True, "SpQRLinear.pack")
         self._csr = None
 
     def _load_from_state_dict(self, state_dict, prefix, *args, **kwargs):
