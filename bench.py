@@ -419,10 +419,12 @@ class NF4Workload:
         self.ctx.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        gather_to_rank0(flat)
+        got = gather_to_rank0(flat)
         e1.record()
         torch.cuda.synchronize()
-        return e0.elapsed_time(e1), flat.numel()
+        # bytes that crossed NVLink into rank 0 (its own buffer stays put)
+        received = sum(b.numel() for b in got[1:]) if got is not None else 0
+        return e0.elapsed_time(e1), received
 
     @staticmethod
     def cpu_baseline():
@@ -1358,7 +1360,11 @@ def run_ours(args):
             "e2e": e2e,
             "gpu_launches": launches_all,
             "clocks": ck,
-            "gather": {"ms": gather_ms, "bytes_rank0": gather_bytes} if ctx.world > 1 else None,
+            # one whole-model job = one step + the final gather of its
+            # packed results to rank 0 (exact sizes, point to point)
+            "gather": {"ms": gather_ms, "bytes_to_rank0": gather_bytes,
+                       "value_with_gather": total_bytes / ((ms + gather_ms) * 1e-3) / scale}
+            if ctx.world > 1 and gather_bytes else None,
         }
         print(json.dumps(line))
     ctx.close()

@@ -66,6 +66,14 @@ const char* lq_status_string(int status);
 int lq_version(void);
 /* Number of kernels this library has enqueued from this process (all threads). */
 uint64_t lq_launch_count(void);
+/* Failure detection (the reference has no device code; its counterpart is the
+ * bounded-wait requirement on every device-side spin-wait): probe of the
+ * bounded mbarrier wait that the pipelined kernels use.  One warp waits on an
+ * mbarrier that gets its arrival (arrive != 0) or never does, for at most
+ * limit_ns (<= 10 s).  Writes out[0] = LQ_OK (the phase completed) or
+ * LQ_ETIMEOUT (the wait gave up), out[1] = the wait's duration in ns
+ * (out: 2 device int64).  The context stays usable after a timeout. */
+int lq_wait_probe(int64_t limit_ns, int arrive, int64_t* out, void* stream);
 
 /* ---- group / row quantization ---------------------------------------------
  * x is [rows, cols] row-major.  Each row is cut into ceil(cols/group)

@@ -56,14 +56,18 @@ __device__ __forceinline__ uint64_t global_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-// Bounded wait; false once kWaitNs of wall time has passed.
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity) {
+// Bounded wait; false once limit_ns of wall time has passed.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* b, uint32_t parity, uint64_t limit_ns) {
   if (mbar_try(b, parity)) return true;
   const uint64_t t0 = global_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try(b, parity)) return true;
-    if ((i & 255) == 0 && global_ns() - t0 > kWaitNs) return false;
+    if ((i & 255) == 0 && global_ns() - t0 > limit_ns) return false;
   }
+}
+// The kernels' waits: bounded by kWaitNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity) {
+  return mbar_wait_for(b, parity, kWaitNs);
 }
 // Warp-uniform bounded wait (every lane polls; all agree on the outcome).
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* b, uint32_t parity) {

@@ -4,8 +4,8 @@ Whole-model weight quantization and KV-cache quantization are independent per
 layer, so N ranks (one process per GPU, torch.distributed over NCCL) each
 take a contiguous block of layers and run the quantization kernels with no
 data-path collective.  The only exchange is the final gather of each rank's
-packed results (4-bit codes + scales) to rank 0 over NVLink, done as one
-flat byte buffer per rank so it is a single NCCL collective.
+packed results (4-bit codes + scales) to rank 0 over NVLink: one flat byte
+buffer per rank, sent point to point at its exact size.
 """
 
 from __future__ import annotations
@@ -67,10 +67,13 @@ def unflatten_bytes(buf: torch.Tensor, like: Sequence[torch.Tensor]) -> List[tor
 
 
 def gather_to_rank0(local: torch.Tensor, group=None) -> List[torch.Tensor] | None:
-    """Gather each rank's flat uint8 buffer to rank 0 (sizes may differ).
+    """Gather each rank's flat uint8 buffer to rank 0, exact sizes.
 
-    One all_gather of the sizes, then one gather of buffers padded to the
-    largest size.  Returns the per-rank buffers on rank 0, None elsewhere."""
+    One all_gather of the sizes; then every other rank sends its buffer to
+    rank 0 point to point, all transfers posted together (batch_isend_irecv)
+    so they overlap on rank 0's links.  Nothing is padded: a rank with fewer
+    layers sends fewer bytes.  Returns the per-rank buffers on rank 0 (its
+    own is `local` itself), None elsewhere."""
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     dev = local.device
@@ -78,15 +81,20 @@ def gather_to_rank0(local: torch.Tensor, group=None) -> List[torch.Tensor] | Non
     sizes = [torch.zeros_like(n) for _ in range(world)]
     dist.all_gather(sizes, n, group=group)
     sizes = [int(s.item()) for s in sizes]
-    mx = max(sizes)
-    padded = torch.zeros(mx, dtype=torch.uint8, device=dev)
-    padded[:local.numel()].copy_(local)
+
+    def peer(r: int) -> int:
+        return r if group is None else dist.get_global_rank(group, r)
+
     if rank == 0:
-        bufs = [torch.empty(mx, dtype=torch.uint8, device=dev) for _ in range(world)]
-        dist.gather(padded, bufs, dst=0, group=group)
-        return [b[:s] for b, s in zip(bufs, sizes)]
-    dist.gather(padded, None, dst=0, group=group)
-    return None
+        bufs = [local] + [torch.empty(sz, dtype=torch.uint8, device=dev) for sz in sizes[1:]]
+        ops = [dist.P2POp(dist.irecv, bufs[r], peer(r), group) for r in range(1, world) if sizes[r]]
+    else:
+        bufs = None
+        ops = [dist.P2POp(dist.isend, local.contiguous(), peer(0), group)] if sizes[rank] else []
+    if ops:
+        for req in dist.batch_isend_irecv(ops):
+            req.wait()
+    return bufs
 
 
 def quantize_layers(num_layers: int, rank: int, world: int,

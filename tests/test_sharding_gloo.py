@@ -126,3 +126,11 @@ def test_rank_failure_is_reported_not_hung():
     assert any(m[1] == 1 and "injected" in m[2] for m in errs)
     # rank 0 leaves with an error from the collective (peer gone / timeout)
     assert all(c == 0 for c in codes)
+
+
+def test_gather_world3_uneven_exact_sizes():
+    """7 layers over 3 ranks (3, 2, 2 layers): every rank's bytes arrive at
+    their own size, nothing padded to the largest rank."""
+    msgs, codes = _run(3, 7)
+    assert ("ok", True) in msgs, msgs
+    assert codes == [0, 0, 0]
