@@ -320,6 +320,26 @@ int lq_w4a16_linear(const void* x, int act_dtype, int64_t M, int64_t N, int64_t 
  * scale), x / y in act_dtype (LQ_F16 or LQ_BF16), bias fp32 [N] or NULL, fp32
  * accumulation; err as for lq_w4a16_linear. */
 size_t lq_nf4_linear_packed_bytes(int64_t N, int64_t K);
+/* lq_nf4_linear_lora: QLoRALinear.forward whole (qlora.py:306-312): y =
+ * x @ W^T + bias + u @ lora_b^T, the LoRA term in the same kernel (the
+ * tensor-core path runs it as one more K step with lora_B's rows as the A
+ * operand, the weight-streaming path adds it per output).  u = scaling *
+ * x @ lora_A^T [M, 64] in act_dtype (columns rank..63 zero), lora_b [N, rank]
+ * in act_dtype; rank even, <= 16 for M > 16 and <= 64 for M <= 16. */
+int lq_nf4_linear_lora(const void* x, int act_dtype, int64_t M, int64_t N, int64_t K,
+                       const void* packed, const float* bias, const void* lora_u,
+                       const void* lora_b, int64_t rank, void* y, int* err, void* stream);
+/* lq_nf4_merge_lora: QLoRALinear.merge_lora (qlora.py:314-317) in one pass:
+ * out [N, K] = W_base + scaling * lora_b @ lora_a with W_base exactly
+ * _dequantize_base's (scales / double-quantized scales as in lq_nf4_unpack,
+ * s_dtype), lora_a [rank, K] and lora_b [N, rank] in p_dtype, each op rounded
+ * as torch rounds it; out_dtype = promote(s_dtype, p_dtype).  K % 8 == 0,
+ * 1 <= rank <= 64. */
+int lq_nf4_merge_lora(const uint8_t* packed_codes, int64_t N, int64_t K, int64_t group,
+                      int64_t dq_group, const void* scales, const void* q_scales,
+                      const void* dq_scales, int s_dtype, const void* lora_a,
+                      const void* lora_b, int p_dtype, int64_t rank, float scaling, void* out,
+                      int out_dtype, void* stream);
 int lq_nf4_linear_pack(const void* codes, const void* scales, const void* q_scales,
                        const void* dq_scales, int s_dtype, int64_t N, int64_t K, int64_t group,
                        int64_t dq_group, int act_dtype, void* packed, void* stream);

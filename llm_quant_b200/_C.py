@@ -67,6 +67,9 @@ _SIGS = {
     "lq_w4a16_linear": [_V, _I, _L, _L, _L, _L, _V, _V, _V, _V, _V],
     "lq_nf4_linear_pack": [_V, _V, _V, _V, _I, _L, _L, _L, _L, _I, _V, _V],
     "lq_nf4_linear": [_V, _I, _L, _L, _L, _V, _V, _V, _V, _V],
+    "lq_nf4_linear_lora": [_V, _I, _L, _L, _L, _V, _V, _V, _V, _L, _V, _V, _V],
+    "lq_nf4_merge_lora": [_V, _L, _L, _L, _L, _V, _V, _V, _I, _V, _V, _I, _L, ctypes.c_float,
+                          _V, _I, _V],
     "lq_sparse_row_add": [_V, _I, _L, _L, _L, _V, _V, _L, _V, _V, _V, _V],
     "lq_wait_probe": [_L, _I, _V, _V],
     "lq_kv_attention": [_V, _I, _L, _L, _L, _L, _L, _L, _L, _I,

@@ -1130,3 +1130,146 @@ extern "C" int lq_codes_convert(const void* src, int src_dtype, int64_t n, void*
   codes_convert_kernel<<<grid_cap(((n + 1) / 2 + 255) / 256, 16), 256, 0, as_stream(stream)>>>(src, src_dtype, n, dst, dst_dtype);
   return launched("codes_convert_kernel");
 }
+
+// ---------------------------------------------------------------------------
+// QLoRALinear.merge_lora (qlora.py:314-317) in one pass:
+//   out[n, k] = W_base[n, k] + scaling * (lora_B @ lora_A)[n, k]
+// W_base is _dequantize_base's weight, bit for bit (NF4 table value rounded
+// to the scales' dtype S times the block's scale, restored through double
+// dequantization when q_scales is given); each torch op's rounding is kept:
+// t = sum_j B[n, j] A[j, k] (fp32 accumulation, rounded to the LoRA dtype P),
+// t = round_P(scaling * t), out = round_O(W + t) with O = promote(S, P).  The
+// rank-r product is the only arithmetic that differs from the reference's
+// (its summation order is BLAS's).
+// Tile of a block: 32 rows x 128 columns; thread = 2 rows x 8 columns, the
+// tile's lora_A columns (r x 128) and lora_B rows (32 x r) in shared memory
+// as fp32.  HBM-bound: 0.5 byte of codes in, sizeof(O) out per element.
+// ---------------------------------------------------------------------------
+namespace lq {
+namespace {
+
+constexpr int kMrRows = 32, kMrCols = 128, kMrMaxRank = 64;
+
+template <typename S, typename P, typename O>
+__global__ void __launch_bounds__(256) nf4_merge_lora_kernel(
+    const uint8_t* __restrict__ codes, const S* __restrict__ scales, const S* __restrict__ q_scales,
+    const S* __restrict__ dq_scales, int64_t group, int64_t dq_group, const P* __restrict__ lora_a,
+    const P* __restrict__ lora_b, int r, float scaling, int N, int K, O* __restrict__ out) {
+  __shared__ float sa[kMrMaxRank][kMrCols];   // lora_A[j, k0 + c]
+  __shared__ float sb[kMrRows][kMrMaxRank];   // lora_B[n0 + i, j]
+  __shared__ float tab[16];
+  const int n0 = blockIdx.y * kMrRows, k0 = blockIdx.x * kMrCols;
+  if (threadIdx.x < 16) tab[threadIdx.x] = Ty<S>::round(kNF4[threadIdx.x]);
+  for (int i = threadIdx.x; i < r * kMrCols; i += blockDim.x) {
+    const int j = i / kMrCols, c = i % kMrCols;
+    sa[j][c] = (k0 + c < K) ? Ty<P>::to_f(lora_a[(int64_t)j * K + k0 + c]) : 0.0f;
+  }
+  for (int i = threadIdx.x; i < kMrRows * r; i += blockDim.x) {
+    const int rr = i / r, j = i % r;
+    sb[rr][j] = (n0 + rr < N) ? Ty<P>::to_f(lora_b[(int64_t)(n0 + rr) * r + j]) : 0.0f;
+  }
+  __syncthreads();
+  const int cl = (threadIdx.x & 15) * 8;  // first of the thread's 8 columns in the tile
+  const int rl = (threadIdx.x >> 4) * 2;  // first of its 2 rows
+  if (k0 + cl >= K) return;
+  float acc[2][8];
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+#pragma unroll
+    for (int c = 0; c < 8; ++c) acc[i][c] = 0.0f;
+  for (int j = 0; j < r; ++j) {
+    float av[8], bv[2];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) av[c] = sa[j][cl + c];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) bv[i] = sb[rl + i][j];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+      for (int c = 0; c < 8; ++c) acc[i][c] = fmaf(bv[i], av[c], acc[i][c]);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int n = n0 + rl + i;
+    if (n >= N) break;
+    const int64_t e0 = (int64_t)n * K + k0 + cl;  // 8 consecutive flat elements (K % 8 == 0)
+    const uint32_t cw = *reinterpret_cast<const uint32_t*>(codes + e0 / 2);
+    int64_t glast = -1;
+    float s = 0.0f;
+    float o[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const int64_t g = (e0 + c) / group;
+      if (g != glast) {
+        glast = g;
+        s = q_scales ? tmul<S>(tdiv<S>(Ty<S>::to_f(q_scales[g]), 127.0f), Ty<S>::to_f(dq_scales[g / dq_group]))
+                     : Ty<S>::to_f(scales[g]);
+      }
+      const float w = tmul<S>(tab[(cw >> (4 * c)) & 15], s);
+      const float t = tmul<P>(scaling, Ty<P>::round(acc[i][c]));
+      o[c] = tadd<O>(w, t);
+    }
+#pragma unroll
+    for (int c = 0; c < 8; ++c) out[e0 + c] = Ty<O>::from_f(o[c]);
+  }
+}
+
+template <typename S, typename P>
+int merge_lora_sp(const uint8_t* codes, const void* s, const void* qs, const void* dqs, int64_t group,
+                  int64_t dq_group, const void* la, const void* lb, int r, float scaling, int N, int K,
+                  void* out, int out_dtype, cudaStream_t st) {
+  dim3 grid((unsigned)((K + kMrCols - 1) / kMrCols), (unsigned)((N + kMrRows - 1) / kMrRows));
+  const S* sp = static_cast<const S*>(s);
+  const S* qp = static_cast<const S*>(qs);
+  const S* dp = static_cast<const S*>(dqs);
+  const P* ap = static_cast<const P*>(la);
+  const P* bp = static_cast<const P*>(lb);
+  // O = promote(S, P): float32 if either is, else S (== P)
+  if (out_dtype == LQ_F32)
+    nf4_merge_lora_kernel<S, P, float><<<grid, 256, 0, st>>>(codes, sp, qp, dp, group, dq_group, ap, bp, r, scaling, N, K, static_cast<float*>(out));
+  else
+    nf4_merge_lora_kernel<S, P, S><<<grid, 256, 0, st>>>(codes, sp, qp, dp, group, dq_group, ap, bp, r, scaling, N, K, static_cast<S*>(out));
+  return launched("nf4_merge_lora_kernel");
+}
+
+template <typename S>
+int merge_lora_s(int p_dtype, const uint8_t* codes, const void* s, const void* qs, const void* dqs,
+                 int64_t group, int64_t dq_group, const void* la, const void* lb, int r, float scaling,
+                 int N, int K, void* out, int out_dtype, cudaStream_t st) {
+  switch (p_dtype) {
+    case LQ_F32: return merge_lora_sp<S, float>(codes, s, qs, dqs, group, dq_group, la, lb, r, scaling, N, K, out, out_dtype, st);
+    case LQ_F16: return merge_lora_sp<S, __half>(codes, s, qs, dqs, group, dq_group, la, lb, r, scaling, N, K, out, out_dtype, st);
+    case LQ_BF16: return merge_lora_sp<S, __nv_bfloat16>(codes, s, qs, dqs, group, dq_group, la, lb, r, scaling, N, K, out, out_dtype, st);
+    default: set_error("unsupported LoRA dtype %d", p_dtype); return LQ_EDTYPE;
+  }
+}
+
+}  // namespace
+}  // namespace lq
+
+extern "C" int lq_nf4_merge_lora(const uint8_t* packed_codes, int64_t N, int64_t K, int64_t group,
+                                 int64_t dq_group, const void* scales, const void* q_scales,
+                                 const void* dq_scales, int s_dtype, const void* lora_a,
+                                 const void* lora_b, int p_dtype, int64_t rank, float scaling,
+                                 void* out, int out_dtype, void* stream) {
+  using namespace lq;
+  LQ_REQUIRE(N >= 0 && K >= 0 && group >= 1, LQ_EINVAL, "bad size");
+  if (N == 0 || K == 0) return LQ_OK;
+  LQ_REQUIRE(K % 8 == 0, LQ_EINVAL, "merge_lora needs in_features %% 8 == 0 (got %lld)", (long long)K);
+  LQ_REQUIRE(N < (1LL << 31) && K < (1LL << 31), LQ_ERANGE, "shape too large");
+  LQ_REQUIRE(rank >= 1 && rank <= kMrMaxRank, LQ_ERANGE, "LoRA rank %lld outside [1, %d]", (long long)rank, kMrMaxRank);
+  LQ_REQUIRE(packed_codes && out && lora_a && lora_b && (scales || q_scales), LQ_EINVAL, "NULL pointer");
+  LQ_REQUIRE(!q_scales || (dq_scales && dq_group > 0), LQ_EINVAL, "double dequantization needs dq_scales and dq_group");
+  LQ_REQUIRE(reinterpret_cast<uintptr_t>(packed_codes) % 4 == 0, LQ_EALIGN, "codes must be 4-byte aligned");
+  const bool f32 = s_dtype == LQ_F32 || p_dtype == LQ_F32;
+  LQ_REQUIRE(f32 ? out_dtype == LQ_F32 : (s_dtype == p_dtype && out_dtype == s_dtype), LQ_EDTYPE,
+             "merge_lora output dtype must be the promotion of the scales' and LoRA dtypes");
+  cudaStream_t st = as_stream(stream);
+  const uint8_t* c = packed_codes;
+  switch (s_dtype) {
+    case LQ_F32: return merge_lora_s<float>(p_dtype, c, scales, q_scales, dq_scales, group, dq_group, lora_a, lora_b, (int)rank, scaling, (int)N, (int)K, out, out_dtype, st);
+    case LQ_F16: return merge_lora_s<__half>(p_dtype, c, scales, q_scales, dq_scales, group, dq_group, lora_a, lora_b, (int)rank, scaling, (int)N, (int)K, out, out_dtype, st);
+    case LQ_BF16: return merge_lora_s<__nv_bfloat16>(p_dtype, c, scales, q_scales, dq_scales, group, dq_group, lora_a, lora_b, (int)rank, scaling, (int)N, (int)K, out, out_dtype, st);
+    default: set_error("unsupported scale dtype %d", s_dtype); return LQ_EDTYPE;
+  }
+}

@@ -56,13 +56,27 @@ __device__ __forceinline__ uint64_t global_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
+// try_wait that, while the phase is incomplete, suspends the thread for up to
+// hint_ns instead of returning at once: a waiting warp then sleeps rather
+// than spinning through issue slots that the other warps need.
+__device__ __forceinline__ bool mbar_try_sleep(uint64_t* b, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait; false once limit_ns of wall time has passed.
 __device__ __forceinline__ bool mbar_wait_for(uint64_t* b, uint32_t parity, uint64_t limit_ns) {
   if (mbar_try(b, parity)) return true;
   const uint64_t t0 = global_ns();
   for (uint32_t i = 1;; ++i) {
-    if (mbar_try(b, parity)) return true;
-    if ((i & 255) == 0 && global_ns() - t0 > limit_ns) return false;
+    if (mbar_try_sleep(b, parity, 10000u)) return true;
+    if ((i & 15) == 0 && global_ns() - t0 > limit_ns) return false;
   }
 }
 // The kernels' waits: bounded by kWaitNs.

@@ -141,6 +141,16 @@ struct W4Args {
   int kb_shift;  // log2(group / kBK) when that is a power of two, else -1
 };
 
+// The LoRA term of QLoRALinear.forward fused into the base product
+// (qlora.py:306-312): y += u @ b^T with u = scaling * x @ lora_A^T [M, r]
+// (computed by the caller; padded to 64 columns of zeros for the tensor-core
+// path) and b = lora_B [N, r], both in the activation dtype.  r = 0: none.
+struct LoraArgs {
+  const void* u = nullptr;
+  const void* b = nullptr;
+  int r = 0;
+};
+
 inline int kb_shift_of(int group) {
   const int r = group / kBK;
   return (r & (r - 1)) == 0 ? __builtin_ctz(r) : -1;
@@ -174,6 +184,33 @@ __device__ __forceinline__ void build_pair_lut(uint32_t* lut, uint32_t* tmp) {
     const uint32_t v = tmp[i >> 3];  // words 4i..4i+3 are copies of entry i / 8
     reinterpret_cast<uint4*>(lut)[i] = make_uint4(v, v, v, v);
   }
+}
+
+// The GEMV's copy of the table: 16 copies (16 KB, so that four blocks fit on
+// an SM), entry b of copy r at word 16 b + r; lane l reads copy l % 16 (lanes
+// l and l + 16 meet in a bank only when their entries differ and have equal
+// parity).
+constexpr int kPairLut16Words = 256 * 16;
+template <typename T>
+__device__ __forceinline__ void build_pair_lut16(uint32_t* lut, uint32_t* tmp) {
+  for (int b = threadIdx.x; b < 256; b += blockDim.x) {
+    union {
+      T h[2];
+      uint32_t u;
+    } pr;
+    pr.h[0] = Ty<T>::from_f(Ty<T>::round(kNF4[b & 15]));
+    pr.h[1] = Ty<T>::from_f(Ty<T>::round(kNF4[b >> 4]));
+    tmp[b] = pr.u;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < kPairLut16Words / 4; i += blockDim.x) {
+    const uint32_t v = tmp[i >> 2];  // words 4i..4i+3 are copies of entry i / 4
+    reinterpret_cast<uint4*>(lut)[i] = make_uint4(v, v, v, v);
+  }
+}
+__device__ __forceinline__ uint32_t pair_lut16_off(uint32_t w, int b, uint32_t copy4) {
+  const uint32_t off = (b == 0 ? (w << 6) : (w >> (8 * b - 6))) & 0x3FC0u;
+  return off | copy4;
 }
 
 // Byte offset of the table word for byte b (0..3) of w, in copy `lane`.
@@ -225,9 +262,11 @@ struct Smem {
 
 template <typename T, int BT, int S, bool NF, int WK>
 __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                                                       const __grid_constant__ CUtensorMap tmap_u,
                                                        const uint8_t* __restrict__ packed,
                                                        const float* __restrict__ bias,
                                                        T* __restrict__ y, W4Args a,
+                                                       const T* __restrict__ lora_b, int lora_r,
                                                        int* __restrict__ err) {
   using L = Smem<T, BT, S, NF, WK>;
   constexpr int SC = WK * (kBK / 2);  // tensor-memory columns of one stage's A slot
@@ -251,7 +290,10 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nt = blockIdx.x;       // weight-row tile
   const int m0 = blockIdx.y * BT;  // first token of the tile
-  const int n_steps = a.n_kb / WK;
+  // the base product's K steps, then (LoRA) one more whose A operand is
+  // lora_B's 128 rows of the tile and whose B operand is u (zero past r)
+  const int n_main = a.n_kb / WK;
+  const int n_steps = n_main + (lora_r > 0 ? 1 : 0);
   const uint8_t* wtile = packed + (size_t)nt * a.n_kb * kWStage;
   const uint8_t* stile = packed + (size_t)(a.N / kRows) * a.n_kb * kWStage +
                          (size_t)nt * a.n_groups * kSStage;
@@ -289,6 +331,7 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
     // ---------------- activation producer ----------------
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_x)) : "memory");
+      if (lora_r > 0) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_u)) : "memory");
       int issued = 0;
       for (int i = 0; i < n_steps; ++i) {
         const int s = i % S;
@@ -296,8 +339,12 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
         if (s_err) break;
         mbar_expect_tx(&full_x[s], L::kX);
 #pragma unroll
-        for (int hk = 0; hk < WK; ++hk)
-          tma_load_2d(smem + L::off_x + s * L::kX + hk * L::kXh, &tmap_x, (i * WK + hk) * kBK, m0, &full_x[s]);
+        for (int hk = 0; hk < WK; ++hk) {
+          if (i < n_main)
+            tma_load_2d(smem + L::off_x + s * L::kX + hk * L::kXh, &tmap_x, (i * WK + hk) * kBK, m0, &full_x[s]);
+          else  // u has 64 columns: the second half of a 128-wide stage is all fill (zeros)
+            tma_load_2d(smem + L::off_x + s * L::kX + hk * L::kXh, &tmap_u, hk * kBK, m0, &full_x[s]);
+        }
         issued = i + 1;
       }
       if (s_err) {
@@ -313,6 +360,14 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
         const int sw = i % SW;
         if (i >= SW && !mbar_wait(&w_empty[sw], ((i / SW) - 1) & 1)) { s_err = 5; break; }
         if (s_err) break;
+        if (i == n_main) {
+          // LoRA step: the tile's 128 rows of lora_B (r values each) into the code slot
+          const uint32_t nb = (uint32_t)(kRows * lora_r * (int)sizeof(T));
+          mbar_expect_tx(&full_w[sw], nb);
+          bulk_load(smem + L::off_w + sw * WK * kWStage, lora_b + (size_t)nt * kRows * lora_r, nb, &full_w[sw]);
+          issued = i + 1;
+          continue;
+        }
         mbar_expect_tx(&full_w[sw], WK * (kWStage + kSStage));
         // the WK weight halves of a step are adjacent in the packed layout
         bulk_load(smem + L::off_w + sw * WK * kWStage, wtile + (size_t)i * WK * kWStage, WK * kWStage, &full_w[sw]);
@@ -371,6 +426,20 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
       const int sw = i % SW;
       if (!mbar_wait_warp(&full_w[sw], (i / SW) & 1)) { ok = false; break; }
       if (i >= S && !mbar_wait_warp(&empty[s], ph ^ 1)) { ok = false; break; }
+      if (i == n_main) {
+        // LoRA step: A = lora_B[row, hk*64 + 32h + 0..31] (zero past r)
+        const uint32_t brow = sbase + L::off_w + sw * WK * kWStage + (uint32_t)(row * lora_r * (int)sizeof(T));
+#pragma unroll
+        for (int hk = 0; hk < WK; ++hk) {
+          uint32_t r[16];
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const int col = hk * kBK + 32 * h + 2 * c;
+            r[c] = col < lora_r ? lds_b32(brow + col * (int)sizeof(T)) : 0u;
+          }
+          tmem_st16(lane_base + kAcol + s * SC + hk * (kBK / 2) + 16 * h, r);
+        }
+      } else {
 #pragma unroll
       for (int hk = 0; hk < WK; ++hk) {
         // this warp's half of the row's codes: words 4h..4h+3 (k = 32h..32h+31)
@@ -402,6 +471,7 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
           }
         }
         tmem_st16(lane_base + kAcol + s * SC + hk * (kBK / 2) + 16 * h, r);
+      }
       }
       tmem_wait_st();
       tc_fence_before();
@@ -448,26 +518,45 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
 }
 
 // ---------------------------------------------------------------------------
-// Small M (M <= 8 tokens): the forward is a weight-streaming GEMV, bound by
-// HBM; a 128 x BT tensor-memory tile would sit mostly idle.  A block of
-// kGemvWarps warps owns 16 (NF: 32) weight rows, small enough that every block
-// of the grid is resident at once; warp w takes the K steps w, w + kGemvWarps,
-// ... (their weights streamed by cp.async into a per-warp ring; 512-byte TMA
-// bulk copies measured slower here, bound by their request rate) and runs
-// mma.sync.m16n8k16 (f32 accumulate) with the weights as the A operand and up
-// to 8 tokens per B tile.  The A fragment of a lane is (rows g, g+8) x (k
-// pairs 2c, 2c+8) of each 16-wide k tile (g = lane / 4, c = lane % 4), which
-// in the packed layout are nibbles (c, c+4) of words 2t and 2t+1 of its two
-// rows: one shift, one LOP3 with the magic exponent and one subtraction of
-// (magic + zero) give (q - zero) exactly in T.  The scale of the row's group
-// multiplies each K step's partial sums (sum_k (q - zero) * x) in fp32, so
-// the weights enter the MMA exactly; the warps' partial sums are added in
-// shared memory.
+// Small M (M <= 16 tokens): the forward is a weight-streaming GEMV, bound by
+// HBM; a 128 x BT tensor-memory tile would sit mostly idle.  It runs
+// mma.sync.m16n8k16 (f32 accumulate) with the weights as the A operand and
+// one or two 8-token B tiles, on a layout of the codes of its own that the
+// pack kernels append to the operand ("GEMV codes"):
+//
+//   [N/16 slabs][K/64 steps][32 lanes][4 words], lane L = 4 g + c owns the 16
+//   bytes of its A fragments: word t holds rows (g, g + 8) x k (4t .. 4t+3) of
+//   the lane's 16-wide k range 16c .. 16c+15 of the step, as
+//     INT4: bits 0-3 / 16-19   row g,   k 4t, 4t+1     (a0)
+//           bits 4-7 / 20-23   row g+8, k 4t, 4t+1     (a1)
+//           bits 8-11 / 24-27  row g,   k 4t+2, 4t+3   (a2)
+//           bits 12-15 / 28-31 row g+8, k 4t+2, 4t+3   (a3)
+//     NF4:  byte b = the (low, high) nibble pair of fragment a_b.
+//   The MMA's k slots (2c, 2c+1, 2c+8, 2c+9) of step t are these k values,
+//   for the weights and the activations alike, so each lane's activations are
+//   16 contiguous halves (two 16-byte loads) and each lane reads exactly its
+//   16 bytes of codes (one shared load, no broadcast).
+//
+// INT4: a fragment is (code | magic) with one LOP3 -- 1024 + q (fp16, bits
+// 0-3), 1024 + 16 q (fp16, bits 4-7: rows g + 8), 128 + q (bf16, after a
+// shift) -- and the zero point is not subtracted per weight: with S = sum of
+// the group's activations (one more MMA per 16-wide k tile with A = 1), the
+// group contributes s * (f D - (o + z) S) to the output, (f, o) = (1, magic)
+// or (1/16, 64), D = the MMA sum of the fragments.  D and S are accumulated
+// over the steps of a group and folded in once per group.  NF4: the fragment
+// is the table pair of the code byte, the block scale multiplies D.
+//
+// A block of WARPS warps owns R16 slabs (16 R16 rows); warp w takes a
+// contiguous share of the K steps, streamed into its own DEPTH-stage ring by
+// bulk copies (one per lane: each slab's 512 bytes of codes and 64 of its
+// group's (zero, scale) pairs, one 128-byte row per token of activations)
+// completing on the slot's mbarrier (bounded waits; a stage that never lands
+// sets *err); the warps' sums are added in shared memory.
 // ---------------------------------------------------------------------------
 template <typename T> struct MmaOp;
 template <> struct MmaOp<__half> {
   __device__ __forceinline__ static void mma(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -480,10 +569,13 @@ template <> struct MmaOp<__half> {
   __device__ __forceinline__ static float hi_f(uint32_t pair) {
     return __half2float(__ushort_as_half((unsigned short)(pair >> 16)));
   }
+  __device__ __forceinline__ static float lo_f(uint32_t pair) {
+    return __half2float(__ushort_as_half((unsigned short)(pair & 0xFFFFu)));
+  }
 };
 template <> struct MmaOp<__nv_bfloat16> {
   __device__ __forceinline__ static void mma(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -494,161 +586,288 @@ template <> struct MmaOp<__nv_bfloat16> {
     return *reinterpret_cast<uint32_t*>(&h);
   }
   __device__ __forceinline__ static float hi_f(uint32_t pair) { return __uint_as_float(pair & 0xFFFF0000u); }
+  __device__ __forceinline__ static float lo_f(uint32_t pair) { return __uint_as_float(pair << 16); }
 };
 
-constexpr int kGemvWarps = 4;  // warps per block = K split of the block's rows
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+
+// Byte offset of the GEMV records in the packed operand (after the tile codes
+// and the (zero, scale) pairs of n_pairs groups per row).
+__host__ __device__ inline int64_t gemv_codes_off(int64_t N, int64_t K, int64_t pairs_per_row) {
+  return N * K / 2 + N * pairs_per_row * 4;
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+// GEMV record of one (16-row slab, group): the group's K steps of codes (512
+// bytes each, lane-major) followed by the slab's 16 (zero, scale) pairs
+// (64 bytes).  Records of a slab are contiguous in K, so a warp's share of
+// the K range is one run of memory.  (NF4: 64-wide groups.)
+__host__ __device__ inline int64_t gv_record_bytes(int64_t group) { return group / kBK * 512 + 64; }
 
-// Block = R16 x 16 consecutive weight rows (inside one 128-row tile); warp w
-// takes the K steps w, w + kGemvWarps, ... of all of them.  A K step's slice
-// of the block -- R16 x 512 contiguous bytes of codes and R16 x 64 of (zero,
-// scale) pairs -- is copied with 16-byte cp.async (L2 only) into the warp's
-// own ring of DEPTH stages, so each warp keeps DEPTH steps of weights in
-// flight without registers; the activations of the next step are loaded into
-// registers (from L1 / L2: every block reads the same x) while the current one
-// is multiplied.
-template <typename T, bool NF, int R16, int DEPTH>
-__global__ void __launch_bounds__(32 * kGemvWarps) w4a16_gemv_kernel(const T* __restrict__ x,
-                                                         const uint8_t* __restrict__ packed,
-                                                         const float* __restrict__ bias,
-                                                         T* __restrict__ y, W4Args a) {
-  constexpr int kCodes = R16 * 512, kStage = R16 * 576;
-  extern __shared__ __align__(16) uint8_t gv_smem[];
-  uint32_t* lut = reinterpret_cast<uint32_t*>(gv_smem);                                  // NF: pair table
-  float* red = reinterpret_cast<float*>(gv_smem + (NF ? kPairLutWords * 4 + 1024 : 0));  // [warps][R16][32][4]
-  uint8_t* ring = reinterpret_cast<uint8_t*>(red + kGemvWarps * R16 * 128);
+// word i (0..3, a compile-time constant after unrolling) of v
+__device__ __forceinline__ uint32_t word_of(const uint4& v, int i) {
+  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+
+template <typename T> struct GvInt4;
+template <> struct GvInt4<__half> {
+  static constexpr uint32_t one = 0x3C003C00u;  // fp16 1.0 pair
+  // fragments a0..a3 of one code word
+  __device__ __forceinline__ static void frag(uint32_t w, uint32_t (&a)[4]) {
+    const uint32_t w8 = w >> 8;
+    a[0] = (w & 0x000F000Fu) | 0x64006400u;   // 1024 + q
+    a[1] = (w & 0x00F000F0u) | 0x64006400u;   // 1024 + 16 q
+    a[2] = (w8 & 0x000F000Fu) | 0x64006400u;
+    a[3] = (w8 & 0x00F000F0u) | 0x64006400u;
+  }
+  // (f, -(o + z)) of rows g and g + 8 from zb = magic + z
+  __device__ __forceinline__ static void fold(float zb, bool hi_row, float& f, float& c) {
+    f = hi_row ? 0.0625f : 1.0f;
+    c = hi_row ? -(zb - 960.0f) : -zb;
+  }
+};
+template <> struct GvInt4<__nv_bfloat16> {
+  static constexpr uint32_t one = 0x3F803F80u;  // bf16 1.0 pair
+  __device__ __forceinline__ static void frag(uint32_t w, uint32_t (&a)[4]) {
+    a[0] = (w & 0x000F000Fu) | 0x43004300u;   // 128 + q
+    a[1] = ((w >> 4) & 0x000F000Fu) | 0x43004300u;
+    a[2] = ((w >> 8) & 0x000F000Fu) | 0x43004300u;
+    a[3] = ((w >> 12) & 0x000F000Fu) | 0x43004300u;
+  }
+  __device__ __forceinline__ static void fold(float zb, bool, float& f, float& c) {
+    f = 1.0f;
+    c = -zb;
+  }
+};
+
+// Stage of the GEMV ring: one group of the warp's K range -- its R16
+// records (codes + pairs) and XR token rows of its activations (2G bytes
+// each, pitch 2G + 16: the pad puts the 8 lanes of each quarter-warp on
+// distinct banks).  Sizes depend on the group size G (64 .. 256).
+__host__ __device__ inline int gv_xpitch(int G) { return 2 * G + 16; }
+__host__ __device__ inline int gv_stage_bytes(int R16, int XR, int G) {
+  return R16 * (int)gv_record_bytes(G) + XR * gv_xpitch(G);
+}
+constexpr int kGvMaxDepth = 4;
+
+template <typename T, bool NF, int R16, int NT, int XR, int WARPS>
+__global__ void __launch_bounds__(32 * WARPS, 4) w4a16_gemv_kernel(const T* __restrict__ x,
+                                                    const uint8_t* __restrict__ packed,
+                                                    const float* __restrict__ bias,
+                                                    T* __restrict__ y, W4Args a, int G, int depth,
+                                                    int* err, const T* __restrict__ lora_u,
+                                                    const T* __restrict__ lora_b, int lora_r) {
+  const int rb = (int)gv_record_bytes(G), xp = gv_xpitch(G);
+  const int xoff0 = R16 * rb, stage = gv_stage_bytes(R16, XR, G);
+  const int spg = G / kBK;  // K steps per group
+  extern __shared__ __align__(128) uint8_t gv_smem[];
+  uint32_t* lut = reinterpret_cast<uint32_t*>(gv_smem);                                    // NF: pair table
+  float* red = reinterpret_cast<float*>(gv_smem + (NF ? kPairLut16Words * 4 + 1024 : 0));  // [warps][R16][NT][32][4]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(red + WARPS * R16 * NT * 128);             // [warps][kGvMaxDepth]
+  uint8_t* ring = reinterpret_cast<uint8_t*>(bars + WARPS * kGvMaxDepth);
+  __shared__ int s_err;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
-  if constexpr (NF) {
-    build_pair_lut<T>(lut, reinterpret_cast<uint32_t*>(gv_smem + kPairLutWords * 4));
-    __syncthreads();
+  if (threadIdx.x == 0) s_err = 0;
+  if constexpr (NF) build_pair_lut16<T>(lut, reinterpret_cast<uint32_t*>(gv_smem + kPairLut16Words * 4));
+  uint64_t* bar = bars + warp * kGvMaxDepth;
+  if (lane == 0) {
+    for (int d = 0; d < depth; ++d) mbar_init(&bar[d], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
-  uint8_t* my = ring + warp * DEPTH * kStage;
-  const int r0 = blockIdx.x * 16 * R16;  // first weight row of the block
-  const int nt = r0 / kRows, rit0 = r0 % kRows;
-  const uint8_t* codes = packed + ((size_t)nt * a.n_kb * kRows + rit0) * 32;
-  const uint8_t* pairs = packed + (size_t)a.N * a.K / 2 + ((size_t)nt * a.n_groups * kRows + rit0) * 4;
-  auto issue = [&](int kb, uint8_t* dst) {
-    const uint8_t* cs = codes + (size_t)kb * kRows * 32;
+  __syncthreads();
+  uint8_t* my = ring + warp * depth * stage;
+  const int slab0 = blockIdx.x * R16;  // first 16-row slab of the block
+  const int r0 = slab0 * 16;           // first weight row
+  const int n_grp = a.K / G;
+  const uint8_t* recs = packed + gemv_codes_off(a.N, a.K, NF ? a.n_kb : a.n_groups) + (size_t)slab0 * n_grp * rb;
+  // this warp's contiguous share of the groups
+  const int per = (n_grp + WARPS - 1) / WARPS;
+  const int g0 = warp * per;
+  const int n_my = max(0, min(n_grp, g0 + per) - g0);
+  const uint32_t stage_tx = (uint32_t)(R16 * rb + a.M * 2 * G);
+  // group i of the warp into slot i % depth: lane 0 issues every copy (one
+  // per slab, one per token row)
+  auto issue = [&](int i) {
+    const int sl = i % depth, grp = g0 + i;
+    uint8_t* dst = my + sl * stage;
+    if (lane == 0) {
+      mbar_expect_tx(&bar[sl], stage_tx);
 #pragma unroll
-    for (int i = 0; i < R16; ++i) cp_async16(dst + (i * 32 + lane) * 16, cs + (i * 32 + lane) * 16);
-    if (lane < 4 * R16) cp_async16(dst + kCodes + lane * 16, pairs + (size_t)group_of(a, kb) * kRows * 4 + lane * 16);
-  };
-  // this warp's K steps: kb = warp + i * kGemvWarps, i < n_my
-  const int n_my = a.n_kb > warp ? (a.n_kb - warp + kGemvWarps - 1) / kGemvWarps : 0;
-#pragma unroll
-  for (int i = 0; i < DEPTH; ++i) {
-    if (i < n_my) issue(warp + i * kGemvWarps, my + i * kStage);
-    cp_async_commit();
-  }
-  // B fragment of lane (g, c): x[token g][k = 16t + 2c (+1), 16t + 2c + 8 (+9)].
-  // Lanes of tokens >= M read token 0: their columns are never stored.
-  const uint32_t* xr = reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint16_t*>(x) +
-                                                         (size_t)(g < a.M ? g : 0) * a.K + 2 * c);
-  auto load_x = [&](int kb, uint32_t (&bx)[4][2]) {
-    const uint32_t* p = xr + kb * (kBK / 2);
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      bx[t][0] = __ldg(p + 8 * t);
-      bx[t][1] = __ldg(p + 8 * t + 4);
+      for (int r = 0; r < R16; ++r)
+        bulk_load(dst + r * rb, recs + ((size_t)r * n_grp + grp) * rb, (uint32_t)rb, &bar[sl]);
+      for (int row = 0; row < a.M; ++row)
+        bulk_load(dst + xoff0 + row * xp, x + (size_t)row * a.K + (size_t)grp * G, (uint32_t)(2 * G), &bar[sl]);
     }
   };
-  float acc[R16][4];
+  for (int i = 0; i < depth && i < n_my; ++i) issue(i);
+  // activations of lane (g, c), B tile j: token 8 j + g (token 0 past M:
+  // those columns are never stored), halves 16 c .. 16 c + 15 of each step
+  int xoff[NT];
+#pragma unroll
+  for (int j = 0; j < NT; ++j) xoff[j] = xoff0 + (8 * j + g < a.M ? 8 * j + g : 0) * xp + 32 * c;
+  // dsum / ssum: MMA sums of the current group, split by the parity of the
+  // 16-wide k tile so that consecutive MMAs are independent
+  float acc[R16][NT][4];
 #pragma unroll
   for (int r = 0; r < R16; ++r)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) acc[r][i] = 0.0f;
-  uint32_t bx[4][2];
-  if (n_my > 0) load_x(warp, bx);
-#pragma unroll 2
-  for (int i = 0; i < n_my; ++i) {
-    const int kb = warp + i * kGemvWarps;
-    uint8_t* st = my + (i % DEPTH) * kStage;
-    uint32_t nx[4][2];
-    if (i + 1 < n_my) load_x(kb + kGemvWarps, nx);
-    cp_async_wait<DEPTH - 1>();
-    __syncwarp();
+    for (int j = 0; j < NT; ++j)
 #pragma unroll
-    for (int r = 0; r < R16; ++r) {
-      const uint4* src = reinterpret_cast<const uint4*>(st + r * 512);
-      const uint4 w0 = src[2 * g], w1 = src[2 * g + 1];        // row g
-      const uint4 w2 = src[2 * g + 16], w3 = src[2 * g + 17];  // row g + 8
-      const uint32_t zs0 = *reinterpret_cast<const uint32_t*>(st + kCodes + r * 64 + 4 * g);
-      const uint32_t zs1 = *reinterpret_cast<const uint32_t*>(st + kCodes + r * 64 + 4 * (g + 8));
-      const uint32_t zb0 = __byte_perm(zs0, zs0, 0x1010), zb1 = __byte_perm(zs1, zs1, 0x1010);
-      const uint32_t ra[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-      const uint32_t rb[8] = {w2.x, w2.y, w2.z, w2.w, w3.x, w3.y, w3.z, w3.w};
-      float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      for (int e = 0; e < 4; ++e) acc[r][j][e] = 0.0f;
+  const uint32_t copy4 = (uint32_t)(lane & 15) << 2;
+  const char* lb = reinterpret_cast<const char*>(lut);
+  const uint32_t ones[4] = {GvInt4<T>::one, GvInt4<T>::one, GvInt4<T>::one, GvInt4<T>::one};
+  int i = 0;
+  for (; i < n_my; ++i) {
+    const int sl = i % depth;
+    const uint8_t* st = my + sl * stage;
+    if (!mbar_wait_warp(&bar[sl], (uint32_t)(i / depth) & 1u)) break;
+    float dsum[R16][NT][2][4], ssum[NT][2][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        ssum[j][0][e] = ssum[j][1][e] = 0.0f;
+#pragma unroll
+        for (int r = 0; r < R16; ++r) dsum[r][j][0][e] = dsum[r][j][1][e] = 0.0f;
+      }
+    for (int ks = 0; ks < spg; ++ks) {
+      uint4 xv[NT][2], cw[R16];
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        xv[j][0] = *reinterpret_cast<const uint4*>(st + xoff[j] + ks * 128);
+        xv[j][1] = *reinterpret_cast<const uint4*>(st + xoff[j] + ks * 128 + 16);
+      }
+#pragma unroll
+      for (int r = 0; r < R16; ++r) cw[r] = *reinterpret_cast<const uint4*>(st + r * rb + ks * 512 + lane * 16);
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
-        uint32_t af[4];
-        if constexpr (NF) {
-          // byte c of words 2t, 2t+1 = k pairs (16t + 2c, +8): table pairs, scaled below
-          const char* lb = reinterpret_cast<const char*>(lut);
-          const uint32_t l4 = (uint32_t)lane << 2;
-          af[0] = *reinterpret_cast<const uint32_t*>(lb + ((((ra[2 * t] >> (8 * c)) & 0xFFu) << 7) | l4));
-          af[1] = *reinterpret_cast<const uint32_t*>(lb + ((((rb[2 * t] >> (8 * c)) & 0xFFu) << 7) | l4));
-          af[2] = *reinterpret_cast<const uint32_t*>(lb + ((((ra[2 * t + 1] >> (8 * c)) & 0xFFu) << 7) | l4));
-          af[3] = *reinterpret_cast<const uint32_t*>(lb + ((((rb[2 * t + 1] >> (8 * c)) & 0xFFu) << 7) | l4));
-        } else {
-          af[0] = MmaOp<T>::sub2(((ra[2 * t] >> (4 * c)) & 0x000F000Fu) | Act<T>::magic, zb0);
-          af[1] = MmaOp<T>::sub2(((rb[2 * t] >> (4 * c)) & 0x000F000Fu) | Act<T>::magic, zb1);
-          af[2] = MmaOp<T>::sub2(((ra[2 * t + 1] >> (4 * c)) & 0x000F000Fu) | Act<T>::magic, zb0);
-          af[3] = MmaOp<T>::sub2(((rb[2 * t + 1] >> (4 * c)) & 0x000F000Fu) | Act<T>::magic, zb1);
-        }
-        MmaOp<T>::mma(part, af, bx[t][0], bx[t][1]);
-      }
-      // scales of rows g and g + 8 (high halves of the pairs)
-      const float s0 = MmaOp<T>::hi_f(zs0), s1 = MmaOp<T>::hi_f(zs1);
-      acc[r][0] = fmaf(part[0], s0, acc[r][0]);
-      acc[r][1] = fmaf(part[1], s0, acc[r][1]);
-      acc[r][2] = fmaf(part[2], s1, acc[r][2]);
-      acc[r][3] = fmaf(part[3], s1, acc[r][3]);
-    }
-    __syncwarp();  // every lane has read the stage before it is refilled
-    if (i + DEPTH < n_my) issue(kb + DEPTH * kGemvWarps, st);
-    cp_async_commit();
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      bx[t][0] = nx[t][0];
-      bx[t][1] = nx[t][1];
+        for (int r = 0; r < R16; ++r) {
+          uint32_t af[4];
+          if constexpr (NF) {
+#pragma unroll
+            for (int b = 0; b < 4; ++b)
+              af[b] = *reinterpret_cast<const uint32_t*>(lb + pair_lut16_off(word_of(cw[r], t), b, copy4));
+          } else {
+            GvInt4<T>::frag(word_of(cw[r], t), af);
+          }
+#pragma unroll
+          for (int j = 0; j < NT; ++j)
+            MmaOp<T>::mma(dsum[r][j][t & 1], af, word_of(xv[j][t >> 1], 2 * (t & 1)),
+                          word_of(xv[j][t >> 1], 2 * (t & 1) + 1));
+        }
+        if constexpr (!NF) {
+#pragma unroll
+          for (int j = 0; j < NT; ++j)
+            MmaOp<T>::mma(ssum[j][t & 1], ones, word_of(xv[j][t >> 1], 2 * (t & 1)),
+                          word_of(xv[j][t >> 1], 2 * (t & 1) + 1));
+        }
+      }
     }
+    // fold the group in: its 16 pairs follow the codes of each record
+#pragma unroll
+    for (int r = 0; r < R16; ++r) {
+      const uint32_t zs0 = *reinterpret_cast<const uint32_t*>(st + r * rb + spg * 512 + 4 * g);
+      const uint32_t zs1 = *reinterpret_cast<const uint32_t*>(st + r * rb + spg * 512 + 4 * (g + 8));
+      const float s0 = MmaOp<T>::hi_f(zs0), s1 = MmaOp<T>::hi_f(zs1);
+      if constexpr (NF) {
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+          acc[r][j][0] = fmaf(dsum[r][j][0][0] + dsum[r][j][1][0], s0, acc[r][j][0]);
+          acc[r][j][1] = fmaf(dsum[r][j][0][1] + dsum[r][j][1][1], s0, acc[r][j][1]);
+          acc[r][j][2] = fmaf(dsum[r][j][0][2] + dsum[r][j][1][2], s1, acc[r][j][2]);
+          acc[r][j][3] = fmaf(dsum[r][j][0][3] + dsum[r][j][1][3], s1, acc[r][j][3]);
+        }
+      } else {
+        float f0, c0, f1, c1;
+        GvInt4<T>::fold(MmaOp<T>::lo_f(zs0), false, f0, c0);
+        GvInt4<T>::fold(MmaOp<T>::lo_f(zs1), true, f1, c1);
+        const float sf0 = s0 * f0, sc0 = s0 * c0, sf1 = s1 * f1, sc1 = s1 * c1;
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+          // rows g, g+8 x tokens 2c, 2c+1; S of the tokens 2c, 2c+1
+          const float S0 = ssum[j][0][0] + ssum[j][1][0], S1 = ssum[j][0][1] + ssum[j][1][1];
+          acc[r][j][0] = fmaf(dsum[r][j][0][0] + dsum[r][j][1][0], sf0, fmaf(S0, sc0, acc[r][j][0]));
+          acc[r][j][1] = fmaf(dsum[r][j][0][1] + dsum[r][j][1][1], sf0, fmaf(S1, sc0, acc[r][j][1]));
+          acc[r][j][2] = fmaf(dsum[r][j][0][2] + dsum[r][j][1][2], sf1, fmaf(S0, sc1, acc[r][j][2]));
+          acc[r][j][3] = fmaf(dsum[r][j][0][3] + dsum[r][j][1][3], sf1, fmaf(S1, sc1, acc[r][j][3]));
+        }
+      }
+    }
+    __syncwarp();  // every lane has read the slot before it is refilled
+    if (i + depth < n_my) issue(i + depth);
   }
-  cp_async_wait<0>();
+  if (i < n_my) {
+    // a stage did not land within the wait limit: record it, and wait
+    // (bounded) for the copies still in flight before the block exits
+    if (lane == 0) s_err = 5;
+    for (int j = i + 1; j < n_my && j < i + depth; ++j) mbar_wait_warp(&bar[j % depth], (uint32_t)(j / depth) & 1u);
+  }
 #pragma unroll
   for (int r = 0; r < R16; ++r)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) red[((warp * R16 + r) * 32 + lane) * 4 + i] = acc[r][i];
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) red[(((warp * R16 + r) * NT + j) * 32 + lane) * 4 + e] = acc[r][j][e];
   __syncthreads();
-  // thread -> (r, lane, i) of the fragments; tokens 2c, 2c+1 are columns 0/1
-  for (int o = threadIdx.x; o < R16 * 128; o += blockDim.x) {
-    const int i = o & 3, ln = (o >> 2) & 31, r = o >> 7;
+  // thread -> (r, j, lane, e) of the fragments: rows g (+8 for e >= 2),
+  // tokens 8 j + 2 c (+1 for odd e)
+  for (int o = threadIdx.x; o < R16 * NT * 128; o += blockDim.x) {
+    const int e = o & 3, ln = (o >> 2) & 31, rj = o >> 7;
+    const int j = rj % NT, r = rj / NT;
     float sum = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kGemvWarps; ++w) sum += red[((w * R16 + r) * 32 + ln) * 4 + i];
-    const int row = r0 + 16 * r + (ln >> 2) + (i >= 2 ? 8 : 0);
-    const int tok = 2 * (ln & 3) + (i & 1);
+    for (int w = 0; w < WARPS; ++w) sum += red[(((w * R16 + r) * NT + j) * 32 + ln) * 4 + e];
+    const int row = r0 + 16 * r + (ln >> 2) + (e >= 2 ? 8 : 0);
+    const int tok = 8 * j + 2 * (ln & 3) + (e & 1);
     if (tok < a.M) {
+      // LoRA: + u[tok] . lora_B[row] (u rows padded to 64 columns)
+      for (int jr = 0; jr < lora_r; ++jr)
+        sum = fmaf(Ty<T>::to_f(lora_u[(size_t)tok * kBK + jr]), Ty<T>::to_f(lora_b[(size_t)row * lora_r + jr]), sum);
       if (bias) sum = __fadd_rn(sum, bias[row]);
       y[(size_t)tok * a.N + row] = Ty<T>::from_f(sum);
     }
   }
+  if (threadIdx.x == 0 && s_err && err) atomicExch(err, s_err);
 }
 
-template <bool NF, int R16, int DEPTH>
-constexpr int gemv_smem() {
-  return (NF ? kPairLutWords * 4 + 1024 : 0) + kGemvWarps * R16 * 512 + kGemvWarps * DEPTH * R16 * 576;
+// Dynamic shared memory of a GEMV block: NF table, the warps' partial sums,
+// barriers, the rings.
+template <bool NF, int R16, int NT, int WARPS>
+inline int gemv_fixed_smem() {
+  return (NF ? kPairLut16Words * 4 + 1024 : 0) + WARPS * R16 * NT * 512 + WARPS * kGvMaxDepth * 8;
+}
+constexpr int kGvSmemCap = 57 * 1024;  // four blocks per SM
+
+// Two 16-row slabs per block: N = 14336 gives 448 blocks, which must all be
+// resident at once (4 per SM, under 57 KB of shared memory each); the ring
+// is as deep (2 .. 4 groups per warp) as that leaves room for.  Returns 1
+// when the group size does not fit (the caller takes the tensor-core path).
+template <typename T, bool NF, int NT, int XR, int WARPS>
+int launch_gemv_nt(const W4Args& a, const void* x, const void* packed, const float* bias, void* y,
+                   int* err, cudaStream_t st, const LoraArgs& lo) {
+  constexpr int R16 = 2;
+  const int G = NF ? kBK : a.group;
+  const int fixed = gemv_fixed_smem<NF, R16, NT, WARPS>();
+  const int stage = gv_stage_bytes(R16, XR, G);
+  int depth = (kGvSmemCap - fixed) / (WARPS * stage);
+  if (depth > kGvMaxDepth) depth = kGvMaxDepth;
+  if (depth < 2 || a.N % (16 * R16) != 0) return 1;
+  const int smem = fixed + WARPS * depth * stage;
+  auto kern = w4a16_gemv_kernel<T, NF, R16, NT, XR, WARPS>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kGvSmemCap) != cudaSuccess)
+    return launched("w4a16_gemv_kernel (attribute)");
+  kern<<<a.N / (16 * R16), 32 * WARPS, smem, st>>>(static_cast<const T*>(x), static_cast<const uint8_t*>(packed),
+                                                   bias, static_cast<T*>(y), a, G, depth, err,
+                                                   static_cast<const T*>(lo.u), static_cast<const T*>(lo.b), lo.r);
+  return launched("w4a16_gemv_kernel");
 }
 
+// 0 = launched (or a launch error), 1 = not applicable here
 template <typename T, bool NF>
 int launch_gemv(const void* x, int M, int N, int K, int group, const void* packed, const float* bias,
-                void* y, cudaStream_t st) {
+                void* y, int* err, cudaStream_t st, const LoraArgs& lo) {
   W4Args a;
   a.M = M;
   a.N = N;
@@ -657,16 +876,10 @@ int launch_gemv(const void* x, int M, int N, int K, int group, const void* packe
   a.n_kb = K / kBK;
   a.n_groups = K / group;
   a.kb_shift = kb_shift_of(group);
-  // the NF table (33 KB) limits blocks per SM: 32 rows per block keeps the
-  // whole grid resident for N up to ~19K
-  constexpr int R16 = NF ? 2 : 1, DEPTH = NF ? 4 : 8;
-  constexpr int smem = gemv_smem<NF, R16, DEPTH>();
-  auto kern = w4a16_gemv_kernel<T, NF, R16, DEPTH>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-    return launched("w4a16_gemv_kernel (attribute)");
-  kern<<<N / (16 * R16), 32 * kGemvWarps, smem, st>>>(static_cast<const T*>(x), static_cast<const uint8_t*>(packed),
-                                                      bias, static_cast<T*>(y), a);
-  return launched("w4a16_gemv_kernel");
+  // M = 1: eight warps split K; larger M: four (the activation rows fill the stage)
+  if (M == 1) return launch_gemv_nt<T, NF, 1, 1, 8>(a, x, packed, bias, y, err, st, lo);
+  if (M <= 8) return launch_gemv_nt<T, NF, 1, 8, 4>(a, x, packed, bias, y, err, st, lo);
+  return launch_gemv_nt<T, NF, 2, 16, 4>(a, x, packed, bias, y, err, st, lo);
 }
 
 // ---------------------------------------------------------------------------
@@ -731,6 +944,42 @@ __global__ void __launch_bounds__(256) w4a16_pack_kernel(const int8_t* __restric
     pr.h[1] = Ty<T>::from_f(s);
     pout[t] = pr.u;
   }
+  // GEMV records (see gv_record_bytes): code word (slab, kb, lane 4g + c, t)
+  // -> rows (16 slab + g, + 8), k = 64 kb + 16 c + 4 t + 0..3, nibble
+  // positions as the GEMV reads them; then the group's 16 (zero_b, scale) pairs
+  uint8_t* gbase = packed + gemv_codes_off(N, K, ng);
+  const int spg = group / kBK;
+  const int64_t rb = gv_record_bytes(group);
+  for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < words;
+       u += (int64_t)gridDim.x * blockDim.x) {
+    const int t = (int)(u & 3), L = (int)((u >> 2) & 31);
+    const int64_t rest = u >> 7;
+    const int kb = (int)(rest % n_kb);
+    const int64_t slab = rest / n_kb;
+    const int64_t n0 = slab * 16 + (L >> 2);
+    const int k0 = kb * kBK + 16 * (L & 3) + 4 * t;
+    const int8_t* p0 = wi + n0 * K + k0;
+    const int8_t* p1 = p0 + 8 * (int64_t)K;
+    auto q = [&](const int8_t* p, int i) { return (uint32_t)((p[i] + bias8) & 15); };
+    uint8_t* rec = gbase + (slab * ng + kb / spg) * rb + (kb % spg) * 512;
+    reinterpret_cast<uint32_t*>(rec)[L * 4 + t] =
+        q(p0, 0) | (q(p0, 1) << 16) | (q(p1, 0) << 4) | (q(p1, 1) << 20) | (q(p0, 2) << 8) |
+        (q(p0, 3) << 24) | (q(p1, 2) << 12) | (q(p1, 3) << 28);
+  }
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < pairs;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t n = t / ng;
+    const int g = (int)(t % ng);
+    const float z = ld_s<ST>(zp, n * ng + g) + (float)bias8;
+    const float sv = ld_s<ST>(sc, n * ng + g);
+    union {
+      T h[2];
+      uint32_t u;
+    } pr;
+    pr.h[0] = Ty<T>::from_f(magic + z);
+    pr.h[1] = Ty<T>::from_f(sv);
+    reinterpret_cast<uint32_t*>(gbase + ((n / 16) * ng + g) * rb + spg * 512)[n % 16] = pr.u;
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -785,6 +1034,39 @@ __global__ void __launch_bounds__(256) nf4lin_pack_kernel(const uint32_t* __rest
     pr.h[1] = Ty<T>::from_f(sv);
     pout[t] = pr.u;
   }
+  // GEMV records (64-wide groups, see gv_record_bytes): byte b of word (slab,
+  // kb, lane 4g + c, t) = the code byte of fragment a_b (rows 16 slab + g, + 8;
+  // k = 64 kb + 16 c + 4 t (+2)); then the step's 16 (0, scale) pairs
+  const uint8_t* cb = reinterpret_cast<const uint8_t*>(codes);
+  uint8_t* gbase = packed + gemv_codes_off(N, K, n_kb);
+  const int64_t rb = gv_record_bytes(kBK);
+  for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < words;
+       u += (int64_t)gridDim.x * blockDim.x) {
+    const int t = (int)(u & 3), L = (int)((u >> 2) & 31);
+    const int64_t rest = u >> 7;
+    const int kb = (int)(rest % n_kb);
+    const int64_t slab = rest / n_kb;
+    const int64_t n0 = slab * 16 + (L >> 2);
+    const int64_t e0 = (n0 * K + kb * kBK + 16 * (L & 3) + 4 * t) / 2;  // byte of (row g, k0, k0 + 1)
+    const int64_t e1 = e0 + 4 * (int64_t)K;                                // row g + 8
+    reinterpret_cast<uint32_t*>(gbase + (slab * n_kb + kb) * rb)[L * 4 + t] =
+        (uint32_t)cb[e0] | ((uint32_t)cb[e1] << 8) | ((uint32_t)cb[e0 + 1] << 16) | ((uint32_t)cb[e1 + 1] << 24);
+  }
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < pairs;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t n = t / n_kb;
+    const int kb = (int)(t % n_kb);
+    const int64_t g = (n * K + (int64_t)kb * kBK) / group;
+    const float sv = q_scales ? tmul<ST>(tdiv<ST>(Ty<ST>::to_f(q_scales[g]), 127.0f), Ty<ST>::to_f(dq_scales[g / dq_group]))
+                              : Ty<ST>::to_f(scales[g]);
+    union {
+      T h[2];
+      uint32_t u;
+    } pr;
+    pr.h[0] = Ty<T>::from_f(0.0f);
+    pr.h[1] = Ty<T>::from_f(sv);
+    reinterpret_cast<uint32_t*>(gbase + ((n / 16) * n_kb + kb) * rb + 512)[n % 16] = pr.u;
+  }
 }
 
 // ---- host side ---------------------------------------------------------------
@@ -834,18 +1116,23 @@ int set_smem_once(Kern kern, int smem_bytes, std::atomic<uint64_t>& done) {
 
 template <typename T, int BT, int S, bool NF, int WK>
 int launch_w4(const void* x, int M, int N, int K, int group, const void* packed, const float* bias,
-              void* y, int* err, cudaStream_t st) {
+              void* y, int* err, cudaStream_t st, const LoraArgs& lo) {
   using L = Smem<T, BT, S, NF, WK>;
-  CUtensorMap map;
+  CUtensorMap map, umap;
   LQ_TRY(encode_x_map<T>(&map, x, M, K, BT));
+  if (lo.r > 0) {
+    LQ_TRY(encode_x_map<T>(&umap, lo.u, M, kBK, BT));  // u padded to 64 columns
+  } else {
+    umap = map;  // unused
+  }
   const W4Args a = w4_args(M, N, K, group);
   auto kern = w4a16_kernel<T, BT, S, NF, WK>;
   const int smem_bytes = L::bytes > 117 * 1024 ? L::bytes : 117 * 1024;
   static std::atomic<uint64_t> attr_done{0};
   LQ_TRY(set_smem_once(kern, smem_bytes, attr_done));
   dim3 grid(N / kRows, (M + BT - 1) / BT);
-  kern<<<grid, kW4Threads, smem_bytes, st>>>(map, static_cast<const uint8_t*>(packed), bias,
-                                    static_cast<T*>(y), a, err);
+  kern<<<grid, kW4Threads, smem_bytes, st>>>(map, umap, static_cast<const uint8_t*>(packed), bias,
+                                    static_cast<T*>(y), a, static_cast<const T*>(lo.b), lo.r, err);
   return launched("w4a16_kernel");
 }
 
@@ -876,34 +1163,38 @@ inline int pick_bt(int M, int N, std::initializer_list<int> cands, bool tensor_b
 // NF4 past M = 128, 64-wide stages.
 template <typename T, bool NF>
 int w4_dispatch(const void* x, int M, int N, int K, int group, const void* packed,
-                const float* bias, void* y, int* err, cudaStream_t st) {
-  if (M <= 8) return launch_gemv<T, NF>(x, M, N, K, group, packed, bias, y, st);
+                const float* bias, void* y, int* err, cudaStream_t st, const LoraArgs& lo = LoraArgs()) {
+  if (M <= 16) {
+    const int rc = launch_gemv<T, NF>(x, M, N, K, group, packed, bias, y, err, st, lo);
+    if (rc != 1) return rc;
+    // group too large for the GEMV's stage: 32-token tensor-core tiles
+    if (K % (2 * kBK) == 0) return launch_w4<T, 32, 4, NF, 2>(x, M, N, K, group, packed, bias, y, err, st, lo);
+    return launch_w4<T, 32, 8, NF, 1>(x, M, N, K, group, packed, bias, y, err, st, lo);
+  }
   if (K % (2 * kBK) == 0) {
-    if (M <= 16) return launch_w4<T, 16, 4, NF, 2>(x, M, N, K, group, packed, bias, y, err, st);
-    if (M <= 32) return launch_w4<T, 32, 4, NF, 2>(x, M, N, K, group, packed, bias, y, err, st);
-    if (M <= 64) return launch_w4<T, 64, 4, NF, 2>(x, M, N, K, group, packed, bias, y, err, st);
-    if (M <= 128) return launch_w4<T, 128, 4, NF, 2>(x, M, N, K, group, packed, bias, y, err, st);
+    if (M <= 32) return launch_w4<T, 32, 4, NF, 2>(x, M, N, K, group, packed, bias, y, err, st, lo);
+    if (M <= 64) return launch_w4<T, 64, 4, NF, 2>(x, M, N, K, group, packed, bias, y, err, st, lo);
+    if (M <= 128) return launch_w4<T, 128, 4, NF, 2>(x, M, N, K, group, packed, bias, y, err, st, lo);
     if constexpr (!NF) {
       switch (pick_bt(M, N, {256, 224, 192, 160}, true)) {
-        case 224: return launch_w4<T, 224, 3, NF, 2>(x, M, N, K, group, packed, bias, y, err, st);
-        case 192: return launch_w4<T, 192, 3, NF, 2>(x, M, N, K, group, packed, bias, y, err, st);
-        case 160: return launch_w4<T, 160, 3, NF, 2>(x, M, N, K, group, packed, bias, y, err, st);
-        default: return launch_w4<T, 256, 3, NF, 2>(x, M, N, K, group, packed, bias, y, err, st);
+        case 224: return launch_w4<T, 224, 3, NF, 2>(x, M, N, K, group, packed, bias, y, err, st, lo);
+        case 192: return launch_w4<T, 192, 3, NF, 2>(x, M, N, K, group, packed, bias, y, err, st, lo);
+        case 160: return launch_w4<T, 160, 3, NF, 2>(x, M, N, K, group, packed, bias, y, err, st, lo);
+        default: return launch_w4<T, 256, 3, NF, 2>(x, M, N, K, group, packed, bias, y, err, st, lo);
       }
     }
     // NF4 past M = 128: its 33 KB table leaves room for three 128-wide
     // stages only up to BT = 192, which measured slower than five 64-wide
     // stages at BT = 224 -- fall through
   }
-  if (M <= 16) return launch_w4<T, 16, 8, NF, 1>(x, M, N, K, group, packed, bias, y, err, st);
-  if (M <= 32) return launch_w4<T, 32, 8, NF, 1>(x, M, N, K, group, packed, bias, y, err, st);
-  if (M <= 64) return launch_w4<T, 64, 8, NF, 1>(x, M, N, K, group, packed, bias, y, err, st);
-  if (M <= 128) return launch_w4<T, 128, 8, NF, 1>(x, M, N, K, group, packed, bias, y, err, st);
+  if (M <= 32) return launch_w4<T, 32, 8, NF, 1>(x, M, N, K, group, packed, bias, y, err, st, lo);
+  if (M <= 64) return launch_w4<T, 64, 8, NF, 1>(x, M, N, K, group, packed, bias, y, err, st, lo);
+  if (M <= 128) return launch_w4<T, 128, 8, NF, 1>(x, M, N, K, group, packed, bias, y, err, st, lo);
   constexpr int S = NF ? 5 : 6;
   switch (pick_bt(M, N, {256, 224, 192}, false)) {
-    case 224: return launch_w4<T, 224, S, NF, 1>(x, M, N, K, group, packed, bias, y, err, st);
-    case 192: return launch_w4<T, 192, S, NF, 1>(x, M, N, K, group, packed, bias, y, err, st);
-    default: return launch_w4<T, 256, S, NF, 1>(x, M, N, K, group, packed, bias, y, err, st);
+    case 224: return launch_w4<T, 224, S, NF, 1>(x, M, N, K, group, packed, bias, y, err, st, lo);
+    case 192: return launch_w4<T, 192, S, NF, 1>(x, M, N, K, group, packed, bias, y, err, st, lo);
+    default: return launch_w4<T, 256, S, NF, 1>(x, M, N, K, group, packed, bias, y, err, st, lo);
   }
 }
 
@@ -969,7 +1260,7 @@ using namespace lq;
 
 extern "C" size_t lq_nf4_linear_packed_bytes(int64_t N, int64_t K) {
   if (N <= 0 || K <= 0) return 0;
-  return (size_t)(N * K / 2 + N * (K / kBK) * 4);
+  return (size_t)(gemv_codes_off(N, K, K / kBK) + N / 16 * (K / kBK) * gv_record_bytes(kBK));
 }
 
 extern "C" int lq_nf4_linear_pack(const void* codes, const void* scales, const void* q_scales,
@@ -1008,9 +1299,33 @@ extern "C" int lq_nf4_linear(const void* x, int act_dtype, int64_t M, int64_t N,
   return LQ_EDTYPE;
 }
 
+extern "C" int lq_nf4_linear_lora(const void* x, int act_dtype, int64_t M, int64_t N, int64_t K,
+                                  const void* packed, const float* bias, const void* lora_u,
+                                  const void* lora_b, int64_t rank, void* y, int* err, void* stream) {
+  int rc = check_shape(N, K, kBK);
+  if (rc) return rc;
+  LQ_REQUIRE(M >= 0 && M < (1LL << 31), LQ_EINVAL, "bad M");
+  if (M == 0) return LQ_OK;
+  LQ_REQUIRE(x && packed && y && lora_u && lora_b, LQ_EINVAL, "NULL pointer");
+  LQ_REQUIRE(aligned16(x) && aligned16(packed) && aligned16(lora_u) && aligned16(lora_b), LQ_EALIGN,
+             "x, packed, lora_u and lora_b must be 16-byte aligned");
+  LQ_REQUIRE(rank >= 2 && rank % 2 == 0 && rank <= (M <= 16 ? kBK : 16), LQ_ERANGE,
+             "fused LoRA needs an even rank <= %d at M = %lld (got %lld)", M <= 16 ? kBK : 16,
+             (long long)M, (long long)rank);
+  LoraArgs lo;
+  lo.u = lora_u;
+  lo.b = lora_b;
+  lo.r = (int)rank;
+  cudaStream_t st = as_stream(stream);
+  if (act_dtype == LQ_F16) return w4_dispatch<__half, true>(x, (int)M, (int)N, (int)K, kBK, packed, bias, y, err, st, lo);
+  if (act_dtype == LQ_BF16) return w4_dispatch<__nv_bfloat16, true>(x, (int)M, (int)N, (int)K, kBK, packed, bias, y, err, st, lo);
+  set_error("NF4 linear activations must be fp16 or bf16 (got dtype %d)", act_dtype);
+  return LQ_EDTYPE;
+}
+
 extern "C" size_t lq_w4a16_packed_bytes(int64_t N, int64_t K, int64_t group) {
   if (N <= 0 || K <= 0 || group <= 0) return 0;
-  return (size_t)(N * K / 2 + N * (K / group) * 4);
+  return (size_t)(gemv_codes_off(N, K, K / group) + N / 16 * (K / group) * gv_record_bytes(group));
 }
 
 extern "C" int lq_w4a16_pack(const int8_t* weight_int, const void* scale, const void* zero_point,

@@ -115,3 +115,145 @@ def base_linear(ql, x: torch.Tensor) -> torch.Tensor:
     if torch.is_grad_enabled() and (x.requires_grad or (ql.bias is not None and ql.bias.requires_grad)):
         return _BaseLinear.apply(x, ql.bias, ql)
     return _forward(ql, x, ql.bias)
+
+
+# ──────────────────────────────────────────────────────────────────────────────
+# LoRA fused into the base product (qlora.py:306-312) and merge_lora
+# (qlora.py:314-317)
+# ──────────────────────────────────────────────────────────────────────────────
+
+def lora_fusable(ql, x: torch.Tensor) -> bool:
+    """The kernels take the LoRA term for an even rank up to 16 (tensor-core
+    path, more than 16 tokens) or 64 (weight-streaming path, up to 16)."""
+    r = ql.rank
+    m = x.numel() // ql.in_features if ql.in_features else 0
+    return r >= 2 and r % 2 == 0 and r <= (64 if m <= 16 else 16)
+
+
+def _lora_u(ql, x2: torch.Tensor, lora_a: torch.Tensor) -> torch.Tensor:
+    """u = scaling * x @ lora_A^T in the activations' dtype, rows padded with
+    zeros to 64 columns (the kernels' row pitch); one cuBLAS call."""
+    r = ql.rank
+    u = torch.zeros(x2.shape[0], 64, dtype=x2.dtype, device=x2.device)
+    torch.addmm(u[:, :r], x2, lora_a.to(x2.dtype).t(), beta=0, alpha=ql.scaling, out=u[:, :r])
+    return u
+
+
+def _lora_forward(ql, x: torch.Tensor, lora_a, lora_b, bias) -> torch.Tensor:
+    packed = packed_operand(ql, x.dtype)
+    N, K = ql.out_features, ql.in_features
+    x2 = x.reshape(-1, K)
+    if not x2.is_contiguous() or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    M = x2.shape[0]
+    y = torch.empty(M, N, dtype=x.dtype, device=x.device)
+    b = None
+    if bias is not None:
+        b = bias.detach()
+        if b.dtype != torch.float32 or not b.is_contiguous():
+            b = b.float().contiguous()
+    u = _lora_u(ql, x2, lora_a.detach())
+    lb = lora_b.detach().to(x.dtype).contiguous()
+    _C.call("lq_nf4_linear_lora", x2.data_ptr(), _C.dt(x2), M, N, K, packed.data_ptr(), _C.ptr(b),
+            u.data_ptr(), lb.data_ptr(), ql.rank, y.data_ptr(), _err_flag(x.device).data_ptr(),
+            _C.stream_ptr(x2))
+    return y.reshape(*x.shape[:-1], N)
+
+
+class _QLoRAFused(torch.autograd.Function):
+    """y = x @ W_base^T + bias + scaling * (x @ A^T) @ B^T in one kernel; the
+    backward (frozen base) gives the gradients of x, lora_A, lora_B, bias."""
+
+    @staticmethod
+    def forward(ctx, x, lora_a, lora_b, bias, ql):
+        ctx.ql = ql
+        ctx.save_for_backward(x, lora_a, lora_b)
+        ctx.has_bias = bias is not None
+        return _lora_forward(ql, x, lora_a, lora_b, bias)
+
+    @staticmethod
+    def backward(ctx, gy):
+        x, lora_a, lora_b = ctx.saved_tensors
+        ql = ctx.ql
+        N, K, s = ql.out_features, ql.in_features, ql.scaling
+        g2 = gy.reshape(-1, N)
+        x2 = x.reshape(-1, K)
+        a = lora_a.to(gy.dtype)
+        b = lora_b.to(gy.dtype)
+        gbp = g2 @ b  # [M, r]
+        gx = ga = gb = gbias = None
+        if ctx.needs_input_grad[0]:
+            gx = (g2 @ ql._dequantize_base().to(gy.dtype) + (gbp @ a) * s).reshape(*gy.shape[:-1], K)
+        if ctx.needs_input_grad[1]:
+            ga = ((gbp * s).t() @ x2).to(lora_a.dtype)
+        if ctx.needs_input_grad[2]:
+            gb = ((g2.t() @ (x2 @ a.t())) * s).to(lora_b.dtype)
+        if ctx.has_bias and ctx.needs_input_grad[3]:
+            gbias = g2.float().sum(0)
+        return gx, ga, gb, gbias, None
+
+
+def qlora_forward(ql, x: torch.Tensor) -> torch.Tensor:
+    """QLoRALinear.forward for eligible x with the LoRA term fused."""
+    if (torch.is_grad_enabled() and (x.requires_grad or ql.lora_A.requires_grad
+                                     or ql.lora_B.requires_grad
+                                     or (ql.bias is not None and ql.bias.requires_grad))):
+        return _QLoRAFused.apply(x, ql.lora_A, ql.lora_B, ql.bias, ql)
+    return _lora_forward(ql, x, ql.lora_A, ql.lora_B, ql.bias)
+
+
+def merge_fusable(ql) -> bool:
+    a, b = ql.lora_A, ql.lora_B
+    return (ql.nf4_codes_packed.is_cuda and a.is_cuda and b.is_cuda and a.dtype == b.dtype
+            and a.dtype in (torch.float32, torch.float16, torch.bfloat16)
+            and 1 <= ql.rank <= 64 and ql.in_features % 8 == 0
+            and ql.nf4_codes_packed.data_ptr() % 4 == 0)
+
+
+def _merge(ql, lora_a, lora_b) -> torch.Tensor:
+    N, K = ql.out_features, ql.in_features
+    codes = ql.nf4_codes_packed
+    ref = ql.dq_q_scales if _use_dq(ql) else ql.nf4_scales
+    out_dtype = torch.promote_types(ref.dtype, lora_a.dtype)
+    out = torch.empty(N, K, dtype=out_dtype, device=codes.device)
+    a = lora_a.detach().contiguous()
+    b = lora_b.detach().contiguous()
+    if _use_dq(ql):
+        qs = ql.dq_q_scales.contiguous()
+        dq = ql.dq_scales.to(qs.dtype).contiguous()
+        _C.call("lq_nf4_merge_lora", codes.data_ptr(), N, K, ql.group_size, ql._dq_gs, None,
+                qs.data_ptr(), dq.data_ptr(), _C.dt(qs), a.data_ptr(), b.data_ptr(), _C.dt(a),
+                ql.rank, ql.scaling, out.data_ptr(), _C.dt(out), _C.stream_ptr(codes))
+    else:
+        s = ql.nf4_scales.contiguous()
+        _C.call("lq_nf4_merge_lora", codes.data_ptr(), N, K, ql.group_size, 0, s.data_ptr(), None,
+                None, _C.dt(s), a.data_ptr(), b.data_ptr(), _C.dt(a), ql.rank, ql.scaling,
+                out.data_ptr(), _C.dt(out), _C.stream_ptr(codes))
+    return out
+
+
+class _MergeLora(torch.autograd.Function):
+    """W_base + scaling * B @ A in one pass; gradients reach lora_A / lora_B."""
+
+    @staticmethod
+    def forward(ctx, lora_a, lora_b, ql):
+        ctx.save_for_backward(lora_a, lora_b)
+        ctx.scaling = ql.scaling
+        return _merge(ql, lora_a, lora_b)
+
+    @staticmethod
+    def backward(ctx, g):
+        a, b = ctx.saved_tensors
+        s = ctx.scaling
+        ga = gb = None
+        if ctx.needs_input_grad[0]:
+            ga = ((b.t().to(g.dtype) @ g) * s).to(a.dtype)
+        if ctx.needs_input_grad[1]:
+            gb = ((g @ a.t().to(g.dtype)) * s).to(b.dtype)
+        return ga, gb, None
+
+
+def merge_lora(ql) -> torch.Tensor:
+    if torch.is_grad_enabled() and (ql.lora_A.requires_grad or ql.lora_B.requires_grad):
+        return _MergeLora.apply(ql.lora_A, ql.lora_B, ql)
+    return _merge(ql, ql.lora_A, ql.lora_B)

@@ -283,6 +283,9 @@ class QLoRALinear(nn.Module):
         activations' dtype; other inputs follow the reference exactly."""
         from . import nf4_linear
         if nf4_linear.eligible(self, x):
+            if nf4_linear.lora_fusable(self, x):
+                # base product, bias and the rank-r LoRA term in one kernel
+                return nf4_linear.qlora_forward(self, x)
             out = nf4_linear.base_linear(self, x)
             lora = F.linear(F.linear(x, self.lora_A.to(x.dtype)), self.lora_B.to(x.dtype))
             return out + lora * self.scaling
@@ -292,7 +295,12 @@ class QLoRALinear(nn.Module):
         return out
 
     def merge_lora(self) -> torch.Tensor:
-        """W_eff = W_base + scaling * B @ A (qlora.py:314-317)."""
+        """W_eff = W_base + scaling * B @ A (qlora.py:314-317): one kernel that
+        dequantizes the base and adds the rank-r update (in the promoted dtype,
+        each op rounded as torch does); gradients still reach lora_A / lora_B."""
+        from . import nf4_linear
+        if nf4_linear.merge_fusable(self):
+            return nf4_linear.merge_lora(self)
         w_base = self._dequantize_base()
         return w_base + self.scaling * (self.lora_B @ self.lora_A)
 

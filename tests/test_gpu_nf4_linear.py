@@ -122,3 +122,83 @@ def test_fp32_path_is_the_reference_computation(L):
     ref = torch.nn.functional.linear(x, wb, ql.bias) + torch.nn.functional.linear(
         torch.nn.functional.linear(x, ql.lora_A), ql.lora_B) * ql.scaling
     assert torch.equal(ql(x), ref)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("M,rank", [(1, 16), (5, 64), (16, 32), (17, 16), (200, 2), (1024, 16),
+                                    (300, 24), (64, 5)])
+def test_lora_fused_and_fallback(L, dtype, M, rank):
+    """The LoRA term inside the base kernel (even rank <= 16 above 16 tokens,
+    <= 64 up to 16) and the unfused path for other ranks give the fp32
+    reference within the same bound."""
+    from llm_quant_b200 import nf4_linear
+    ql, g = _module(L, 256, 1024, dtype, 64, True, seed=M * 7 + rank, rank=rank)
+    with torch.no_grad():
+        ql.lora_A.copy_(torch.randn(rank, 1024, generator=g) * 0.05)
+    x = torch.randn(M, 1024, generator=g).to(dtype).cuda()
+    fused = nf4_linear.lora_fusable(ql, x)
+    assert fused == (rank % 2 == 0 and rank <= (64 if M <= 16 else 16))
+    with torch.no_grad():
+        y = ql(x)
+    ref = _reference(ql, x)
+    _check(y, ref)
+    # the LoRA term is really in the output: without it the error is large
+    base = x.float() @ ql._dequantize_base().float().T + ql.bias.float()
+    assert (y.float() - base).abs().max().item() > 0.1 * (ref - base).abs().max().item()
+
+
+def test_lora_fused_config_shape(L):
+    """Linear(4096, 14336) NF4 base, rank 16, M = 1024 (the qlora_linear bench shape)."""
+    ql, g = _module(L, 14336, 4096, torch.bfloat16, 64, True, seed=99, rank=16)
+    with torch.no_grad():
+        ql.lora_A.copy_(torch.randn(16, 4096, generator=g) * 0.02)
+    x = torch.randn(1024, 4096, generator=g).to(torch.bfloat16).cuda()
+    with torch.no_grad():
+        y = ql(x)
+    _check(y, _reference(ql, x))
+
+
+@pytest.mark.parametrize("sdtype,pdtype", [(torch.bfloat16, torch.float32), (torch.float16, torch.float16),
+                                           (torch.bfloat16, torch.bfloat16), (torch.float32, torch.float32)])
+@pytest.mark.parametrize("dq", [True, False])
+@pytest.mark.parametrize("rank", [1, 16, 64])
+def test_merge_lora_one_pass(L, sdtype, pdtype, dq, rank):
+    """merge_lora = _dequantize_base() + scaling * lora_B @ lora_A, in the
+    promoted dtype: the base part bit-exact, the rank-r product to float
+    rounding of its summation order."""
+    g = torch.Generator().manual_seed(rank + int(dq))
+    N, K = 384, 640
+    w = (torch.randn(N, K, generator=g) * 0.02).to(sdtype).cuda()
+    ql = L.QLoRALinear(K, N, rank=rank, group_size=64, double_quant=dq).cuda()
+    ql.pack_base(w)
+    with torch.no_grad():
+        ql.lora_A.copy_(torch.randn(rank, K, generator=g) * 0.05)
+        ql.lora_B.copy_(torch.randn(N, rank, generator=g) * 0.05)
+    ql.lora_A.data = ql.lora_A.data.to(pdtype)
+    ql.lora_B.data = ql.lora_B.data.to(pdtype)
+    from llm_quant_b200 import nf4_linear
+    assert nf4_linear.merge_fusable(ql)
+    with torch.no_grad():
+        m = ql.merge_lora()
+        ref = ql._dequantize_base() + ql.scaling * (ql.lora_B @ ql.lora_A)
+    assert m.dtype == ref.dtype == torch.promote_types(sdtype, pdtype)
+    tol = 1e-5 if m.dtype == torch.float32 else 1e-2
+    torch.testing.assert_close(m.float(), ref.float(), rtol=tol, atol=tol * ref.abs().max().item())
+    with torch.no_grad():  # a zero LoRA update leaves exactly the dequantized base
+        ql.lora_B.zero_()
+        assert torch.equal(ql.merge_lora().to(ref.dtype), ql._dequantize_base().to(ref.dtype))
+
+
+def test_merge_lora_gradients(L):
+    g = torch.Generator().manual_seed(8)
+    w = (torch.randn(128, 256, generator=g) * 0.02).to(torch.bfloat16).cuda()
+    ql = L.QLoRALinear(256, 128, rank=8, group_size=64).cuda()
+    ql.pack_base(w)
+    with torch.no_grad():
+        ql.lora_B.copy_(torch.randn(128, 8, generator=g) * 0.05)
+    m = ql.merge_lora()
+    gm = torch.randn(m.shape, generator=g).cuda()
+    m.backward(gm)
+    a, b = ql.lora_A.detach(), ql.lora_B.detach()
+    torch.testing.assert_close(ql.lora_A.grad, ql.scaling * b.t() @ gm, rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(ql.lora_B.grad, ql.scaling * gm @ a.t(), rtol=1e-4, atol=1e-4)
