@@ -75,17 +75,58 @@ struct GroupArgs {
 // Per-element output of the fused modes.  A zero point of +0.0 (symmetric
 // quantization) is skipped: t + 0 only turns a -0.0 into +0.0, which ste_round
 // and the code casts treat alike, and q - 0 is exact for integer q.
-template <typename T, int MODE>
-__device__ __forceinline__ float apply_q(float v, float scale, float zp, float qmin, float qmax,
-                                         bool zp0) {
-  float t = tdiv<T>(v, scale);
-  if (!zp0) t = tadd<T>(t, zp);
+// The quotient stage of apply_q, t = round_T(x / scale) (+ zp), without an
+// IEEE division per element where that provably gives the same result, from
+// the group's reciprocal rcp = rcp_rn(scale):
+//   bf16: round_bf16(x * rcp) == round_bf16(fl32(x / scale)) whenever the
+//         product is a normal fp32 number (both operands have 8-bit
+//         significands: their quotient is exactly representable or at least
+//         2^-17 away from every bf16 rounding midpoint, x * rcp is within
+//         2^-23 of it); zero, subnormal and non-finite products divide.
+//   fp32, when only rint(t + zp) reaches the outputs (integer codes, and fake
+//         quantization through ste_round, whose zero is +0.0 either way; not
+//         float codes, which keep the sign of a zero): t0 = x * rcp is within 2^-22 |t0| of fl32(x / scale),
+//         so t0 + zp is within 2^-22 |t0| + 2^-23 |t| of the reference's
+//         t; when it lies more than W = 2^-20 (|t0| + |t|) from every
+//         half-integer, both round to the same integer and t0 + zp stands in
+//         for t.  Otherwise (ties, values near a tie, non-finite) it divides.
+//   fp16: divides.
+template <typename T, bool RINT_ONLY>
+__device__ __forceinline__ float quotient_zp(float v, float scale, float rcp, float zp, bool zp0) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    const float p = __fmul_rn(v, rcp);
+    float t = (fabsf(p) >= 1.17549435e-38f || v == 0.0f) ? Ty<T>::round(p) : tdiv<T>(v, scale);
+    return zp0 ? t : tadd<T>(t, zp);
+  } else if constexpr (std::is_same<T, float>::value && RINT_ONLY) {
+    const float t0 = __fmul_rn(v, rcp);
+    const float t = zp0 ? t0 : __fadd_rn(t0, zp);
+    const float w = __fmul_rn(__fadd_rn(fabsf(t0), fabsf(t)), 9.5367431640625e-07f);  // 2^-20
+    if (__fsub_rn(0.5f, fabsf(__fsub_rn(t, rintf(t)))) > w) return t;
+    const float e = tdiv<T>(v, scale);
+    return zp0 ? e : tadd<T>(e, zp);
+  } else {
+    const float t = tdiv<T>(v, scale);
+    return zp0 ? t : tadd<T>(t, zp);
+  }
+}
+
+template <typename T, int MODE, bool RINT_ONLY>
+__device__ __forceinline__ float apply_q(float v, float scale, float rcp, float zp, float qmin,
+                                         float qmax, bool zp0) {
+  const float t = quotient_zp<T, RINT_ONLY>(v, scale, rcp, zp, zp0);
   if constexpr (MODE == MODE_FAKE) {
     float q = tclamp_t<T>(tste(t), qmin, qmax);
     return tmul<T>(zp0 ? q : tsub<T>(q, zp), scale);
   } else {
     return tclamp_t<T>(trint(t), qmin, qmax);
   }
+}
+
+// Outputs that depend on the quotient only through its rint: fake
+// quantization and integer codes.
+template <int MODE, typename OutT, typename T>
+__host__ __device__ constexpr bool rint_only() {
+  return MODE == MODE_FAKE || !std::is_same<OutT, T>::value;
 }
 
 // The symmetric skip is exact for fake quantization and integer codes; a
@@ -148,13 +189,14 @@ struct Tile {
                                        const GroupArgs& a, int t, int tps, float scale,
                                        float zp) {
     OutT* base = out + a.out_row(row) * a.cols + gcol0;
+    const float rcp = __frcp_rn(scale);
 #pragma unroll
     for (int k = 0; k < NVT; ++k) {
       if (!(inb & (1u << k))) continue;
       int64_t e = (int64_t)(k * tps + t) * V;
       float o[V];
 #pragma unroll
-      for (int i = 0; i < V; ++i) o[i] = apply_q<T, MODE>(v[k * V + i], scale, zp, a.qmin, a.qmax, zp0_ok<MODE, OutT, T>(a));
+      for (int i = 0; i < V; ++i) o[i] = apply_q<T, MODE, rint_only<MODE, OutT, T>()>(v[k * V + i], scale, rcp, zp, a.qmin, a.qmax, zp0_ok<MODE, OutT, T>(a));
       if constexpr (VEC) {
         store_vec<OutT, T, V>(base + e, o);
       } else {
@@ -267,8 +309,9 @@ __global__ void __launch_bounds__(1024) group_stream_kernel(const T* __restrict_
     }
     if constexpr (MODE != MODE_QPARAMS) {
       OutT* ob = out + a.out_row(row) * a.cols + gcol0;
+      const float rcp = __frcp_rn(scale);
       for (int64_t e = threadIdx.x; e < a.G && gcol0 + e < a.cols; e += blockDim.x)
-        ob[e] = Store<OutT, T>::cv(apply_q<T, MODE>(Ty<T>::to_f(base[e]), scale, zp, a.qmin, a.qmax, zp0_ok<MODE, OutT, T>(a)));
+        ob[e] = Store<OutT, T>::cv(apply_q<T, MODE, rint_only<MODE, OutT, T>()>(Ty<T>::to_f(base[e]), scale, rcp, zp, a.qmin, a.qmax, zp0_ok<MODE, OutT, T>(a)));
     }
   }
 }

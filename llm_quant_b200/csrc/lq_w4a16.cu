@@ -598,8 +598,9 @@ __host__ __device__ inline int64_t gemv_codes_off(int64_t N, int64_t K, int64_t 
 }
 // GEMV record of one (16-row slab, group): the group's K steps of codes (512
 // bytes each, lane-major) followed by the slab's 16 (zero, scale) pairs
-// (64 bytes).  Records of a slab are contiguous in K, so a warp's share of
-// the K range is one run of memory.  (NF4: 64-wide groups.)
+// (64 bytes).  Records are stored slab-major ([slab][group]): a slab's whole
+// K range is one run of memory, fetched in a few large bulk copies.  (NF4:
+// 64-wide groups.)
 __host__ __device__ inline int64_t gv_record_bytes(int64_t group) { return group / kBK * 512 + 64; }
 
 // word i (0..3, a compile-time constant after unrolling) of v
@@ -609,7 +610,6 @@ __device__ __forceinline__ uint32_t word_of(const uint4& v, int i) {
 
 template <typename T> struct GvInt4;
 template <> struct GvInt4<__half> {
-  static constexpr uint32_t one = 0x3C003C00u;  // fp16 1.0 pair
   // fragments a0..a3 of one code word
   __device__ __forceinline__ static void frag(uint32_t w, uint32_t (&a)[4]) {
     const uint32_t w8 = w >> 8;
@@ -625,7 +625,6 @@ template <> struct GvInt4<__half> {
   }
 };
 template <> struct GvInt4<__nv_bfloat16> {
-  static constexpr uint32_t one = 0x3F803F80u;  // bf16 1.0 pair
   __device__ __forceinline__ static void frag(uint32_t w, uint32_t (&a)[4]) {
     a[0] = (w & 0x000F000Fu) | 0x43004300u;   // 128 + q
     a[1] = ((w >> 4) & 0x000F000Fu) | 0x43004300u;
@@ -638,233 +637,412 @@ template <> struct GvInt4<__nv_bfloat16> {
   }
 };
 
-// Stage of the GEMV ring: one group of the warp's K range -- its R16
-// records (codes + pairs) and XR token rows of its activations (2G bytes
-// each, pitch 2G + 16: the pad puts the 8 lanes of each quarter-warp on
-// distinct banks).  Sizes depend on the group size G (64 .. 256).
-__host__ __device__ inline int gv_xpitch(int G) { return 2 * G + 16; }
-__host__ __device__ inline int gv_stage_bytes(int R16, int XR, int G) {
-  return R16 * (int)gv_record_bytes(G) + XR * gv_xpitch(G);
+// Set a kernel's dynamic shared-memory limit once per device.
+template <typename Kern>
+int set_smem_once(Kern kern, int smem_bytes, std::atomic<uint64_t>& done) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);  // one bit per device
+  if (!(done.load() & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+    LQ_REQUIRE(e == cudaSuccess, LQ_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    done.fetch_or(bit);
+  }
+  return LQ_OK;
 }
-constexpr int kGvMaxDepth = 4;
 
-template <typename T, bool NF, int R16, int NT, int XR, int WARPS>
-__global__ void __launch_bounds__(32 * WARPS, 4) w4a16_gemv_kernel(const T* __restrict__ x,
+// Persistent streaming GEMV.  One block per SM owns the slabs b, b + grid,
+// ...; their records stream through a STAGES-deep shared-memory ring in
+// chunks of CG groups: one bulk copy of ~32 KB per chunk, issued by a
+// producer warp that refills a slot once every consumer warp has released
+// it (full / empty mbarriers per slot), so up to ~200 KB per SM are in
+// flight.  The 16 consumer warps split each chunk's groups and never wait
+// for one another: a warp stores its share of a slab (fp32, in one of two
+// buffers by slab parity) and the last of the 16 to do so adds the shares
+// and writes the slab's outputs.  With XS the activations (M rows of K halves, at most
+// 136 KB) are copied once into shared memory; otherwise the lanes read them
+// from global memory (L2).  For INT4 the block first forms S[group][token] =
+// the group's activation sums (fp32), which fold the zero points: a group adds
+// s (f D - (o + z) S) to its rows' outputs, D the MMA sum of the (o + q)
+// fragments.  The LoRA term is one more MMA pass per slab, lora_B's rows as A
+// and u as B.
+constexpr int kGvWarps = 16;      // consumer warps; one producer warp more
+constexpr int kGvMaxStages = 16;
+constexpr int kGvSmemMax = 227 * 1024;
+constexpr int kGvXsMax = 136 * 1024;
+__host__ __device__ inline int gv_xpitch_bytes(int K) { return 2 * K + 16; }
+
+struct GvArgs {
+  int G, cg, stages;
+};
+
+template <typename T, bool NF, int NT, bool XS, int SPG>
+__global__ void __launch_bounds__(32 * (kGvWarps + 1), 1) w4a16_gemv_kernel(const T* __restrict__ x,
                                                     const uint8_t* __restrict__ packed,
                                                     const float* __restrict__ bias,
-                                                    T* __restrict__ y, W4Args a, int G, int depth,
-                                                    int* err, const T* __restrict__ lora_u,
+                                                    T* __restrict__ y, W4Args a, GvArgs v, int* err,
+                                                    const T* __restrict__ lora_u,
                                                     const T* __restrict__ lora_b, int lora_r) {
-  const int rb = (int)gv_record_bytes(G), xp = gv_xpitch(G);
-  const int xoff0 = R16 * rb, stage = gv_stage_bytes(R16, XR, G);
-  const int spg = G / kBK;  // K steps per group
+  constexpr int CH = (NT == 2 && !XS) ? 1 : 2;  // MMA chains per group and B tile
+  constexpr int GP = (NF && NT == 2) ? 1 : 2;    // groups per pass
+  const int G = v.G, cg = v.cg, stages = v.stages;
+  const int rb = (int)gv_record_bytes(G);
+  const int spg = SPG > 0 ? SPG : G / kBK;  // K steps per group
+  const int n_grp = a.K / G;
+  const int n_chunk = (n_grp + cg - 1) / cg;
+  const int n_slab = a.N / 16;
+  const int chunk_bytes = cg * rb;
   extern __shared__ __align__(128) uint8_t gv_smem[];
-  uint32_t* lut = reinterpret_cast<uint32_t*>(gv_smem);                                    // NF: pair table
-  float* red = reinterpret_cast<float*>(gv_smem + (NF ? kPairLut16Words * 4 + 1024 : 0));  // [warps][R16][NT][32][4]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(red + WARPS * R16 * NT * 128);             // [warps][kGvMaxDepth]
-  uint8_t* ring = reinterpret_cast<uint8_t*>(bars + WARPS * kGvMaxDepth);
-  __shared__ int s_err;
+  uint8_t* p = gv_smem;
+  uint32_t* lut = reinterpret_cast<uint32_t*>(p);  // NF: pair table (+1 KB build space)
+  if (NF) p += kPairLut16Words * 4 + 1024;
+  float* red = reinterpret_cast<float*>(p);  // [2][warps][NT * 128] slab shares, fragment order
+  p += 2 * kGvWarps * NT * 512;
+  int* cnt = reinterpret_cast<int*>(p);  // [2] warps done with the buffer's slab
+  int* gen = cnt + 2;                    // [2] slabs written out of the buffer
+  p += 128;
+  uint64_t* full = reinterpret_cast<uint64_t*>(p);  // [kGvMaxStages]
+  uint64_t* empty = full + kGvMaxStages;            // [kGvMaxStages]
+  uint64_t* xbar = empty + kGvMaxStages;
+  p += 2 * kGvMaxStages * 8 + 128;
+  float* S = reinterpret_cast<float*>(p);  // INT4: [n_grp][16 tokens]
+  if (!NF) p += ((n_grp * 64 + 127) / 128) * 128;
+  uint8_t* xs = p;  // XS: [M][K] halves at pitch 2 K + 16 bytes
+  if (XS) p += ((a.M * gv_xpitch_bytes(a.K) + 127) / 128) * 128;
+  uint8_t* ring = p;  // [stages][chunk_bytes]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, c = lane & 3;
-  if (threadIdx.x == 0) s_err = 0;
-  if constexpr (NF) build_pair_lut16<T>(lut, reinterpret_cast<uint32_t*>(gv_smem + kPairLut16Words * 4));
-  uint64_t* bar = bars + warp * kGvMaxDepth;
-  if (lane == 0) {
-    for (int d = 0; d < depth; ++d) mbar_init(&bar[d], 1);
+  const bool producer = warp == kGvWarps;
+  const uint8_t* recs = packed + gemv_codes_off(a.N, a.K, NF ? a.n_kb : a.n_groups);
+  // this block's units, in order: (slab blockIdx.x + i grid, chunk j) = unit i n_chunk + j
+  const int my_slabs = blockIdx.x < n_slab ? (n_slab - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int n_units = my_slabs * n_chunk;
+  auto issue = [&](int u) {
+    const int slab = blockIdx.x + (u / n_chunk) * gridDim.x, ch = u % n_chunk;
+    const uint32_t nb = (uint32_t)(min(cg, n_grp - ch * cg) * rb);
+    const int sl = u % stages;
+    mbar_expect_tx(&full[sl], nb);
+    bulk_load(ring + (size_t)sl * chunk_bytes, recs + ((size_t)slab * n_grp + (size_t)ch * cg) * rb, nb, &full[sl]);
+  };
+  if (threadIdx.x < 4) cnt[threadIdx.x] = 0;  // and gen
+  if (producer && lane == 0) {
+    for (int i = 0; i < stages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kGvWarps);
+    }
+    mbar_init(xbar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    if (XS) {
+      mbar_expect_tx(xbar, (uint32_t)(a.M * a.K * 2));
+      for (int row = 0; row < a.M; ++row)
+        bulk_load(xs + row * gv_xpitch_bytes(a.K), x + (size_t)row * a.K, (uint32_t)(a.K * 2), xbar);
+    }
+    for (int u = 0; u < stages && u < n_units; ++u) issue(u);
+  }
+  if constexpr (NF) build_pair_lut16<T>(lut, reinterpret_cast<uint32_t*>(gv_smem + kPairLut16Words * 4));
+  __syncthreads();
+  bool ok = XS ? mbar_wait(xbar, 0) : true;
+  if constexpr (!NF) {
+    // group sums of the activations: eight lanes per (group, token), each
+    // adding G / 8 halves, then three shuffles (tokens past M are not read)
+    const int n_items = n_grp * a.M, part = threadIdx.x & 7, per = G / 8;
+    for (int base = 0; base < n_items; base += blockDim.x / 8) {
+      const int it = base + (int)(threadIdx.x >> 3);
+      float sum = 0.0f;
+      if (it < n_items && ok) {
+        const int gi = it / a.M, tok = it % a.M;
+        const T* xr = XS ? reinterpret_cast<const T*>(xs + tok * gv_xpitch_bytes(a.K)) + gi * G + part * per
+                         : x + (size_t)tok * a.K + gi * G + part * per;
+        for (int k = 0; k < per; k += 8) {
+          const uint4 q = XS ? *reinterpret_cast<const uint4*>(xr + k) : __ldg(reinterpret_cast<const uint4*>(xr + k));
+          const T* h = reinterpret_cast<const T*>(&q);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) sum += Ty<T>::to_f(h[e]);
+        }
+      }
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+      if (it < n_items && part == 0) S[(it / a.M) * 16 + it % a.M] = sum;
+    }
   }
   __syncthreads();
-  uint8_t* my = ring + warp * depth * stage;
-  const int slab0 = blockIdx.x * R16;  // first 16-row slab of the block
-  const int r0 = slab0 * 16;           // first weight row
-  const int n_grp = a.K / G;
-  const uint8_t* recs = packed + gemv_codes_off(a.N, a.K, NF ? a.n_kb : a.n_groups) + (size_t)slab0 * n_grp * rb;
-  // this warp's contiguous share of the groups
-  const int per = (n_grp + WARPS - 1) / WARPS;
-  const int g0 = warp * per;
-  const int n_my = max(0, min(n_grp, g0 + per) - g0);
-  const uint32_t stage_tx = (uint32_t)(R16 * rb + a.M * 2 * G);
-  // group i of the warp into slot i % depth: lane 0 issues every copy (one
-  // per slab, one per token row)
-  auto issue = [&](int i) {
-    const int sl = i % depth, grp = g0 + i;
-    uint8_t* dst = my + sl * stage;
+  if (producer) {
+    // refill slot u % stages for unit u once the 16 consumers released unit u - stages
+    int u = stages;
     if (lane == 0) {
-      mbar_expect_tx(&bar[sl], stage_tx);
-#pragma unroll
-      for (int r = 0; r < R16; ++r)
-        bulk_load(dst + r * rb, recs + ((size_t)r * n_grp + grp) * rb, (uint32_t)rb, &bar[sl]);
-      for (int row = 0; row < a.M; ++row)
-        bulk_load(dst + xoff0 + row * xp, x + (size_t)row * a.K + (size_t)grp * G, (uint32_t)(2 * G), &bar[sl]);
+      for (; ok && u < n_units; ++u) {
+        if (!mbar_wait(&empty[u % stages], (uint32_t)(u / stages - 1) & 1u)) {
+          atomicExch(err, 5);
+          break;
+        }
+        issue(u);
+      }
+      // before the block exits, every copy it issued has landed (bounded)
+      const int issued = min(u, n_units);
+      for (int w = max(0, issued - stages); w < issued; ++w) mbar_wait(&full[w % stages], (uint32_t)(w / stages) & 1u);
     }
-  };
-  for (int i = 0; i < depth && i < n_my; ++i) issue(i);
-  // activations of lane (g, c), B tile j: token 8 j + g (token 0 past M:
-  // those columns are never stored), halves 16 c .. 16 c + 15 of each step
-  int xoff[NT];
+    return;
+  }
+  const int g = lane >> 2, c = lane & 3;
+  // activations of lane (g, c) in B tile j: token 8 j + g (token 0 for
+  // columns past M, which are never stored), halves 16 c .. 16 c + 15 of each
+  // 64-wide step
+  const uint32_t xs_a = smem_u32(xs), ring_a = smem_u32(ring), lut_a = smem_u32(lut);
+  uint32_t xoff[NT];  // XS: byte offset in the shared copy
+  int64_t xoffg[NT];  // else: byte offset in x
 #pragma unroll
-  for (int j = 0; j < NT; ++j) xoff[j] = xoff0 + (8 * j + g < a.M ? 8 * j + g : 0) * xp + 32 * c;
-  // dsum / ssum: MMA sums of the current group, split by the parity of the
-  // 16-wide k tile so that consecutive MMAs are independent
-  float acc[R16][NT][4];
-#pragma unroll
-  for (int r = 0; r < R16; ++r)
-#pragma unroll
-    for (int j = 0; j < NT; ++j)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) acc[r][j][e] = 0.0f;
+  for (int j = 0; j < NT; ++j) {
+    const int tok = 8 * j + g < a.M ? 8 * j + g : 0;
+    xoff[j] = (uint32_t)(tok * gv_xpitch_bytes(a.K) + 32 * c);
+    xoffg[j] = (int64_t)tok * a.K * 2 + 32 * c;
+  }
   const uint32_t copy4 = (uint32_t)(lane & 15) << 2;
-  const char* lb = reinterpret_cast<const char*>(lut);
-  const uint32_t ones[4] = {GvInt4<T>::one, GvInt4<T>::one, GvInt4<T>::one, GvInt4<T>::one};
-  int i = 0;
-  for (; i < n_my; ++i) {
-    const int sl = i % depth;
-    const uint8_t* st = my + sl * stage;
-    if (!mbar_wait_warp(&bar[sl], (uint32_t)(i / depth) & 1u)) break;
-    float dsum[R16][NT][2][4], ssum[NT][2][4];
+  float acc[NT][4];
 #pragma unroll
-    for (int j = 0; j < NT; ++j)
+  for (int j = 0; j < NT; ++j)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        ssum[j][0][e] = ssum[j][1][e] = 0.0f;
+    for (int e = 0; e < 4; ++e) acc[j][e] = 0.0f;
+  int sl = 0, ch = 0, si = 0;
+  uint32_t par = 0;
+  for (int u = 0; u < n_units; ++u) {
+    if (!(ok && mbar_wait(&full[sl], par))) {
+      if (lane == 0) atomicExch(err, 5);
+      break;
+    }
+    const int ng = min(cg, n_grp - ch * cg);
+    const uint32_t st = ring_a + (uint32_t)(sl * chunk_bytes);
+    // warp w takes the chunk's groups w, w + 16, ..., GP at a time (gl and
+    // gl + 16): their MMA chains are independent, so their latencies overlap
+    for (int gl = warp; gl < ng; gl += GP * kGvWarps) {
+      const bool two = GP == 2 && gl + kGvWarps < ng;
+      const int grp[2] = {ch * cg + gl, ch * cg + gl + (two ? kGvWarps : 0)};
+      const uint32_t rec[2] = {st + (uint32_t)(gl * rb), st + (uint32_t)((gl + (two ? kGvWarps : 0)) * rb)};
+      float dc[GP][NT][CH][4];
 #pragma unroll
-        for (int r = 0; r < R16; ++r) dsum[r][j][0][e] = dsum[r][j][1][e] = 0.0f;
-      }
-    for (int ks = 0; ks < spg; ++ks) {
-      uint4 xv[NT][2], cw[R16];
+      for (int q = 0; q < GP; ++q)
 #pragma unroll
-      for (int j = 0; j < NT; ++j) {
-        xv[j][0] = *reinterpret_cast<const uint4*>(st + xoff[j] + ks * 128);
-        xv[j][1] = *reinterpret_cast<const uint4*>(st + xoff[j] + ks * 128 + 16);
-      }
+        for (int j = 0; j < NT; ++j)
 #pragma unroll
-      for (int r = 0; r < R16; ++r) cw[r] = *reinterpret_cast<const uint4*>(st + r * rb + ks * 512 + lane * 16);
+          for (int h = 0; h < CH; ++h)
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
+            for (int e = 0; e < 4; ++e) dc[q][j][h][e] = 0.0f;
 #pragma unroll
-        for (int r = 0; r < R16; ++r) {
-          uint32_t af[4];
-          if constexpr (NF) {
+      for (int ks = 0; ks < (SPG > 0 ? SPG : 1); ++ks)
+        for (int kr = ks; kr < (SPG > 0 ? ks + 1 : spg); ++kr) {
+          uint4 cw[GP];
+          uint4 xv[GP][NT][2];
 #pragma unroll
-            for (int b = 0; b < 4; ++b)
-              af[b] = *reinterpret_cast<const uint32_t*>(lb + pair_lut16_off(word_of(cw[r], t), b, copy4));
-          } else {
-            GvInt4<T>::frag(word_of(cw[r], t), af);
+          for (int q = 0; q < GP; ++q) {
+            cw[q] = lds_v4(rec[q] + kr * 512 + lane * 16);
+            const uint32_t xk = (uint32_t)(grp[q] * G + kr * kBK) * 2u;
+#pragma unroll
+            for (int j = 0; j < NT; ++j) {
+              if constexpr (XS) {
+                xv[q][j][0] = lds_v4(xs_a + xoff[j] + xk);
+                xv[q][j][1] = lds_v4(xs_a + xoff[j] + xk + 16);
+              } else {
+                const uint4* xp = reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(x) + xoffg[j] + xk);
+                xv[q][j][0] = __ldg(xp);
+                xv[q][j][1] = __ldg(xp + 1);
+              }
+            }
           }
 #pragma unroll
-          for (int j = 0; j < NT; ++j)
-            MmaOp<T>::mma(dsum[r][j][t & 1], af, word_of(xv[j][t >> 1], 2 * (t & 1)),
-                          word_of(xv[j][t >> 1], 2 * (t & 1) + 1));
-        }
-        if constexpr (!NF) {
+          for (int t = 0; t < 4; ++t)
 #pragma unroll
-          for (int j = 0; j < NT; ++j)
-            MmaOp<T>::mma(ssum[j][t & 1], ones, word_of(xv[j][t >> 1], 2 * (t & 1)),
-                          word_of(xv[j][t >> 1], 2 * (t & 1) + 1));
+            for (int q = 0; q < GP; ++q) {
+              uint32_t af[4];
+              if constexpr (NF) {
+#pragma unroll
+                for (int b = 0; b < 4; ++b) af[b] = lds_b32(lut_a + pair_lut16_off(word_of(cw[q], t), b, copy4));
+              } else {
+                GvInt4<T>::frag(word_of(cw[q], t), af);
+              }
+#pragma unroll
+              for (int j = 0; j < NT; ++j)
+                MmaOp<T>::mma(dc[q][j][t % CH], af, word_of(xv[q][j][t >> 1], 2 * (t & 1)),
+                              word_of(xv[q][j][t >> 1], 2 * (t & 1) + 1));
+            }
+        }
+#pragma unroll
+      for (int q = 0; q < GP; ++q) {
+        if (q == 1 && !two) break;
+        float d[NT][4];
+#pragma unroll
+        for (int j = 0; j < NT; ++j)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float sum = dc[q][j][0][e];
+#pragma unroll
+            for (int h = 1; h < CH; ++h) sum += dc[q][j][h][e];
+            d[j][e] = sum;
+          }
+        // fold the group in: the slab's 16 (zero, scale) pairs follow its codes
+        const uint32_t zs0 = lds_b32(rec[q] + spg * 512 + 4 * g);
+        const uint32_t zs1 = lds_b32(rec[q] + spg * 512 + 4 * (g + 8));
+        const float s0 = MmaOp<T>::hi_f(zs0), s1 = MmaOp<T>::hi_f(zs1);
+        if constexpr (NF) {
+#pragma unroll
+          for (int j = 0; j < NT; ++j) {
+            acc[j][0] = fmaf(d[j][0], s0, acc[j][0]);
+            acc[j][1] = fmaf(d[j][1], s0, acc[j][1]);
+            acc[j][2] = fmaf(d[j][2], s1, acc[j][2]);
+            acc[j][3] = fmaf(d[j][3], s1, acc[j][3]);
+          }
+        } else {
+          float f0, c0, f1, c1;
+          GvInt4<T>::fold(MmaOp<T>::lo_f(zs0), false, f0, c0);
+          GvInt4<T>::fold(MmaOp<T>::lo_f(zs1), true, f1, c1);
+          const float sf0 = s0 * f0, sc0 = s0 * c0, sf1 = s1 * f1, sc1 = s1 * c1;
+#pragma unroll
+          for (int j = 0; j < NT; ++j) {
+            // rows g, g + 8 x tokens 8 j + 2 c, 8 j + 2 c + 1
+            const float2 sv = *reinterpret_cast<const float2*>(&S[grp[q] * 16 + 8 * j + 2 * c]);
+            acc[j][0] = fmaf(d[j][0], sf0, fmaf(sv.x, sc0, acc[j][0]));
+            acc[j][1] = fmaf(d[j][1], sf0, fmaf(sv.y, sc0, acc[j][1]));
+            acc[j][2] = fmaf(d[j][2], sf1, fmaf(sv.x, sc1, acc[j][2]));
+            acc[j][3] = fmaf(d[j][3], sf1, fmaf(sv.y, sc1, acc[j][3]));
+          }
         }
       }
     }
-    // fold the group in: its 16 pairs follow the codes of each record
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[sl]);  // the slot may be refilled
+    if (ch == n_chunk - 1) {
+      const int slab = blockIdx.x + si * gridDim.x;
+      if (warp == 0 && lora_r > 0) {
+        // LoRA: + u[tok] . lora_B[row], 16-wide rank tiles (columns past r read as 0)
+        for (int k0 = 0; k0 < lora_r; k0 += 16) {
+          uint32_t af[4];
 #pragma unroll
-    for (int r = 0; r < R16; ++r) {
-      const uint32_t zs0 = *reinterpret_cast<const uint32_t*>(st + r * rb + spg * 512 + 4 * g);
-      const uint32_t zs1 = *reinterpret_cast<const uint32_t*>(st + r * rb + spg * 512 + 4 * (g + 8));
-      const float s0 = MmaOp<T>::hi_f(zs0), s1 = MmaOp<T>::hi_f(zs1);
-      if constexpr (NF) {
+          for (int q = 0; q < 4; ++q) {
+            const int row = slab * 16 + g + (q & 1) * 8, col = k0 + 2 * c + (q >> 1) * 8;
+            af[q] = col < lora_r ? *reinterpret_cast<const uint32_t*>(lora_b + (size_t)row * lora_r + col) : 0u;
+          }
 #pragma unroll
-        for (int j = 0; j < NT; ++j) {
-          acc[r][j][0] = fmaf(dsum[r][j][0][0] + dsum[r][j][1][0], s0, acc[r][j][0]);
-          acc[r][j][1] = fmaf(dsum[r][j][0][1] + dsum[r][j][1][1], s0, acc[r][j][1]);
-          acc[r][j][2] = fmaf(dsum[r][j][0][2] + dsum[r][j][1][2], s1, acc[r][j][2]);
-          acc[r][j][3] = fmaf(dsum[r][j][0][3] + dsum[r][j][1][3], s1, acc[r][j][3]);
-        }
-      } else {
-        float f0, c0, f1, c1;
-        GvInt4<T>::fold(MmaOp<T>::lo_f(zs0), false, f0, c0);
-        GvInt4<T>::fold(MmaOp<T>::lo_f(zs1), true, f1, c1);
-        const float sf0 = s0 * f0, sc0 = s0 * c0, sf1 = s1 * f1, sc1 = s1 * c1;
-#pragma unroll
-        for (int j = 0; j < NT; ++j) {
-          // rows g, g+8 x tokens 2c, 2c+1; S of the tokens 2c, 2c+1
-          const float S0 = ssum[j][0][0] + ssum[j][1][0], S1 = ssum[j][0][1] + ssum[j][1][1];
-          acc[r][j][0] = fmaf(dsum[r][j][0][0] + dsum[r][j][1][0], sf0, fmaf(S0, sc0, acc[r][j][0]));
-          acc[r][j][1] = fmaf(dsum[r][j][0][1] + dsum[r][j][1][1], sf0, fmaf(S1, sc0, acc[r][j][1]));
-          acc[r][j][2] = fmaf(dsum[r][j][0][2] + dsum[r][j][1][2], sf1, fmaf(S0, sc1, acc[r][j][2]));
-          acc[r][j][3] = fmaf(dsum[r][j][0][3] + dsum[r][j][1][3], sf1, fmaf(S1, sc1, acc[r][j][3]));
+          for (int j = 0; j < NT; ++j) {
+            const T* ur = lora_u + (size_t)(8 * j + g < a.M ? 8 * j + g : 0) * kBK + k0 + 2 * c;
+            MmaOp<T>::mma(acc[j], af, *reinterpret_cast<const uint32_t*>(ur), *reinterpret_cast<const uint32_t*>(ur + 8));
+          }
         }
       }
+      // this warp's share of the slab into its slot of buffer si % 2 (free
+      // once slab si - 2 is written out); the last of the 16 adds the slots
+      // and writes the outputs
+      const int r = si & 1;
+      float* rbuf = red + r * (kGvWarps * NT * 128);
+      if (si >= 2 && *reinterpret_cast<volatile int*>(&gen[r]) < (si >> 1)) {
+        const uint64_t t0 = global_ns();
+        for (uint32_t i = 0; *reinterpret_cast<volatile int*>(&gen[r]) < (si >> 1); ++i)
+          if ((i & 63) == 63 && global_ns() - t0 > kWaitNs) {
+            if (lane == 0) atomicExch(err, 5);
+            break;
+          }
+      }
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        *reinterpret_cast<float4*>(&rbuf[(warp * NT + j) * 128 + lane * 4]) = make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[j][e] = 0.0f;
+      }
+      __threadfence_block();
+      __syncwarp();
+      int last = 0;
+      if (lane == 0) last = atomicAdd(&cnt[r], 1) == kGvWarps - 1;
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (last) {
+        __threadfence_block();
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+          float4 sum = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll 4
+          for (int w = 0; w < kGvWarps; ++w) {
+            const uint4 q = lds_v4(smem_u32(&rbuf[(w * NT + j) * 128 + lane * 4]));
+            sum.x += __uint_as_float(q.x);
+            sum.y += __uint_as_float(q.y);
+            sum.z += __uint_as_float(q.z);
+            sum.w += __uint_as_float(q.w);
+          }
+          const float vals[4] = {sum.x, sum.y, sum.z, sum.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int tok = 8 * j + 2 * (lane & 3) + (e & 1);
+            if (tok >= a.M) continue;
+            const int row = slab * 16 + (lane >> 2) + (e >= 2 ? 8 : 0);
+            y[(size_t)tok * a.N + row] = Ty<T>::from_f(bias ? __fadd_rn(vals[e], bias[row]) : vals[e]);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) {
+          cnt[r] = 0;
+          __threadfence_block();
+          *reinterpret_cast<volatile int*>(&gen[r]) = (si >> 1) + 1;
+        }
+      }
+      ++si;
     }
-    __syncwarp();  // every lane has read the slot before it is refilled
-    if (i + depth < n_my) issue(i + depth);
-  }
-  if (i < n_my) {
-    // a stage did not land within the wait limit: record it, and wait
-    // (bounded) for the copies still in flight before the block exits
-    if (lane == 0) s_err = 5;
-    for (int j = i + 1; j < n_my && j < i + depth; ++j) mbar_wait_warp(&bar[j % depth], (uint32_t)(j / depth) & 1u);
-  }
-#pragma unroll
-  for (int r = 0; r < R16; ++r)
-#pragma unroll
-    for (int j = 0; j < NT; ++j)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) red[(((warp * R16 + r) * NT + j) * 32 + lane) * 4 + e] = acc[r][j][e];
-  __syncthreads();
-  // thread -> (r, j, lane, e) of the fragments: rows g (+8 for e >= 2),
-  // tokens 8 j + 2 c (+1 for odd e)
-  for (int o = threadIdx.x; o < R16 * NT * 128; o += blockDim.x) {
-    const int e = o & 3, ln = (o >> 2) & 31, rj = o >> 7;
-    const int j = rj % NT, r = rj / NT;
-    float sum = 0.0f;
-#pragma unroll
-    for (int w = 0; w < WARPS; ++w) sum += red[(((w * R16 + r) * NT + j) * 32 + ln) * 4 + e];
-    const int row = r0 + 16 * r + (ln >> 2) + (e >= 2 ? 8 : 0);
-    const int tok = 8 * j + 2 * (ln & 3) + (e & 1);
-    if (tok < a.M) {
-      // LoRA: + u[tok] . lora_B[row] (u rows padded to 64 columns)
-      for (int jr = 0; jr < lora_r; ++jr)
-        sum = fmaf(Ty<T>::to_f(lora_u[(size_t)tok * kBK + jr]), Ty<T>::to_f(lora_b[(size_t)row * lora_r + jr]), sum);
-      if (bias) sum = __fadd_rn(sum, bias[row]);
-      y[(size_t)tok * a.N + row] = Ty<T>::from_f(sum);
+    if (++ch == n_chunk) ch = 0;
+    if (++sl == stages) {
+      sl = 0;
+      par ^= 1u;
     }
   }
-  if (threadIdx.x == 0 && s_err && err) atomicExch(err, s_err);
 }
 
-// Dynamic shared memory of a GEMV block: NF table, the warps' partial sums,
-// barriers, the rings.
-template <bool NF, int R16, int NT, int WARPS>
-inline int gemv_fixed_smem() {
-  return (NF ? kPairLut16Words * 4 + 1024 : 0) + WARPS * R16 * NT * 512 + WARPS * kGvMaxDepth * 8;
+// Shared memory of the streaming GEMV before its ring: table (NF4), slab
+// shares and counters, barriers, group sums (INT4), activations (XS).
+inline int gv_fixed_smem(bool nf, bool xs, int NT, int M, int K, int G) {
+  const int n_grp = K / G;
+  return (nf ? kPairLut16Words * 4 + 1024 : 0) + 2 * kGvWarps * NT * 512 + 128 +
+         2 * kGvMaxStages * 8 + 128 + (nf ? 0 : ((n_grp * 64 + 127) / 128) * 128) +
+         (xs ? ((M * gv_xpitch_bytes(K) + 127) / 128) * 128 : 0);
 }
-constexpr int kGvSmemCap = 57 * 1024;  // four blocks per SM
 
-// Two 16-row slabs per block: N = 14336 gives 448 blocks, which must all be
-// resident at once (4 per SM, under 57 KB of shared memory each); the ring
-// is as deep (2 .. 4 groups per warp) as that leaves room for.  Returns 1
-// when the group size does not fit (the caller takes the tensor-core path).
-template <typename T, bool NF, int NT, int XR, int WARPS>
+template <typename T, bool NF, int NT, bool XS, int SPG>
 int launch_gemv_nt(const W4Args& a, const void* x, const void* packed, const float* bias, void* y,
                    int* err, cudaStream_t st, const LoraArgs& lo) {
-  constexpr int R16 = 2;
-  const int G = NF ? kBK : a.group;
-  const int fixed = gemv_fixed_smem<NF, R16, NT, WARPS>();
-  const int stage = gv_stage_bytes(R16, XR, G);
-  int depth = (kGvSmemCap - fixed) / (WARPS * stage);
-  if (depth > kGvMaxDepth) depth = kGvMaxDepth;
-  if (depth < 2 || a.N % (16 * R16) != 0) return 1;
-  const int smem = fixed + WARPS * depth * stage;
-  auto kern = w4a16_gemv_kernel<T, NF, R16, NT, XR, WARPS>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kGvSmemCap) != cudaSuccess)
-    return launched("w4a16_gemv_kernel (attribute)");
-  kern<<<a.N / (16 * R16), 32 * WARPS, smem, st>>>(static_cast<const T*>(x), static_cast<const uint8_t*>(packed),
-                                                   bias, static_cast<T*>(y), a, G, depth, err,
-                                                   static_cast<const T*>(lo.u), static_cast<const T*>(lo.b), lo.r);
+  static std::atomic<uint64_t> attr_done{0};
+  GvArgs v;
+  v.G = NF ? kBK : a.group;
+  const int rb = (int)gv_record_bytes(v.G);
+  const int n_grp = a.K / v.G;
+  // chunks of ~32 KB (whole groups, a multiple of the warp count when K
+  // allows), fewer when that leaves under four stages
+  const int fixed = gv_fixed_smem(NF, XS, NT, a.M, a.K, v.G);
+  const int avail = kGvSmemMax - fixed;
+  int cg = (32768 + rb - 1) / rb;
+  const int cg4 = avail / 4 / rb / kGvWarps * kGvWarps;
+  if (cg4 >= kGvWarps && cg4 < cg) cg = cg4;
+  cg = (cg + kGvWarps - 1) / kGvWarps * kGvWarps;
+  if (cg > n_grp) cg = n_grp;
+  v.cg = cg;
+  v.stages = avail / (cg * rb);
+  if (v.stages > kGvMaxStages) v.stages = kGvMaxStages;
+  if (v.stages < 2) return 1;
+  const int smem = fixed + v.stages * cg * rb;
+  auto kern = w4a16_gemv_kernel<T, NF, NT, XS, SPG>;
+  LQ_TRY(set_smem_once(kern, kGvSmemMax, attr_done));
+  const int n_slab = a.N / 16;
+  const int grid = n_slab < num_sms() ? n_slab : num_sms();
+  kern<<<grid, 32 * (kGvWarps + 1), smem, st>>>(static_cast<const T*>(x), static_cast<const uint8_t*>(packed), bias,
+                                               static_cast<T*>(y), a, v, err, static_cast<const T*>(lo.u),
+                                               static_cast<const T*>(lo.b), lo.r);
   return launched("w4a16_gemv_kernel");
 }
 
-// 0 = launched (or a launch error), 1 = not applicable here
+template <typename T, bool NF, int SPG>
+int launch_gemv_m(const W4Args& a, const void* x, const void* packed, const float* bias, void* y, int* err,
+                  cudaStream_t st, const LoraArgs& lo, bool xs) {
+  if (a.M <= 8)
+    return xs ? launch_gemv_nt<T, NF, 1, true, SPG>(a, x, packed, bias, y, err, st, lo)
+              : launch_gemv_nt<T, NF, 1, false, SPG>(a, x, packed, bias, y, err, st, lo);
+  return xs ? launch_gemv_nt<T, NF, 2, true, SPG>(a, x, packed, bias, y, err, st, lo)
+            : launch_gemv_nt<T, NF, 2, false, SPG>(a, x, packed, bias, y, err, st, lo);
+}
+
+// 0 = launched (or a launch error), 1 = not applicable here (groups above
+// 256, or the shared memory leaves fewer than two ring stages)
 template <typename T, bool NF>
 int launch_gemv(const void* x, int M, int N, int K, int group, const void* packed, const float* bias,
                 void* y, int* err, cudaStream_t st, const LoraArgs& lo) {
@@ -876,10 +1054,19 @@ int launch_gemv(const void* x, int M, int N, int K, int group, const void* packe
   a.n_kb = K / kBK;
   a.n_groups = K / group;
   a.kb_shift = kb_shift_of(group);
-  // M = 1: eight warps split K; larger M: four (the activation rows fill the stage)
-  if (M == 1) return launch_gemv_nt<T, NF, 1, 1, 8>(a, x, packed, bias, y, err, st, lo);
-  if (M <= 8) return launch_gemv_nt<T, NF, 1, 8, 4>(a, x, packed, bias, y, err, st, lo);
-  return launch_gemv_nt<T, NF, 2, 16, 4>(a, x, packed, bias, y, err, st, lo);
+  if (!NF && group > 4 * kBK) return 1;
+  // the activations are copied to shared memory when they fit and their rows
+  // start on 16-byte boundaries (K is a multiple of 64)
+  const bool xs = (int64_t)M * gv_xpitch_bytes(K) <= kGvXsMax && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+  // K steps per group as a compile-time constant for the common groups
+  // (NF4: 64; INT4: 64, 128), looped otherwise
+  const int spg = NF ? 1 : group / kBK;
+  if (spg == 1) return launch_gemv_m<T, NF, 1>(a, x, packed, bias, y, err, st, lo, xs);
+  if constexpr (!NF) {
+    if (spg == 2) return launch_gemv_m<T, NF, 2>(a, x, packed, bias, y, err, st, lo, xs);
+    return launch_gemv_m<T, NF, 0>(a, x, packed, bias, y, err, st, lo, xs);
+  }
+  return 1;
 }
 
 // ---------------------------------------------------------------------------
@@ -1097,21 +1284,6 @@ inline W4Args w4_args(int M, int N, int K, int group) {
   a.n_groups = K / group;
   a.kb_shift = kb_shift_of(group);
   return a;
-}
-
-// Every CTA allocates all 512 tensor-memory columns: request enough shared
-// memory that only one CTA fits on an SM, so none waits in tcgen05.alloc.
-template <typename Kern>
-int set_smem_once(Kern kern, int smem_bytes, std::atomic<uint64_t>& done) {
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const uint64_t bit = 1ull << (dev & 63);  // one bit per device
-  if (!(done.load() & bit)) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
-    LQ_REQUIRE(e == cudaSuccess, LQ_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    done.fetch_or(bit);
-  }
-  return LQ_OK;
 }
 
 template <typename T, int BT, int S, bool NF, int WK>
