@@ -959,7 +959,7 @@ class QLoRALinearWorkload(W4A16Workload):
     every M.  Weak scaling (replicas)."""
     name = "qlora_linear"
     workload = "qlora_linear_nf4_bf16_K4096_N14336_block64_dq256_M1024_x6_layers"
-    main_kernel = "nf4_linear_kernel"
+    main_kernel = "w4a16_kernel<nf4>"
 
     def __init__(self, ctx):
         torch = ctx.torch
@@ -996,7 +996,7 @@ class QLoRALinearWorkload(W4A16Workload):
                 c[0] += 1
             t = cuda_time_ms(self.ctx.torch, f, 4 * self.LAYERS)
             wbytes = self.N * self.K / 2 + self.N * (self.K // 64) * 4
-            kname = "nf4_linear_gemv_kernel" if m <= 8 else "nf4_linear_kernel"
+            kname = "w4a16_gemv_kernel<nf4>" if m <= 8 else "w4a16_kernel<nf4>"
             out[f"{kname} M={m}"] = (self.flops(m), t, m, wbytes + 2 * m * self.K + 2 * m * self.N)
         return out
 

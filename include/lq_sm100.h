@@ -323,9 +323,10 @@ size_t lq_nf4_linear_packed_bytes(int64_t N, int64_t K);
 /* lq_nf4_linear_lora: QLoRALinear.forward whole (qlora.py:306-312): y =
  * x @ W^T + bias + u @ lora_b^T, the LoRA term in the same kernel (the
  * tensor-core path runs it as one more K step with lora_B's rows as the A
- * operand, the weight-streaming path adds it per output).  u = scaling *
- * x @ lora_A^T [M, 64] in act_dtype (columns rank..63 zero), lora_b [N, rank]
- * in act_dtype; rank even, <= 16 for M > 16 and <= 64 for M <= 16. */
+ * operand, the weight-streaming path as one more MMA pass per 16-row slab).
+ * u = scaling * x @ lora_A^T [M, 64] in act_dtype (columns rank..63 zero),
+ * lora_b [N, rank] in act_dtype; rank even, <= 16 for M > 8 and <= 64 for
+ * M <= 8. */
 int lq_nf4_linear_lora(const void* x, int act_dtype, int64_t M, int64_t N, int64_t K,
                        const void* packed, const float* bias, const void* lora_u,
                        const void* lora_b, int64_t rank, void* y, int* err, void* stream);

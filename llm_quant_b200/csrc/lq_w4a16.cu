@@ -518,20 +518,22 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
 }
 
 // ---------------------------------------------------------------------------
-// Small M (M <= 16 tokens): the forward is a weight-streaming GEMV, bound by
+// Small M (M <= 8 tokens): the forward is a weight-streaming GEMV, bound by
 // HBM; a 128 x BT tensor-memory tile would sit mostly idle.  It runs
 // mma.sync.m16n8k16 (f32 accumulate) with the weights as the A operand and
-// one or two 8-token B tiles, on a layout of the codes of its own that the
-// pack kernels append to the operand ("GEMV codes"):
+// one 8-token B tile, on a layout of the codes of its own that the pack
+// kernels append to the operand ("GEMV records", gv_record_bytes):
 //
-//   [N/16 slabs][K/64 steps][32 lanes][4 words], lane L = 4 g + c owns the 16
-//   bytes of its A fragments: word t holds rows (g, g + 8) x k (4t .. 4t+3) of
-//   the lane's 16-wide k range 16c .. 16c+15 of the step, as
+//   [N/16 slabs][groups][steps of the group: 32 lanes x 4 words][16 pairs],
+//   lane L = 4 g + c owns the 16 bytes of its A fragments: word t holds rows
+//   (g, g + 8) x k (4t .. 4t+3) of the lane's 16-wide k range 16c .. 16c+15
+//   of the 64-wide step, as
 //     INT4: bits 0-3 / 16-19   row g,   k 4t, 4t+1     (a0)
 //           bits 4-7 / 20-23   row g+8, k 4t, 4t+1     (a1)
 //           bits 8-11 / 24-27  row g,   k 4t+2, 4t+3   (a2)
 //           bits 12-15 / 28-31 row g+8, k 4t+2, 4t+3   (a3)
-//     NF4:  byte b = the (low, high) nibble pair of fragment a_b.
+//     NF4:  byte b = the (low, high) nibble pair of fragment a_b;
+//   then the slab's 16 (magic + zero, scale) pairs (NF4: (0, block scale)).
 //   The MMA's k slots (2c, 2c+1, 2c+8, 2c+9) of step t are these k values,
 //   for the weights and the activations alike, so each lane's activations are
 //   16 contiguous halves (two 16-byte loads) and each lane reads exactly its
@@ -540,18 +542,11 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
 // INT4: a fragment is (code | magic) with one LOP3 -- 1024 + q (fp16, bits
 // 0-3), 1024 + 16 q (fp16, bits 4-7: rows g + 8), 128 + q (bf16, after a
 // shift) -- and the zero point is not subtracted per weight: with S = sum of
-// the group's activations (one more MMA per 16-wide k tile with A = 1), the
-// group contributes s * (f D - (o + z) S) to the output, (f, o) = (1, magic)
-// or (1/16, 64), D = the MMA sum of the fragments.  D and S are accumulated
-// over the steps of a group and folded in once per group.  NF4: the fragment
-// is the table pair of the code byte, the block scale multiplies D.
-//
-// A block of WARPS warps owns R16 slabs (16 R16 rows); warp w takes a
-// contiguous share of the K steps, streamed into its own DEPTH-stage ring by
-// bulk copies (one per lane: each slab's 512 bytes of codes and 64 of its
-// group's (zero, scale) pairs, one 128-byte row per token of activations)
-// completing on the slot's mbarrier (bounded waits; a stage that never lands
-// sets *err); the warps' sums are added in shared memory.
+// the group's activations (formed once per block), the group contributes
+// s * (f D - (o + z) S) to the output, (f, o) = (1, magic) or (1/16, 64),
+// D = the MMA sum of the fragments over the group's steps.  NF4: the
+// fragment is the table pair of the code byte, the block scale multiplies D.
+// The kernel itself (w4a16_gemv_kernel) is described at its definition.
 // ---------------------------------------------------------------------------
 template <typename T> struct MmaOp;
 template <> struct MmaOp<__half> {
@@ -1007,14 +1002,16 @@ int launch_gemv_nt(const W4Args& a, const void* x, const void* packed, const flo
   v.G = NF ? kBK : a.group;
   const int rb = (int)gv_record_bytes(v.G);
   const int n_grp = a.K / v.G;
-  // chunks of ~32 KB (whole groups, a multiple of the warp count when K
-  // allows), fewer when that leaves under four stages
+  // chunks of ~32 KB (whole groups, a multiple of the warp count), smaller
+  // when that leaves under three stages
   const int fixed = gv_fixed_smem(NF, XS, NT, a.M, a.K, v.G);
   const int avail = kGvSmemMax - fixed;
-  int cg = (32768 + rb - 1) / rb;
-  const int cg4 = avail / 4 / rb / kGvWarps * kGvWarps;
-  if (cg4 >= kGvWarps && cg4 < cg) cg = cg4;
-  cg = (cg + kGvWarps - 1) / kGvWarps * kGvWarps;
+  int cg = ((32768 + rb - 1) / rb + kGvWarps - 1) / kGvWarps * kGvWarps;
+  if (3 * cg * rb > avail) {
+    cg = avail / 3 / rb;
+    if (cg >= kGvWarps) cg = cg / kGvWarps * kGvWarps;
+    if (cg < 1) return 1;
+  }
   if (cg > n_grp) cg = n_grp;
   v.cg = cg;
   v.stages = avail / (cg * rb);
@@ -1034,15 +1031,13 @@ int launch_gemv_nt(const W4Args& a, const void* x, const void* packed, const flo
 template <typename T, bool NF, int SPG>
 int launch_gemv_m(const W4Args& a, const void* x, const void* packed, const float* bias, void* y, int* err,
                   cudaStream_t st, const LoraArgs& lo, bool xs) {
-  if (a.M <= 8)
-    return xs ? launch_gemv_nt<T, NF, 1, true, SPG>(a, x, packed, bias, y, err, st, lo)
-              : launch_gemv_nt<T, NF, 1, false, SPG>(a, x, packed, bias, y, err, st, lo);
-  return xs ? launch_gemv_nt<T, NF, 2, true, SPG>(a, x, packed, bias, y, err, st, lo)
-            : launch_gemv_nt<T, NF, 2, false, SPG>(a, x, packed, bias, y, err, st, lo);
+  return xs ? launch_gemv_nt<T, NF, 1, true, SPG>(a, x, packed, bias, y, err, st, lo)
+            : launch_gemv_nt<T, NF, 1, false, SPG>(a, x, packed, bias, y, err, st, lo);
 }
 
-// 0 = launched (or a launch error), 1 = not applicable here (groups above
-// 256, or the shared memory leaves fewer than two ring stages)
+// 0 = launched (or a launch error), 1 = not applicable here (more than 8
+// tokens -- from 9 on the 32-token tensor-core tile measured faster --,
+// groups above 256, or the shared memory leaves fewer than two ring stages)
 template <typename T, bool NF>
 int launch_gemv(const void* x, int M, int N, int K, int group, const void* packed, const float* bias,
                 void* y, int* err, cudaStream_t st, const LoraArgs& lo) {
@@ -1054,7 +1049,7 @@ int launch_gemv(const void* x, int M, int N, int K, int group, const void* packe
   a.n_kb = K / kBK;
   a.n_groups = K / group;
   a.kb_shift = kb_shift_of(group);
-  if (!NF && group > 4 * kBK) return 1;
+  if (M > 8 || (!NF && group > 4 * kBK)) return 1;
   // the activations are copied to shared memory when they fit and their rows
   // start on 16-byte boundaries (K is a multiple of 64)
   const bool xs = (int64_t)M * gv_xpitch_bytes(K) <= kGvXsMax && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
@@ -1339,7 +1334,7 @@ int w4_dispatch(const void* x, int M, int N, int K, int group, const void* packe
   if (M <= 16) {
     const int rc = launch_gemv<T, NF>(x, M, N, K, group, packed, bias, y, err, st, lo);
     if (rc != 1) return rc;
-    // group too large for the GEMV's stage: 32-token tensor-core tiles
+    // 9 - 16 tokens (or a group too large for the GEMV): 32-token tensor-core tiles
     if (K % (2 * kBK) == 0) return launch_w4<T, 32, 4, NF, 2>(x, M, N, K, group, packed, bias, y, err, st, lo);
     return launch_w4<T, 32, 8, NF, 1>(x, M, N, K, group, packed, bias, y, err, st, lo);
   }
@@ -1481,8 +1476,8 @@ extern "C" int lq_nf4_linear_lora(const void* x, int act_dtype, int64_t M, int64
   LQ_REQUIRE(x && packed && y && lora_u && lora_b, LQ_EINVAL, "NULL pointer");
   LQ_REQUIRE(aligned16(x) && aligned16(packed) && aligned16(lora_u) && aligned16(lora_b), LQ_EALIGN,
              "x, packed, lora_u and lora_b must be 16-byte aligned");
-  LQ_REQUIRE(rank >= 2 && rank % 2 == 0 && rank <= (M <= 16 ? kBK : 16), LQ_ERANGE,
-             "fused LoRA needs an even rank <= %d at M = %lld (got %lld)", M <= 16 ? kBK : 16,
+  LQ_REQUIRE(rank >= 2 && rank % 2 == 0 && rank <= (M <= 8 ? kBK : 16), LQ_ERANGE,
+             "fused LoRA needs an even rank <= %d at M = %lld (got %lld)", M <= 8 ? kBK : 16,
              (long long)M, (long long)rank);
   LoraArgs lo;
   lo.u = lora_u;

@@ -124,10 +124,10 @@ def base_linear(ql, x: torch.Tensor) -> torch.Tensor:
 
 def lora_fusable(ql, x: torch.Tensor) -> bool:
     """The kernels take the LoRA term for an even rank up to 16 (tensor-core
-    path, more than 16 tokens) or 64 (weight-streaming path, up to 16)."""
+    path, more than 8 tokens) or 64 (weight-streaming path, up to 8)."""
     r = ql.rank
     m = x.numel() // ql.in_features if ql.in_features else 0
-    return r >= 2 and r % 2 == 0 and r <= (64 if m <= 16 else 16)
+    return r >= 2 and r % 2 == 0 and r <= (64 if m <= 8 else 16)
 
 
 def _lora_u(ql, x2: torch.Tensor, lora_a: torch.Tensor) -> torch.Tensor:

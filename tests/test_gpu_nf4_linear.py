@@ -125,11 +125,11 @@ def test_fp32_path_is_the_reference_computation(L):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("M,rank", [(1, 16), (5, 64), (16, 32), (17, 16), (200, 2), (1024, 16),
-                                    (300, 24), (64, 5)])
+@pytest.mark.parametrize("M,rank", [(1, 16), (5, 64), (8, 48), (16, 32), (16, 16), (17, 16), (200, 2),
+                                    (1024, 16), (300, 24), (64, 5)])
 def test_lora_fused_and_fallback(L, dtype, M, rank):
-    """The LoRA term inside the base kernel (even rank <= 16 above 16 tokens,
-    <= 64 up to 16) and the unfused path for other ranks give the fp32
+    """The LoRA term inside the base kernel (even rank <= 16 above 8 tokens,
+    <= 64 up to 8) and the unfused path for other ranks give the fp32
     reference within the same bound."""
     from llm_quant_b200 import nf4_linear
     ql, g = _module(L, 256, 1024, dtype, 64, True, seed=M * 7 + rank, rank=rank)
@@ -137,7 +137,7 @@ def test_lora_fused_and_fallback(L, dtype, M, rank):
         ql.lora_A.copy_(torch.randn(rank, 1024, generator=g) * 0.05)
     x = torch.randn(M, 1024, generator=g).to(dtype).cuda()
     fused = nf4_linear.lora_fusable(ql, x)
-    assert fused == (rank % 2 == 0 and rank <= (64 if M <= 16 else 16))
+    assert fused == (rank % 2 == 0 and rank <= (64 if M <= 8 else 16))
     with torch.no_grad():
         y = ql(x)
     ref = _reference(ql, x)
