@@ -330,6 +330,15 @@ size_t lq_nf4_linear_packed_bytes(int64_t N, int64_t K);
 int lq_nf4_linear_lora(const void* x, int act_dtype, int64_t M, int64_t N, int64_t K,
                        const void* packed, const float* bias, const void* lora_u,
                        const void* lora_b, int64_t rank, void* y, int* err, void* stream);
+/* lq_lora_u: the LoRA down-projection of QLoRALinear.forward (qlora.py:311,
+ * F.linear(x, lora_A) * scaling) as the u operand of lq_nf4_linear_lora:
+ * u[M, 64] (act_dtype) = scaling * x[M, K] @ lora_a[rank, K]^T in columns
+ * 0..rank-1 and zeros in rank..63; fp32 accumulation on the tensor cores,
+ * rounded once to act_dtype.  lora_a in LQ_F32 or act_dtype; K % 64 == 0,
+ * 1 <= rank <= 64; x and lora_a 16-byte aligned. */
+int lq_lora_u(const void* x, int act_dtype, int64_t M, int64_t K, const void* lora_a, int a_dtype,
+              int64_t rank, float scaling, void* u, void* stream);
+
 /* lq_nf4_merge_lora: QLoRALinear.merge_lora (qlora.py:314-317) in one pass:
  * out [N, K] = W_base + scaling * lora_b @ lora_a with W_base exactly
  * _dequantize_base's (scales / double-quantized scales as in lq_nf4_unpack,

@@ -1,0 +1,193 @@
+// lq_lora.cu -- the LoRA down-projection of QLoRALinear.forward
+// (qlora.py:311: F.linear(x, lora_A) * scaling), written straight into the
+// zero-padded [M, 64] activation-dtype operand that the fused NF4 kernels take
+// as u.  One launch replaces a memset, a dtype cast of lora_A and a cuBLAS
+// call with a 16-column output.
+//
+// A block owns a 16-token tile of x; its 16 warps take the K steps (64 wide)
+// w, w + 16, ... (a few each, their loads in flight together) and run mma.sync.m16n8k16 (fp32 accumulate) with x as A and
+// lora_A^T as B, one 8-column B tile per 8 ranks.  A lane reads the 16
+// contiguous halves 16c .. 16c+15 of each step for its two token rows and its
+// rank row (the k slots of the four MMAs of a step are a fixed permutation of
+// those 16, the same on both operands, so each lane needs two 16-byte loads
+// per row and no shuffles).  The warps' partial sums are added in shared
+// memory; the block writes scaling * sum rounded to the activation dtype, and
+// zeros in columns rank .. 63.  (Splitting K over a cluster of blocks, summed
+// through distributed shared memory, measured slower: 12.1 against 7.9 us at
+// M = 1024, K = 4096, rank 16.)
+#include <type_traits>
+
+#include "lq_common.cuh"
+
+namespace lq {
+namespace {
+
+constexpr int kLuWarps = 16;
+constexpr int kLuPitch = 64;  // u row pitch (the fused kernels' LoRA K step)
+
+template <typename T> struct LuMma;
+template <> struct LuMma<__half> {
+  __device__ __forceinline__ static void mma(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  }
+  __device__ __forceinline__ static uint32_t pack(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+};
+template <> struct LuMma<__nv_bfloat16> {
+  __device__ __forceinline__ static void mma(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  }
+  __device__ __forceinline__ static uint32_t pack(float lo, float hi) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+};
+
+__device__ __forceinline__ uint32_t lu_word(const uint4& v, int i) {
+  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+
+// 16 k values of rank row `row` (zero past the rank) as 8 words of T pairs
+template <typename T, typename AT>
+__device__ __forceinline__ void lu_load_a(const AT* a, int row, int rank, int64_t K, int64_t k, uint4 (&w)[2]) {
+  if (row >= rank) {
+    w[0] = w[1] = make_uint4(0u, 0u, 0u, 0u);
+    return;
+  }
+  if constexpr (std::is_same<AT, float>::value) {
+    const float4* p = reinterpret_cast<const float4*>(a + (size_t)row * K + k);
+    float4 f[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) f[i] = __ldg(p + i);
+    w[0] = make_uint4(LuMma<T>::pack(f[0].x, f[0].y), LuMma<T>::pack(f[0].z, f[0].w), LuMma<T>::pack(f[1].x, f[1].y),
+                      LuMma<T>::pack(f[1].z, f[1].w));
+    w[1] = make_uint4(LuMma<T>::pack(f[2].x, f[2].y), LuMma<T>::pack(f[2].z, f[2].w), LuMma<T>::pack(f[3].x, f[3].y),
+                      LuMma<T>::pack(f[3].z, f[3].w));
+  } else {
+    const uint4* p = reinterpret_cast<const uint4*>(a + (size_t)row * K + k);
+    w[0] = __ldg(p);
+    w[1] = __ldg(p + 1);
+  }
+}
+
+template <typename T, typename AT, int NTL>
+__global__ void __launch_bounds__(32 * kLuWarps) lora_u_kernel(const T* __restrict__ x, const AT* __restrict__ a,
+                                                               T* __restrict__ u, int64_t M, int64_t K, int rank,
+                                                               float scaling) {
+  constexpr int H = kLuWarps / 2;
+  __shared__ float red[H][NTL][32][4];
+  // the fused linear that consumes u may start its set-up meanwhile; it waits
+  // for this grid before it touches global memory
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int64_t m0 = (int64_t)blockIdx.x * 16;
+  // token rows of this lane (rows past M read row M - 1; never stored)
+  const int64_t r0 = min(m0 + g, M - 1), r1 = min(m0 + g + 8, M - 1);
+  float d[NTL][4];
+#pragma unroll
+  for (int nt = 0; nt < NTL; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) d[nt][e] = 0.0f;
+  const int64_t n_steps = K / 64;
+  constexpr int UNR = NTL <= 2 ? 4 : NTL <= 4 ? 2 : 1;
+#pragma unroll UNR
+  for (int64_t s = warp; s < n_steps; s += kLuWarps) {
+    const int64_t k = s * 64 + 16 * c;
+    const uint4* p0 = reinterpret_cast<const uint4*>(x + r0 * K + k);
+    const uint4* p1 = reinterpret_cast<const uint4*>(x + r1 * K + k);
+    const uint4 x0[2] = {__ldg(p0), __ldg(p0 + 1)};
+    const uint4 x1[2] = {__ldg(p1), __ldg(p1 + 1)};
+    uint4 av[NTL][2];
+#pragma unroll
+    for (int nt = 0; nt < NTL; ++nt) lu_load_a<T, AT>(a, nt * 8 + g, rank, K, k, av[nt]);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const int h = t >> 1, w0 = 2 * (t & 1);
+#pragma unroll
+      for (int nt = 0; nt < NTL; ++nt)
+        LuMma<T>::mma(d[nt], lu_word(x0[h], w0), lu_word(x1[h], w0), lu_word(x0[h], w0 + 1), lu_word(x1[h], w0 + 1),
+                      lu_word(av[nt][h], w0), lu_word(av[nt][h], w0 + 1));
+    }
+  }
+  // warps w and w + 8 share a slot of the partial sums
+  if (warp >= H) {
+#pragma unroll
+    for (int nt = 0; nt < NTL; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) red[warp - H][nt][lane][e] = d[nt][e];
+  }
+  __syncthreads();
+  if (warp < H) {
+#pragma unroll
+    for (int nt = 0; nt < NTL; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) red[warp][nt][lane][e] += d[nt][e];
+  }
+  __syncthreads();
+  // 16 rows x 32 column pairs of the padded output
+  for (int i = threadIdx.x; i < 16 * (kLuPitch / 2); i += blockDim.x) {
+    const int row = i / (kLuPitch / 2), pr = i % (kLuPitch / 2);
+    if (m0 + row >= M) continue;
+    const int nt = pr / 4, cc = pr % 4, ln = (row % 8) * 4 + cc, e = row >= 8 ? 2 : 0;
+    float v0 = 0.0f, v1 = 0.0f;
+    if (nt < NTL && 2 * pr < rank) {
+#pragma unroll
+      for (int w = 0; w < H; ++w) {
+        v0 += red[w][nt][ln][e];
+        v1 += red[w][nt][ln][e + 1];
+      }
+      v0 *= scaling;
+      v1 = 2 * pr + 1 < rank ? v1 * scaling : 0.0f;
+    }
+    reinterpret_cast<uint32_t*>(u + (m0 + row) * kLuPitch)[pr] = LuMma<T>::pack(v0, v1);
+  }
+}
+
+template <typename T, typename AT>
+int lora_u_t(const void* x, int64_t M, int64_t K, const void* a, int rank, float scaling, void* u, cudaStream_t st) {
+  const dim3 grid((unsigned)((M + 15) / 16));
+  const T* xp = static_cast<const T*>(x);
+  const AT* ap = static_cast<const AT*>(a);
+  T* up = static_cast<T*>(u);
+  if (rank <= 16)
+    lora_u_kernel<T, AT, 2><<<grid, 32 * kLuWarps, 0, st>>>(xp, ap, up, M, K, rank, scaling);
+  else if (rank <= 32)
+    lora_u_kernel<T, AT, 4><<<grid, 32 * kLuWarps, 0, st>>>(xp, ap, up, M, K, rank, scaling);
+  else
+    lora_u_kernel<T, AT, 8><<<grid, 32 * kLuWarps, 0, st>>>(xp, ap, up, M, K, rank, scaling);
+  return launched("lora_u_kernel");
+}
+
+}  // namespace
+}  // namespace lq
+
+extern "C" int lq_lora_u(const void* x, int act_dtype, int64_t M, int64_t K, const void* lora_a, int a_dtype,
+                         int64_t rank, float scaling, void* u, void* stream) {
+  using namespace lq;
+  LQ_REQUIRE(M >= 0 && M < (1LL << 31) && K >= 0 && K < (1LL << 31), LQ_EINVAL, "bad size");
+  if (M == 0) return LQ_OK;
+  LQ_REQUIRE(K % 64 == 0 && K > 0, LQ_EINVAL, "lora_u needs in_features %% 64 == 0 (got %lld)", (long long)K);
+  LQ_REQUIRE(rank >= 1 && rank <= kLuPitch, LQ_ERANGE, "LoRA rank %lld outside [1, 64]", (long long)rank);
+  LQ_REQUIRE(x && lora_a && u, LQ_EINVAL, "NULL pointer");
+  LQ_REQUIRE(aligned16(x) && aligned16(lora_a) && reinterpret_cast<uintptr_t>(u) % 4 == 0, LQ_EALIGN,
+             "x and lora_a must be 16-byte aligned, u 4-byte aligned");
+  LQ_REQUIRE(a_dtype == LQ_F32 || a_dtype == act_dtype, LQ_EDTYPE, "lora_A must be fp32 or the activation dtype");
+  cudaStream_t st = as_stream(stream);
+  if (act_dtype == LQ_F16)
+    return a_dtype == LQ_F32 ? lora_u_t<__half, float>(x, M, K, lora_a, (int)rank, scaling, u, st)
+                             : lora_u_t<__half, __half>(x, M, K, lora_a, (int)rank, scaling, u, st);
+  if (act_dtype == LQ_BF16)
+    return a_dtype == LQ_F32 ? lora_u_t<__nv_bfloat16, float>(x, M, K, lora_a, (int)rank, scaling, u, st)
+                             : lora_u_t<__nv_bfloat16, __nv_bfloat16>(x, M, K, lora_a, (int)rank, scaling, u, st);
+  set_error("lora_u: activations must be fp16 or bf16 (got dtype %d)", act_dtype);
+  return LQ_EDTYPE;
+}

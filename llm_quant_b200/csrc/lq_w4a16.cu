@@ -326,6 +326,11 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // With the LoRA term the kernel is launched as a programmatic dependent of
+  // the u kernel: the set-up above overlaps that kernel's tail, and no thread
+  // touches global memory before the previous kernel is complete (a no-op
+  // after an ordinary launch).
+  pdl_wait();
 
   if (warp == 0) {
     // ---------------- activation producer ----------------
@@ -1298,8 +1303,15 @@ int launch_w4(const void* x, int M, int N, int K, int group, const void* packed,
   static std::atomic<uint64_t> attr_done{0};
   LQ_TRY(set_smem_once(kern, smem_bytes, attr_done));
   dim3 grid(N / kRows, (M + BT - 1) / BT);
-  kern<<<grid, kW4Threads, smem_bytes, st>>>(map, umap, static_cast<const uint8_t*>(packed), bias,
-                                    static_cast<T*>(y), a, static_cast<const T*>(lo.b), lo.r, err);
+  if (lo.r > 0) {
+    const cudaError_t e = launch_pdl(kern, grid, dim3(kW4Threads), smem_bytes, st, map, umap,
+                                     static_cast<const uint8_t*>(packed), bias, static_cast<T*>(y), a,
+                                     static_cast<const T*>(lo.b), lo.r, err);
+    LQ_REQUIRE(e == cudaSuccess, LQ_ECUDA, "w4a16_kernel launch: %s", cudaGetErrorString(e));
+  } else {
+    kern<<<grid, kW4Threads, smem_bytes, st>>>(map, umap, static_cast<const uint8_t*>(packed), bias,
+                                      static_cast<T*>(y), a, static_cast<const T*>(lo.b), lo.r, err);
+  }
   return launched("w4a16_kernel");
 }
 

@@ -132,11 +132,33 @@ def lora_fusable(ql, x: torch.Tensor) -> bool:
 
 def _lora_u(ql, x2: torch.Tensor, lora_a: torch.Tensor) -> torch.Tensor:
     """u = scaling * x @ lora_A^T in the activations' dtype, rows padded with
-    zeros to 64 columns (the kernels' row pitch); one cuBLAS call."""
-    r = ql.rank
-    u = torch.zeros(x2.shape[0], 64, dtype=x2.dtype, device=x2.device)
-    torch.addmm(u[:, :r], x2, lora_a.to(x2.dtype).t(), beta=0, alpha=ql.scaling, out=u[:, :r])
+    zeros to 64 columns (the kernels' row pitch): one lq_lora_u launch on
+    lora_A cast to the activations' dtype (cached while lora_A is unchanged)."""
+    a = _cast_cached(ql, "_lora_a_cast", lora_a, x2.dtype)
+    u = torch.empty(x2.shape[0], 64, dtype=x2.dtype, device=x2.device)
+    _C.call("lq_lora_u", x2.data_ptr(), _C.dt(x2), x2.shape[0], ql.in_features, a.data_ptr(), _C.dt(a),
+            ql.rank, float(ql.scaling), u.data_ptr(), _C.stream_ptr(x2))
     return u
+
+
+def _cast_cached(ql, slot: str, src: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """src in `dtype`, contiguous and 16-byte aligned: cast once and kept
+    while src is unchanged (same storage, same in-place version counter; the
+    cache holds the source, so its address cannot be reused meanwhile)."""
+    if src.dtype == dtype and src.is_contiguous() and src.data_ptr() % 16 == 0:
+        return src
+    key = (src.data_ptr(), src._version, dtype, tuple(src.shape), src.stride())
+    cached = getattr(ql, slot, None)
+    if cached is not None and cached[0] == key:
+        return cached[2]
+    t = src.to(dtype).contiguous()
+    setattr(ql, slot, (key, src, t))
+    return t
+
+
+def _lora_b(ql, lora_b: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """lora_B in the activations' dtype (the kernels' A operand of the LoRA step)."""
+    return _cast_cached(ql, "_lora_b_cast", lora_b, dtype)
 
 
 def _lora_forward(ql, x: torch.Tensor, lora_a, lora_b, bias) -> torch.Tensor:
@@ -153,7 +175,7 @@ def _lora_forward(ql, x: torch.Tensor, lora_a, lora_b, bias) -> torch.Tensor:
         if b.dtype != torch.float32 or not b.is_contiguous():
             b = b.float().contiguous()
     u = _lora_u(ql, x2, lora_a.detach())
-    lb = lora_b.detach().to(x.dtype).contiguous()
+    lb = _lora_b(ql, lora_b.detach(), x.dtype)
     _C.call("lq_nf4_linear_lora", x2.data_ptr(), _C.dt(x2), M, N, K, packed.data_ptr(), _C.ptr(b),
             u.data_ptr(), lb.data_ptr(), ql.rank, y.data_ptr(), _err_flag(x.device).data_ptr(),
             _C.stream_ptr(x2))

@@ -202,3 +202,41 @@ def test_merge_lora_gradients(L):
     a, b = ql.lora_A.detach(), ql.lora_B.detach()
     torch.testing.assert_close(ql.lora_A.grad, ql.scaling * b.t() @ gm, rtol=1e-4, atol=1e-4)
     torch.testing.assert_close(ql.lora_B.grad, ql.scaling * gm @ a.t(), rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("a_dtype", ["f32", "act"])
+@pytest.mark.parametrize("M,K,rank", [(1, 64, 1), (5, 256, 7), (16, 1024, 16), (17, 4096, 16),
+                                      (100, 512, 32), (33, 640, 48), (1024, 4096, 64)])
+def test_lora_u_kernel(L, dtype, a_dtype, M, K, rank):
+    """lq_lora_u = scaling * x @ lora_A^T in columns < rank, zeros up to 64,
+    rounded once to the activation dtype (fp32 accumulation)."""
+    from llm_quant_b200 import _C
+    g = torch.Generator().manual_seed(M * 131 + rank)
+    x = torch.randn(M, K, generator=g).to(dtype).cuda()
+    a = (torch.randn(rank, K, generator=g) * 0.05).cuda()
+    if a_dtype == "act":
+        a = a.to(dtype)
+    u = torch.full((M, 64), float("nan"), dtype=dtype, device="cuda")
+    _C.call("lq_lora_u", x.data_ptr(), _C.dt(x), M, K, a.data_ptr(), _C.dt(a), rank, 0.75,
+            u.data_ptr(), _C.stream_ptr(x))
+    ref = 0.75 * (x.float() @ a.to(dtype).float().T)
+    torch.testing.assert_close(u[:, :rank].float(), ref, rtol=1e-2, atol=1e-2 * ref.abs().max().item() + 1e-3)
+    assert torch.equal(u[:, rank:].float(), torch.zeros(M, 64 - rank, device="cuda"))
+
+
+def test_lora_b_cast_follows_updates(L):
+    """The cached activation-dtype copy of lora_B is rebuilt after an in-place
+    update (optimizer step) and after the parameter is rebound."""
+    ql, g = _module(L, 256, 512, torch.bfloat16, 64, True, seed=77, rank=8)
+    with torch.no_grad():
+        ql.lora_A.copy_(torch.randn(8, 512, generator=g) * 0.05)
+    x = torch.randn(4, 512, generator=g).to(torch.bfloat16).cuda()
+    with torch.no_grad():
+        y1 = ql(x)
+        ql.lora_B.add_(0.5)
+        y2 = ql(x)
+        _check(y2, _reference(ql, x))
+        assert not torch.equal(y1, y2)
+        ql.lora_B.data = torch.randn(256, 8, generator=g).cuda() * 0.1
+        _check(ql(x), _reference(ql, x))
