@@ -59,6 +59,26 @@ def packed_operand(ql, act_dtype: torch.dtype) -> torch.Tensor:
     return packed
 
 
+def fp32_bias(ql):
+    """The layer's bias as the kernels take it (fp32, contiguous), converted
+    once and kept while the bias is unchanged (same storage, same in-place
+    version counter; the cache holds the source, so its address cannot be
+    reused meanwhile).  None without a bias."""
+    b = ql.bias
+    if b is None:
+        return None
+    b = b.detach()
+    if b.dtype == torch.float32 and b.is_contiguous():
+        return b
+    key = (b.data_ptr(), b._version, tuple(b.shape), b.stride())
+    cached = getattr(ql, "_bias_f32", None)
+    if cached is not None and cached[0] == key:
+        return cached[2]
+    t = b.float().contiguous()
+    ql._bias_f32 = (key, b, t)
+    return t
+
+
 def linear(ql, x: torch.Tensor) -> torch.Tensor:
     """y = x @ dequant(W)^T + bias with the fused W4A16 kernel."""
     packed = packed_operand(ql, x.dtype)
@@ -68,11 +88,7 @@ def linear(ql, x: torch.Tensor) -> torch.Tensor:
         x2 = x2.contiguous()
     M = x2.shape[0]
     y = torch.empty(M, N, dtype=x.dtype, device=x.device)
-    bias = None
-    if ql.bias is not None:
-        bias = ql.bias.detach()
-        if bias.dtype != torch.float32 or not bias.is_contiguous():
-            bias = bias.float().contiguous()
+    bias = fp32_bias(ql)
     _C.call("lq_w4a16_linear", x2.data_ptr(), _C.dt(x2), M, N, K, ql.group_size,
             packed.data_ptr(), _C.ptr(bias), y.data_ptr(), _err_flag(x.device).data_ptr(),
             _C.stream_ptr(x2))

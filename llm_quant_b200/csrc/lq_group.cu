@@ -218,26 +218,35 @@ __global__ void __launch_bounds__(256) group_warp_kernel(const T* __restrict__ x
   const int64_t nteams = ((int64_t)gridDim.x * blockDim.x) / tps;
   // all lanes of a warp iterate the same number of times (shuffles below)
   const int64_t warp_team0 = team - (lane / tps);
+  // the team's next group is loaded before the current one is reduced and
+  // written, so its loads are in flight meanwhile
+  auto fetch = [&](Tile<T, NVT, VEC>& tl, int64_t g) {
+    if (g < a.total_groups) tl.load(x, g / a.groups_per_row, (g % a.groups_per_row) * a.G, a, t, tps);
+    else tl.inb = 0;
+  };
+  Tile<T, NVT, VEC> tile;
+  fetch(tile, warp_team0 + lane / tps);
   for (int64_t g0 = warp_team0; g0 < a.total_groups; g0 += nteams) {
     const int64_t g = g0 + lane / tps;
     const bool live = g < a.total_groups;
-    const int64_t row = live ? g / a.groups_per_row : 0;
-    const int64_t gcol0 = live ? (g % a.groups_per_row) * a.G : 0;
-    Tile<T, NVT, VEC> tile;
-    if (live) tile.load(x, row, gcol0, a, t, tps);
-    else tile.inb = 0;
+    Tile<T, NVT, VEC> next;
+    fetch(next, g + nteams);
     MinMax r;
     tile.reduce_local(r, a.sym);
     for (int m = 1; m < tps; m <<= 1) r.shfl_xor_merge(m, a.sym);
-    if (!live) continue;
-    float scale, zp;
-    qparams_from<T>(r, a.sym, a.qmin, a.qmax, a.lo, scale, zp);
-    if (t == 0 && scale_out) {
-      const int64_t si = a.sc_index(g);
-      scale_out[si] = Ty<T>::from_f(scale);
-      zp_out[si] = Ty<T>::from_f(zp);
+    if (live) {
+      const int64_t row = g / a.groups_per_row;
+      const int64_t gcol0 = (g % a.groups_per_row) * a.G;
+      float scale, zp;
+      qparams_from<T>(r, a.sym, a.qmin, a.qmax, a.lo, scale, zp);
+      if (t == 0 && scale_out) {
+        const int64_t si = a.sc_index(g);
+        scale_out[si] = Ty<T>::from_f(scale);
+        zp_out[si] = Ty<T>::from_f(zp);
+      }
+      if constexpr (MODE != MODE_QPARAMS) tile.template emit<MODE>(out, row, gcol0, a, t, tps, scale, zp);
     }
-    if constexpr (MODE != MODE_QPARAMS) tile.template emit<MODE>(out, row, gcol0, a, t, tps, scale, zp);
+    tile = next;
   }
 }
 

@@ -3,9 +3,10 @@
 Whole-model weight quantization and KV-cache quantization are independent per
 layer, so N ranks (one process per GPU, torch.distributed over NCCL) each
 take a contiguous block of layers and run the quantization kernels with no
-data-path collective.  The only exchange is the final gather of each rank's
-packed results (4-bit codes + scales) to rank 0 over NVLink: one flat byte
-buffer per rank, sent point to point at its exact size.
+data-path collective.  The only exchange is the gather of each rank's packed
+results (4-bit codes + scales) to rank 0 over NVLink at exact sizes: either
+once at the end (`gather_to_rank0`, one flat buffer per rank) or layer by
+layer while the later layers compute (`LayerGather`).
 """
 
 from __future__ import annotations
@@ -42,18 +43,23 @@ def _padded(nb: int) -> int:
 
 def flatten_bytes(tensors: Sequence[torch.Tensor]) -> torch.Tensor:
     """Concatenate tensors' raw bytes into one uint8 buffer (on their device),
-    each part starting on a 16-byte boundary."""
+    each part starting on a 16-byte boundary (zero padding between parts);
+    one concatenation kernel."""
     tensors = list(tensors)
     if not tensors:
         return torch.empty(0, dtype=torch.uint8)
-    total = sum(_padded(t.numel() * t.element_size()) for t in tensors)
-    buf = torch.zeros(total, dtype=torch.uint8, device=tensors[0].device)
-    off = 0
+    dev = tensors[0].device
+    zeros = torch.zeros(_ALIGN, dtype=torch.uint8, device=dev)
+    parts = []
     for t in tensors:
         nb = t.numel() * t.element_size()
-        buf[off:off + nb].copy_(t.contiguous().view(-1).view(torch.uint8))
-        off += _padded(nb)
-    return buf
+        if nb:
+            parts.append(t.contiguous().reshape(-1).view(torch.uint8))
+        if _padded(nb) > nb:
+            parts.append(zeros[:_padded(nb) - nb])
+    if not parts:
+        return torch.empty(0, dtype=torch.uint8, device=dev)
+    return torch.cat(parts)
 
 
 def unflatten_bytes(buf: torch.Tensor, like: Sequence[torch.Tensor]) -> List[torch.Tensor]:
@@ -101,3 +107,65 @@ def quantize_layers(num_layers: int, rank: int, world: int,
                     quantize_layer: Callable[[int], PackedLayer]) -> List[PackedLayer]:
     """Run `quantize_layer` on this rank's block of layers (no collective)."""
     return [quantize_layer(i) for i in layer_block(num_layers, rank, world)]
+
+
+class LayerGather:
+    """Gather of every rank's per-layer packed results to rank 0, overlapped
+    with the remaining layers' kernels.
+
+    Rank 0 posts one receive per remote layer up front (exact sizes, known on
+    every rank from `layer_nbytes`); every other rank calls `send` right after
+    enqueuing a layer's kernels: the layer's tensors are flattened into one
+    byte buffer on the current stream and sent point to point, so NCCL's
+    stream moves layer i while the compute stream runs layer i + 1.  Between
+    one pair of ranks the sends and receives are matched in issue order (layer
+    order).  `wait` completes everything and returns, on rank 0, the flat
+    buffer of every layer by global index (its own layers as flattened by
+    `send`), None elsewhere."""
+
+    def __init__(self, layer_nbytes: Sequence[int], rank: int, world: int, device, group=None):
+        self.rank, self.world, self.group = rank, world, group
+        self.n_layers = len(layer_nbytes)
+        self.owner = {}
+        for r in range(world):
+            for i in layer_block(self.n_layers, r, world):
+                self.owner[i] = r
+        self.bufs = {}
+        self.reqs = []
+        self.sent = []  # keep sent buffers alive until wait()
+        if rank == 0 and world > 1:
+            ops = []
+            for i in range(self.n_layers):
+                r = self.owner[i]
+                if r == 0 or layer_nbytes[i] == 0:
+                    continue
+                self.bufs[i] = torch.empty(layer_nbytes[i], dtype=torch.uint8, device=device)
+                ops.append(dist.P2POp(dist.irecv, self.bufs[i], self._peer(r), group))
+            if ops:
+                self.reqs += dist.batch_isend_irecv(ops)
+
+    def _peer(self, r: int) -> int:
+        return r if self.group is None else dist.get_global_rank(self.group, r)
+
+    def send(self, layer: int, tensors: Sequence[torch.Tensor]) -> None:
+        """Flatten `layer`'s results and send them to rank 0 (rank 0 keeps them)."""
+        if self.owner[layer] != self.rank:
+            raise ValueError(f"layer {layer} belongs to rank {self.owner[layer]}, not {self.rank}")
+        flat = flatten_bytes(tensors)
+        if self.rank == 0:
+            self.bufs[layer] = flat
+        elif flat.numel():
+            self.sent.append(flat)
+            self.reqs.append(dist.isend(flat, self._peer(0), group=self.group))
+
+    def wait(self):
+        for r in self.reqs:
+            r.wait()
+        self.reqs, self.sent = [], []
+        return self.bufs if self.rank == 0 else None
+
+
+def layer_packed_nbytes(sizes: Sequence[Sequence[int]]) -> List[int]:
+    """Flat byte size (16-byte aligned parts, as flatten_bytes) per layer,
+    from each layer's list of tensor byte sizes."""
+    return [sum(_padded(nb) for nb in layer) for layer in sizes]

@@ -134,3 +134,47 @@ def test_gather_world3_uneven_exact_sizes():
     msgs, codes = _run(3, 7)
     assert ("ok", True) in msgs, msgs
     assert codes == [0, 0, 0]
+
+
+def _layer_gather_worker(rank, world, port, n_layers, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from llm_quant_b200.sharded import LayerGather, layer_packed_nbytes
+        # every rank knows every layer's sizes (the model config)
+        sizes = [[t.numel() * t.element_size() for t in _layer_tensors(i)] for i in range(n_layers)]
+        lg = LayerGather(layer_packed_nbytes(sizes), rank, world, torch.device("cpu"))
+        for i in layer_block(n_layers, rank, world):
+            lg.send(i, _layer_tensors(i))
+        got = lg.wait()
+        if rank == 0:
+            ok = sorted(got) == list(range(n_layers))
+            for i in range(n_layers):
+                back = unflatten_bytes(got[i], _layer_tensors(i))
+                ok = ok and all(torch.equal(a.view(torch.uint8), b.view(torch.uint8))
+                                for a, b in zip(_layer_tensors(i), back))
+            q.put(ok)
+    finally:
+        dist.destroy_process_group()
+
+
+def _layer_tensors(i):
+    g = torch.Generator().manual_seed(7 + i)
+    return [torch.randint(0, 256, (33 + 5 * i,), generator=g, dtype=torch.uint8),
+            torch.randn(3 + i, generator=g).to(torch.bfloat16), torch.randn(2, generator=g)]
+
+
+@pytest.mark.parametrize("world,n_layers", [(2, 5), (3, 7)])
+def test_layer_gather_overlapped(world, n_layers):
+    """LayerGather: each rank sends its layers as it finishes them, rank 0
+    receives every layer at its exact size, matched in layer order."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_layer_gather_worker, args=(r, world, port, n_layers, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    for p in ps:
+        p.join(120)
+    assert all(p.exitcode == 0 for p in ps)
+    assert q.get(timeout=10) is True
