@@ -186,33 +186,6 @@ __device__ __forceinline__ void build_pair_lut(uint32_t* lut, uint32_t* tmp) {
   }
 }
 
-// The GEMV's copy of the table: 16 copies (16 KB, so that four blocks fit on
-// an SM), entry b of copy r at word 16 b + r; lane l reads copy l % 16 (lanes
-// l and l + 16 meet in a bank only when their entries differ and have equal
-// parity).
-constexpr int kPairLut16Words = 256 * 16;
-template <typename T>
-__device__ __forceinline__ void build_pair_lut16(uint32_t* lut, uint32_t* tmp) {
-  for (int b = threadIdx.x; b < 256; b += blockDim.x) {
-    union {
-      T h[2];
-      uint32_t u;
-    } pr;
-    pr.h[0] = Ty<T>::from_f(Ty<T>::round(kNF4[b & 15]));
-    pr.h[1] = Ty<T>::from_f(Ty<T>::round(kNF4[b >> 4]));
-    tmp[b] = pr.u;
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < kPairLut16Words / 4; i += blockDim.x) {
-    const uint32_t v = tmp[i >> 2];  // words 4i..4i+3 are copies of entry i / 4
-    reinterpret_cast<uint4*>(lut)[i] = make_uint4(v, v, v, v);
-  }
-}
-__device__ __forceinline__ uint32_t pair_lut16_off(uint32_t w, int b, uint32_t copy4) {
-  const uint32_t off = (b == 0 ? (w << 6) : (w >> (8 * b - 6))) & 0x3FC0u;
-  return off | copy4;
-}
-
 // Byte offset of the table word for byte b (0..3) of w, in copy `lane`.
 __device__ __forceinline__ uint32_t pair_lut_off(uint32_t w, int b, uint32_t lane4) {
   const uint32_t off = (b == 0 ? (w << 7) : (w >> (8 * b - 7))) & 0x7F80u;
@@ -422,6 +395,8 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
     const int q = warp & 3;          // tensor-memory lane quarter
     const int h = wi >> 2;           // half of each 64-wide K half (A slot columns 16h..16h+15)
     const int row = q * 32 + lane;   // weight row within the tile
+    // the row's bias, requested now and added in the epilogue
+    const float b = bias ? __ldg(&bias[nt * kRows + row]) : 0.0f;
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
     const uint32_t sbase = smem_u32(smem);
     bool ok = true;
@@ -497,7 +472,6 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
     if (ok && mbar_wait_warp(acc_full, 0)) {
       tc_fence_after();
       const int n = nt * kRows + row;
-      const float b = bias ? bias[n] : 0.0f;
 #pragma unroll 1
       for (int c = 32 * (dw >> 2); c < BT; c += 64 * kDG) {
         uint32_t v[32];
@@ -695,7 +669,7 @@ __global__ void __launch_bounds__(32 * (kGvWarps + 1), 1) w4a16_gemv_kernel(cons
   extern __shared__ __align__(128) uint8_t gv_smem[];
   uint8_t* p = gv_smem;
   uint32_t* lut = reinterpret_cast<uint32_t*>(p);  // NF: pair table (+1 KB build space)
-  if (NF) p += kPairLut16Words * 4 + 1024;
+  if (NF) p += kPairLutWords * 4 + 1024;
   float* red = reinterpret_cast<float*>(p);  // [2][warps][NT * 128] slab shares, fragment order
   p += 2 * kGvWarps * NT * 512;
   int* cnt = reinterpret_cast<int*>(p);  // [2] warps done with the buffer's slab
@@ -739,7 +713,7 @@ __global__ void __launch_bounds__(32 * (kGvWarps + 1), 1) w4a16_gemv_kernel(cons
     }
     for (int u = 0; u < stages && u < n_units; ++u) issue(u);
   }
-  if constexpr (NF) build_pair_lut16<T>(lut, reinterpret_cast<uint32_t*>(gv_smem + kPairLut16Words * 4));
+  if constexpr (NF) build_pair_lut<T>(lut, reinterpret_cast<uint32_t*>(gv_smem + kPairLutWords * 4));
   __syncthreads();
   bool ok = XS ? mbar_wait(xbar, 0) : true;
   if constexpr (!NF) {
@@ -797,7 +771,7 @@ __global__ void __launch_bounds__(32 * (kGvWarps + 1), 1) w4a16_gemv_kernel(cons
     xoff[j] = (uint32_t)(tok * gv_xpitch_bytes(a.K) + 32 * c);
     xoffg[j] = (int64_t)tok * a.K * 2 + 32 * c;
   }
-  const uint32_t copy4 = (uint32_t)(lane & 15) << 2;
+  const uint32_t lane4 = (uint32_t)lane << 2;  // NF4: the lane's copy of the pair table
   float acc[NT][4];
 #pragma unroll
   for (int j = 0; j < NT; ++j)
@@ -805,7 +779,14 @@ __global__ void __launch_bounds__(32 * (kGvWarps + 1), 1) w4a16_gemv_kernel(cons
     for (int e = 0; e < 4; ++e) acc[j][e] = 0.0f;
   int sl = 0, ch = 0, si = 0;
   uint32_t par = 0;
+  float bias_r[2] = {0.0f, 0.0f};  // bias of the lane's rows of the current slab
   for (int u = 0; u < n_units; ++u) {
+    if (ch == 0 && bias) {
+      // requested at the slab's start, used when (if) this warp writes it out
+      const int row = (blockIdx.x + si * gridDim.x) * 16 + (lane >> 2);
+      bias_r[0] = __ldg(&bias[row]);
+      bias_r[1] = __ldg(&bias[row + 8]);
+    }
     if (!(ok && mbar_wait(&full[sl], par))) {
       if (lane == 0) atomicExch(err, 5);
       break;
@@ -855,7 +836,7 @@ __global__ void __launch_bounds__(32 * (kGvWarps + 1), 1) w4a16_gemv_kernel(cons
               uint32_t af[4];
               if constexpr (NF) {
 #pragma unroll
-                for (int b = 0; b < 4; ++b) af[b] = lds_b32(lut_a + pair_lut16_off(word_of(cw[q], t), b, copy4));
+                for (int b = 0; b < 4; ++b) af[b] = lds_b32(lut_a + pair_lut_off(word_of(cw[q], t), b, lane4));
               } else {
                 GvInt4<T>::frag(word_of(cw[q], t), af);
               }
@@ -970,7 +951,7 @@ __global__ void __launch_bounds__(32 * (kGvWarps + 1), 1) w4a16_gemv_kernel(cons
             const int tok = 8 * j + 2 * (lane & 3) + (e & 1);
             if (tok >= a.M) continue;
             const int row = slab * 16 + (lane >> 2) + (e >= 2 ? 8 : 0);
-            y[(size_t)tok * a.N + row] = Ty<T>::from_f(bias ? __fadd_rn(vals[e], bias[row]) : vals[e]);
+            y[(size_t)tok * a.N + row] = Ty<T>::from_f(bias ? __fadd_rn(vals[e], bias_r[e >> 1]) : vals[e]);
           }
         }
         __syncwarp();
@@ -994,7 +975,7 @@ __global__ void __launch_bounds__(32 * (kGvWarps + 1), 1) w4a16_gemv_kernel(cons
 // shares and counters, barriers, group sums (INT4), activations (XS).
 inline int gv_fixed_smem(bool nf, bool xs, int NT, int M, int K, int G) {
   const int n_grp = K / G;
-  return (nf ? kPairLut16Words * 4 + 1024 : 0) + 2 * kGvWarps * NT * 512 + 128 +
+  return (nf ? kPairLutWords * 4 + 1024 : 0) + 2 * kGvWarps * NT * 512 + 128 +
          2 * kGvMaxStages * 8 + 128 + (nf ? 0 : ((n_grp * 64 + 127) / 128) * 128) +
          (xs ? ((M * gv_xpitch_bytes(K) + 127) / 128) * 128 : 0);
 }
