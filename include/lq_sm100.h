@@ -330,6 +330,18 @@ size_t lq_nf4_linear_packed_bytes(int64_t N, int64_t K);
 int lq_nf4_linear_lora(const void* x, int act_dtype, int64_t M, int64_t N, int64_t K,
                        const void* packed, const float* bias, const void* lora_u,
                        const void* lora_b, int64_t rank, void* y, int* err, void* stream);
+/* lq_nf4_qlora_forward: QLoRALinear.forward whole (qlora.py:306-312) in two
+ * launches: lq_lora_u (u = scaling * x @ lora_a^T into the caller's u
+ * workspace, [M, 64] act_dtype) and the fused kernel of lq_nf4_linear_lora,
+ * which runs as a programmatic dependent of the first: its base product
+ * starts while u is computed, only the LoRA step waits for u.  lora_a in
+ * LQ_F32 or act_dtype, lora_b [N, rank] act_dtype; limits as for
+ * lq_nf4_linear_lora. */
+int lq_nf4_qlora_forward(const void* x, int act_dtype, int64_t M, int64_t N, int64_t K,
+                         const void* packed, const float* bias, const void* lora_a, int a_dtype,
+                         const void* lora_b, int64_t rank, float scaling, void* u, void* y, int* err,
+                         void* stream);
+
 /* lq_lora_u: the LoRA down-projection of QLoRALinear.forward (qlora.py:311,
  * F.linear(x, lora_A) * scaling) as the u operand of lq_nf4_linear_lora:
  * u[M, 64] (act_dtype) = scaling * x[M, K] @ lora_a[rank, K]^T in columns

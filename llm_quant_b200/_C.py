@@ -69,6 +69,7 @@ _SIGS = {
     "lq_nf4_linear": [_V, _I, _L, _L, _L, _V, _V, _V, _V, _V],
     "lq_nf4_linear_lora": [_V, _I, _L, _L, _L, _V, _V, _V, _V, _L, _V, _V, _V],
     "lq_lora_u": [_V, _I, _L, _L, _V, _I, _L, ctypes.c_float, _V, _V],
+    "lq_nf4_qlora_forward": [_V, _I, _L, _L, _L, _V, _V, _V, _I, _V, _L, ctypes.c_float, _V, _V, _V, _V],
     "lq_nf4_merge_lora": [_V, _L, _L, _L, _L, _V, _V, _V, _I, _V, _V, _I, _L, ctypes.c_float,
                           _V, _I, _V],
     "lq_sparse_row_add": [_V, _I, _L, _L, _L, _V, _V, _L, _V, _V, _V, _V],

@@ -139,6 +139,10 @@ template <> struct Act<__nv_bfloat16> {
 struct W4Args {
   int M, N, K, group, n_kb, n_groups;
   int kb_shift;  // log2(group / kBK) when that is a power of two, else -1
+  // 1: launched right behind the kernel that writes u (lq_nf4_qlora_forward),
+  // so only u's load waits for it; 0: every thread waits before its first
+  // global access (any predecessor)
+  int u_only_wait;
 };
 
 // The LoRA term of QLoRALinear.forward fused into the base product
@@ -149,6 +153,7 @@ struct LoraArgs {
   const void* u = nullptr;
   const void* b = nullptr;
   int r = 0;
+  int u_only_wait = 0;  // see W4Args
 };
 
 inline int kb_shift_of(int group) {
@@ -302,8 +307,9 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
   // With the LoRA term the kernel is launched as a programmatic dependent of
   // the u kernel: the set-up above overlaps that kernel's tail, and no thread
   // touches global memory before the previous kernel is complete (a no-op
-  // after an ordinary launch).
-  pdl_wait();
+  // after an ordinary launch) -- or, right behind lq_lora_u, whose only
+  // output is u, just the load of u waits (the base product runs meanwhile).
+  if (!a.u_only_wait) pdl_wait();
 
   if (warp == 0) {
     // ---------------- activation producer ----------------
@@ -320,8 +326,10 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
         for (int hk = 0; hk < WK; ++hk) {
           if (i < n_main)
             tma_load_2d(smem + L::off_x + s * L::kX + hk * L::kXh, &tmap_x, (i * WK + hk) * kBK, m0, &full_x[s]);
-          else  // u has 64 columns: the second half of a 128-wide stage is all fill (zeros)
+          else {  // u has 64 columns: the second half of a 128-wide stage is all fill (zeros)
+            if (hk == 0 && a.u_only_wait) pdl_wait();
             tma_load_2d(smem + L::off_x + s * L::kX + hk * L::kXh, &tmap_u, hk * kBK, m0, &full_x[s]);
+          }
         }
         issued = i + 1;
       }
@@ -1035,6 +1043,7 @@ int launch_gemv(const void* x, int M, int N, int K, int group, const void* packe
   a.n_kb = K / kBK;
   a.n_groups = K / group;
   a.kb_shift = kb_shift_of(group);
+  a.u_only_wait = 0;
   if (M > 8 || (!NF && group > 4 * kBK)) return 1;
   // the activations are copied to shared memory when they fit and their rows
   // start on 16-byte boundaries (K is a multiple of 64)
@@ -1264,6 +1273,7 @@ inline W4Args w4_args(int M, int N, int K, int group) {
   a.n_kb = K / kBK;
   a.n_groups = K / group;
   a.kb_shift = kb_shift_of(group);
+  a.u_only_wait = 0;
   return a;
 }
 
@@ -1278,7 +1288,8 @@ int launch_w4(const void* x, int M, int N, int K, int group, const void* packed,
   } else {
     umap = map;  // unused
   }
-  const W4Args a = w4_args(M, N, K, group);
+  W4Args a = w4_args(M, N, K, group);
+  a.u_only_wait = lo.r > 0 ? lo.u_only_wait : 0;
   auto kern = w4a16_kernel<T, BT, S, NF, WK>;
   const int smem_bytes = L::bytes > 117 * 1024 ? L::bytes : 117 * 1024;
   static std::atomic<uint64_t> attr_done{0};
@@ -1481,6 +1492,34 @@ extern "C" int lq_nf4_linear_lora(const void* x, int act_dtype, int64_t M, int64
   if (act_dtype == LQ_BF16) return w4_dispatch<__nv_bfloat16, true>(x, (int)M, (int)N, (int)K, kBK, packed, bias, y, err, st, lo);
   set_error("NF4 linear activations must be fp16 or bf16 (got dtype %d)", act_dtype);
   return LQ_EDTYPE;
+}
+
+extern "C" int lq_nf4_qlora_forward(const void* x, int act_dtype, int64_t M, int64_t N, int64_t K,
+                                    const void* packed, const float* bias, const void* lora_a, int a_dtype,
+                                    const void* lora_b, int64_t rank, float scaling, void* u, void* y,
+                                    int* err, void* stream) {
+  int rc = check_shape(N, K, kBK);
+  if (rc) return rc;
+  LQ_REQUIRE(M >= 0 && M < (1LL << 31), LQ_EINVAL, "bad M");
+  if (M == 0) return LQ_OK;
+  LQ_REQUIRE(x && packed && y && lora_a && lora_b && u, LQ_EINVAL, "NULL pointer");
+  LQ_REQUIRE(aligned16(x) && aligned16(packed) && aligned16(u) && aligned16(lora_b), LQ_EALIGN,
+             "x, packed, u and lora_b must be 16-byte aligned");
+  LQ_REQUIRE(rank >= 2 && rank % 2 == 0 && rank <= (M <= 8 ? kBK : 16), LQ_ERANGE,
+             "fused LoRA needs an even rank <= %d at M = %lld (got %lld)", M <= 8 ? kBK : 16,
+             (long long)M, (long long)rank);
+  LQ_REQUIRE(act_dtype == LQ_F16 || act_dtype == LQ_BF16, LQ_EDTYPE,
+             "NF4 linear activations must be fp16 or bf16 (got dtype %d)", act_dtype);
+  rc = lq_lora_u(x, act_dtype, M, K, lora_a, a_dtype, rank, scaling, u, stream);
+  if (rc) return rc;
+  LoraArgs lo;
+  lo.u = u;
+  lo.b = lora_b;
+  lo.r = (int)rank;
+  lo.u_only_wait = 1;  // the kernel ahead of it in the stream is lq_lora_u, which writes only u
+  cudaStream_t st = as_stream(stream);
+  if (act_dtype == LQ_F16) return w4_dispatch<__half, true>(x, (int)M, (int)N, (int)K, kBK, packed, bias, y, err, st, lo);
+  return w4_dispatch<__nv_bfloat16, true>(x, (int)M, (int)N, (int)K, kBK, packed, bias, y, err, st, lo);
 }
 
 extern "C" size_t lq_w4a16_packed_bytes(int64_t N, int64_t K, int64_t group) {

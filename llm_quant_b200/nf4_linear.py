@@ -174,11 +174,14 @@ def _lora_forward(ql, x: torch.Tensor, lora_a, lora_b, bias) -> torch.Tensor:
         b = bias.detach()
         if b.dtype != torch.float32 or not b.is_contiguous():
             b = b.float().contiguous()
-    u = _lora_u(ql, x2, lora_a.detach())
+    # u = scaling * x @ lora_A^T and the fused kernel, the second started
+    # behind the first (lq_nf4_qlora_forward)
+    a = _cast_cached(ql, "_lora_a_cast", lora_a.detach(), x2.dtype)
     lb = _lora_b(ql, lora_b.detach(), x.dtype)
-    _C.call("lq_nf4_linear_lora", x2.data_ptr(), _C.dt(x2), M, N, K, packed.data_ptr(), _C.ptr(b),
-            u.data_ptr(), lb.data_ptr(), ql.rank, y.data_ptr(), _err_flag(x.device).data_ptr(),
-            _C.stream_ptr(x2))
+    u = torch.empty(M, 64, dtype=x2.dtype, device=x2.device)
+    _C.call("lq_nf4_qlora_forward", x2.data_ptr(), _C.dt(x2), M, N, K, packed.data_ptr(), _C.ptr(b),
+            a.data_ptr(), _C.dt(a), lb.data_ptr(), ql.rank, float(ql.scaling), u.data_ptr(), y.data_ptr(),
+            _err_flag(x.device).data_ptr(), _C.stream_ptr(x2))
     return y.reshape(*x.shape[:-1], N)
 
 
