@@ -72,14 +72,16 @@ def unflatten_bytes(buf: torch.Tensor, like: Sequence[torch.Tensor]) -> List[tor
     return out
 
 
-def gather_to_rank0(local: torch.Tensor, group=None) -> List[torch.Tensor] | None:
+def gather_to_rank0(local: torch.Tensor, group=None, chunk_bytes: int = 64 << 20) -> List[torch.Tensor] | None:
     """Gather each rank's flat uint8 buffer to rank 0, exact sizes.
 
     One all_gather of the sizes; then every other rank sends its buffer to
-    rank 0 point to point, all transfers posted together (batch_isend_irecv)
-    so they overlap on rank 0's links.  Nothing is padded: a rank with fewer
-    layers sends fewer bytes.  Returns the per-rank buffers on rank 0 (its
-    own is `local` itself), None elsewhere."""
+    rank 0 point to point in pieces of at most `chunk_bytes`, all transfers
+    posted together (batch_isend_irecv) so they overlap on rank 0's links
+    (single transfers of ~1 GB from three peers at once measured 43 GB/s into
+    rank 0 on 4 B200s, against ~500 GB/s in pieces of tens of MB).  Nothing
+    is padded: a rank with fewer layers sends fewer bytes.  Returns the
+    per-rank buffers on rank 0 (its own is `local` itself), None elsewhere."""
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     dev = local.device
@@ -91,12 +93,16 @@ def gather_to_rank0(local: torch.Tensor, group=None) -> List[torch.Tensor] | Non
     def peer(r: int) -> int:
         return r if group is None else dist.get_global_rank(group, r)
 
+    def pieces(t: torch.Tensor, n: int):
+        return [t[o:o + chunk_bytes] for o in range(0, n, chunk_bytes)]
+
     if rank == 0:
         bufs = [local] + [torch.empty(sz, dtype=torch.uint8, device=dev) for sz in sizes[1:]]
-        ops = [dist.P2POp(dist.irecv, bufs[r], peer(r), group) for r in range(1, world) if sizes[r]]
+        ops = [dist.P2POp(dist.irecv, piece, peer(r), group)
+               for r in range(1, world) for piece in pieces(bufs[r], sizes[r])]
     else:
         bufs = None
-        ops = [dist.P2POp(dist.isend, local.contiguous(), peer(0), group)] if sizes[rank] else []
+        ops = [dist.P2POp(dist.isend, piece, peer(0), group) for piece in pieces(local.contiguous(), sizes[rank])]
     if ops:
         for req in dist.batch_isend_irecv(ops):
             req.wait()

@@ -65,7 +65,7 @@ def _oracle_pack(i):
                            "scales": torch.from_numpy(scales).to(torch.bfloat16)})
 
 
-def _worker(rank, world, port, num_layers, fail_rank, q):
+def _worker(rank, world, port, num_layers, fail_rank, q, chunk=None):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     from datetime import timedelta
@@ -75,7 +75,7 @@ def _worker(rank, world, port, num_layers, fail_rank, q):
             raise RuntimeError("injected failure on the host")
         layers = quantize_layers(num_layers, rank, world, _oracle_pack)
         flat = flatten_bytes([t for pl in layers for t in pl.tensors.values()])
-        got = gather_to_rank0(flat)
+        got = gather_to_rank0(flat) if chunk is None else gather_to_rank0(flat, chunk_bytes=chunk)
         if rank == 0:
             # rebuild every layer from the gathered bytes and compare
             out = []
@@ -95,11 +95,11 @@ def _worker(rank, world, port, num_layers, fail_rank, q):
             pass
 
 
-def _run(world, num_layers, fail_rank=-1):
+def _run(world, num_layers, fail_rank=-1, chunk=None):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, num_layers, fail_rank, q))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, num_layers, fail_rank, q, chunk))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -118,6 +118,14 @@ def test_gather_world2():
     msgs, codes = _run(2, 5)
     assert ("ok", True) in msgs, msgs
     assert codes == [0, 0]
+
+
+def test_gather_in_pieces_world3():
+    """Each rank's buffer goes in many small pieces (48 bytes), reassembled
+    in order on rank 0."""
+    msgs, codes = _run(3, 7, chunk=48)
+    assert ("ok", True) in msgs, msgs
+    assert codes == [0, 0, 0]
 
 
 def test_rank_failure_is_reported_not_hung():
