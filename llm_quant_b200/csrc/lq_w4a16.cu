@@ -641,9 +641,9 @@ int set_smem_once(Kern kern, int smem_bytes, std::atomic<uint64_t>& done) {
 // flight.  The 16 consumer warps split each chunk's groups and never wait
 // for one another: a warp stores its share of a slab (fp32, in one of two
 // buffers by slab parity) and the last of the 16 to do so adds the shares
-// and writes the slab's outputs.  With XS the activations (M rows of K halves, at most
-// 136 KB) are copied once into shared memory; otherwise the lanes read them
-// from global memory (L2).  For INT4 the block first forms S[group][token] =
+// and writes the slab's outputs.  With XS the activations (M rows of K
+// halves, at most 136 KB) are copied once into shared memory; otherwise the
+// lanes read them from global memory (L2).  For INT4 the block first forms S[group][token] =
 // the group's activation sums (fp32), which fold the zero points: a group adds
 // s (f D - (o + z) S) to its rows' outputs, D the MMA sum of the (o + q)
 // fragments.  The LoRA term is one more MMA pass per slab, lora_B's rows as A
