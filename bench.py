@@ -60,6 +60,7 @@ NCU_TRAFFIC = {
     "rotquant": 222.0e6 / (16384 * 4096),  # fht3_kernel, 3.31 B per element
     "kv": 277.2e6 / (8 * 8 * 8192 * 128),  # kv_dequant_seg_kernel, 4.13 B per element
     "w4a16": 44.7e6,                     # w4a16_kernel at M = 1024, bytes per launch
+    "qlora_linear": 48.19e6,             # w4a16_kernel<nf4> at M = 1024, bytes per launch
     "kv_attention": 70.5e6 / (8 * 8 * 4096),  # kv_attn_kernel, 269 B per cached token
 }
 
@@ -1222,10 +1223,14 @@ def profile_case(name, ctx):
         ql.pack_base(w)
         ql.requires_grad_(False)
         x = torch.randn(1024, 4096, generator=g, device=ctx.dev).to(torch.bfloat16)
-        for _ in range(3):
-            ql(x)
-        for _ in range(3):
-            ql(x[:1])
+        from llm_quant_b200 import nf4_linear
+        with torch.no_grad():
+            for _ in range(3):  # the base product alone (the bench's timed kernel)
+                nf4_linear.base_linear(ql, x)
+            for _ in range(3):
+                ql(x)
+            for _ in range(3):
+                ql(x[:1])
     torch.cuda.synchronize()
     print(f"profile case {name} done")
 

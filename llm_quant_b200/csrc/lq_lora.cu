@@ -89,7 +89,9 @@ __global__ void __launch_bounds__(32 * kLuWarps) lora_u_kernel(const T* __restri
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
-  const int64_t m0 = (int64_t)blockIdx.x * 16;
+  const int64_t n_tiles = (M + 15) / 16;
+  for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+  const int64_t m0 = tile * 16;
   // token rows of this lane (rows past M read row M - 1; never stored)
   const int64_t r0 = min(m0 + g, M - 1), r1 = min(m0 + g + 8, M - 1);
   float d[NTL][4];
@@ -150,11 +152,15 @@ __global__ void __launch_bounds__(32 * kLuWarps) lora_u_kernel(const T* __restri
     }
     reinterpret_cast<uint32_t*>(u + (m0 + row) * kLuPitch)[pr] = LuMma<T>::pack(v0, v1);
   }
+  __syncthreads();  // red is rewritten by the next tile
+  }
 }
 
 template <typename T, typename AT>
-int lora_u_t(const void* x, int64_t M, int64_t K, const void* a, int rank, float scaling, void* u, cudaStream_t st) {
-  const dim3 grid((unsigned)((M + 15) / 16));
+int lora_u_t(const void* x, int64_t M, int64_t K, const void* a, int rank, float scaling, void* u, cudaStream_t st,
+             int max_blocks) {
+  const int64_t tiles = (M + 15) / 16;
+  const dim3 grid((unsigned)(max_blocks > 0 && max_blocks < tiles ? max_blocks : tiles));
   const T* xp = static_cast<const T*>(x);
   const AT* ap = static_cast<const AT*>(a);
   T* up = static_cast<T*>(u);
@@ -168,11 +174,14 @@ int lora_u_t(const void* x, int64_t M, int64_t K, const void* a, int rank, float
 }
 
 }  // namespace
-}  // namespace lq
 
-extern "C" int lq_lora_u(const void* x, int act_dtype, int64_t M, int64_t K, const void* lora_a, int a_dtype,
-                         int64_t rank, float scaling, void* u, void* stream) {
-  using namespace lq;
+// lq_lora_u on at most max_blocks blocks (<= 0: one per 16-token tile), each
+// looping over its tiles.  A kernel queued behind it cannot share an SM with
+// these blocks when it takes a whole SM's shared memory; on fewer SMs the
+// down-projection takes longer but leaves the rest of the machine to that
+// kernel's first tiles.
+int lora_u_launch(const void* x, int act_dtype, int64_t M, int64_t K, const void* lora_a, int a_dtype, int64_t rank,
+                  float scaling, void* u, void* stream, int max_blocks) {
   LQ_REQUIRE(M >= 0 && M < (1LL << 31) && K >= 0 && K < (1LL << 31), LQ_EINVAL, "bad size");
   if (M == 0) return LQ_OK;
   LQ_REQUIRE(K % 64 == 0 && K > 0, LQ_EINVAL, "lora_u needs in_features %% 64 == 0 (got %lld)", (long long)K);
@@ -183,11 +192,18 @@ extern "C" int lq_lora_u(const void* x, int act_dtype, int64_t M, int64_t K, con
   LQ_REQUIRE(a_dtype == LQ_F32 || a_dtype == act_dtype, LQ_EDTYPE, "lora_A must be fp32 or the activation dtype");
   cudaStream_t st = as_stream(stream);
   if (act_dtype == LQ_F16)
-    return a_dtype == LQ_F32 ? lora_u_t<__half, float>(x, M, K, lora_a, (int)rank, scaling, u, st)
-                             : lora_u_t<__half, __half>(x, M, K, lora_a, (int)rank, scaling, u, st);
+    return a_dtype == LQ_F32 ? lora_u_t<__half, float>(x, M, K, lora_a, (int)rank, scaling, u, st, max_blocks)
+                             : lora_u_t<__half, __half>(x, M, K, lora_a, (int)rank, scaling, u, st, max_blocks);
   if (act_dtype == LQ_BF16)
-    return a_dtype == LQ_F32 ? lora_u_t<__nv_bfloat16, float>(x, M, K, lora_a, (int)rank, scaling, u, st)
-                             : lora_u_t<__nv_bfloat16, __nv_bfloat16>(x, M, K, lora_a, (int)rank, scaling, u, st);
+    return a_dtype == LQ_F32 ? lora_u_t<__nv_bfloat16, float>(x, M, K, lora_a, (int)rank, scaling, u, st, max_blocks)
+                             : lora_u_t<__nv_bfloat16, __nv_bfloat16>(x, M, K, lora_a, (int)rank, scaling, u, st, max_blocks);
   set_error("lora_u: activations must be fp16 or bf16 (got dtype %d)", act_dtype);
   return LQ_EDTYPE;
+}
+
+}  // namespace lq
+
+extern "C" int lq_lora_u(const void* x, int act_dtype, int64_t M, int64_t K, const void* lora_a, int a_dtype,
+                         int64_t rank, float scaling, void* u, void* stream) {
+  return lq::lora_u_launch(x, act_dtype, M, K, lora_a, a_dtype, rank, scaling, u, stream, 0);
 }

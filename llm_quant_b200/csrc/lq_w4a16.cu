@@ -35,6 +35,12 @@
 #include <initializer_list>
 
 namespace lq {
+// lq_lora.cu: lq_lora_u on at most max_blocks blocks (<= 0: no limit)
+int lora_u_launch(const void* x, int act_dtype, int64_t M, int64_t K, const void* lora_a, int a_dtype, int64_t rank,
+                  float scaling, void* u, void* stream, int max_blocks);
+}  // namespace lq
+
+namespace lq {
 namespace {
 
 constexpr int kBK = 64;           // K per stage (128 bytes of fp16)
@@ -168,12 +174,14 @@ __device__ __forceinline__ int group_of(const W4Args& a, int kb) {
 
 // NF4 weights (QLoRALinear): code byte b = elements 2i (low nibble) and
 // 2i+1 (high nibble) -> the pair (round_T(NF4[lo]), round_T(NF4[hi])).  The
-// 256-entry table is stored 32 times, entry b of copy r at word 32 b + r, so
-// lane r of a warp reads copy r and 32 independent lookups never share a
-// bank.  tmp holds the 256 pairs while the copies are written.  Every thread
-// of the block calls this (it synchronizes).
+// 256-entry table is stored C times (C = 32 or 16), entry b of copy r at word
+// C b + r; lane l reads copy l % C, so with 32 copies 32 independent lookups
+// never share a bank (with 16, lanes l and l + 16 meet when their entries
+// differ and have equal parity, for half the table's size).  tmp holds the
+// 256 pairs while the copies are written.  Every thread of the block calls
+// this (it synchronizes).
 constexpr int kPairLutWords = 256 * 32;
-template <typename T>
+template <typename T, int C = 32>
 __device__ __forceinline__ void build_pair_lut(uint32_t* lut, uint32_t* tmp) {
   for (int b = threadIdx.x; b < 256; b += blockDim.x) {
     union {
@@ -185,15 +193,19 @@ __device__ __forceinline__ void build_pair_lut(uint32_t* lut, uint32_t* tmp) {
     tmp[b] = pr.u;
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < kPairLutWords / 4; i += blockDim.x) {
-    const uint32_t v = tmp[i >> 3];  // words 4i..4i+3 are copies of entry i / 8
+  for (int i = threadIdx.x; i < 256 * C / 4; i += blockDim.x) {
+    const uint32_t v = tmp[(4 * i) / C];  // words 4i..4i+3 are copies of entry 4i / C
     reinterpret_cast<uint4*>(lut)[i] = make_uint4(v, v, v, v);
   }
 }
 
-// Byte offset of the table word for byte b (0..3) of w, in copy `lane`.
+// Byte offset of the table word for byte b (0..3) of w, in copy lane4 / 4
+// (lane4 = 4 * (lane % C)).
+template <int C = 32>
 __device__ __forceinline__ uint32_t pair_lut_off(uint32_t w, int b, uint32_t lane4) {
-  const uint32_t off = (b == 0 ? (w << 7) : (w >> (8 * b - 7))) & 0x7F80u;
+  constexpr int SH = C == 32 ? 7 : 6;  // log2 of the entry stride in bytes
+  constexpr uint32_t MASK = 255u << SH;
+  const uint32_t off = (b == 0 ? (w << SH) : (w >> (8 * b - SH))) & MASK;
   return off | lane4;
 }
 
@@ -220,7 +232,11 @@ struct Smem {
   static constexpr int kXh = BT * kBK * 2;  // activation bytes of one 64-wide half
   static constexpr int kX = WK * kXh;       // activation tile bytes per stage
   static constexpr int kWS = WK * (kWStage + kSStage);  // weight + pair bytes per stage
-  static constexpr int kRest = (NF ? kPairLutWords * 4 + 1024 : 0) + 2048;  // table, barriers, slack
+  // NF4 table copies: 16 for the wide tiles with 128-wide stages (room for
+  // three stages), 32 otherwise
+  static constexpr int kLutC = (NF && BT > 128 && WK == 2) ? 16 : 32;
+  static constexpr int kLutBytes = NF ? 256 * kLutC * 4 : 0;
+  static constexpr int kRest = (NF ? kLutBytes + 1024 : 0) + 2048;  // table, barriers, slack
   // 226 KB: a block's opt-in limit is 1 KB under the SM's 227 KB (a
   // 231648-byte layout failed cudaFuncSetAttribute, 231168 bytes launched)
   static constexpr int kBudget = 226 * 1024;
@@ -230,7 +246,7 @@ struct Smem {
   static constexpr int off_w = off_x + S * kX;                  // [SW][WK] weight halves
   static constexpr int off_s = off_w + SW * WK * kWStage;       // [SW][WK] pair halves
   static constexpr int off_lut = off_s + SW * WK * kSStage;     // NF4 pair table (NF only)
-  static constexpr int off_tmp = off_lut + (NF ? kPairLutWords * 4 : 0);
+  static constexpr int off_tmp = off_lut + kLutBytes;
   static constexpr int off_bar = off_tmp + (NF ? 1024 : 0);
   // barriers: full_x[S], a_full[S], empty[S], full_w[SW], w_empty[SW], acc_full
   static constexpr int n_bar = 3 * S + 2 * SW + 1;
@@ -298,7 +314,7 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   if constexpr (NF) {
-    build_pair_lut<T>(reinterpret_cast<uint32_t*>(smem + L::off_lut), reinterpret_cast<uint32_t*>(smem + L::off_tmp));
+    build_pair_lut<T, L::kLutC>(reinterpret_cast<uint32_t*>(smem + L::off_lut), reinterpret_cast<uint32_t*>(smem + L::off_tmp));
   }
   tc_fence_before();
   __syncthreads();
@@ -441,10 +457,10 @@ __global__ void __launch_bounds__(kW4Threads, 1) w4a16_kernel(const __grid_const
         if constexpr (NF) {
           // byte c = k pair (2c, 2c+1) -> table pair * scale = round_T(NF4 * scale)
           const uint32_t lb = sbase + L::off_lut;
-          const uint32_t l4 = (uint32_t)lane << 2;
+          const uint32_t l4 = (uint32_t)(lane % L::kLutC) << 2;
 #pragma unroll
           for (int c = 0; c < 16; ++c) {
-            const uint32_t pv = lds_b32(lb + pair_lut_off(w[c >> 2], c & 3, l4));
+            const uint32_t pv = lds_b32(lb + pair_lut_off<L::kLutC>(w[c >> 2], c & 3, l4));
             r[c] = Act<T>::mul2(pv, sc);
           }
         } else {
@@ -1330,8 +1346,8 @@ inline int pick_bt(int M, int N, std::initializer_list<int> cands, bool tensor_b
 }
 
 // K multiple of 128: 128-wide stages (WK = 2), as many as shared and tensor
-// memory allow (3 for the wide tiles, 4 up to BT = 128).  Otherwise, and for
-// NF4 past M = 128, 64-wide stages.
+// memory allow (3 for the wide tiles, 4 up to BT = 128).  Otherwise 64-wide
+// stages.
 template <typename T, bool NF>
 int w4_dispatch(const void* x, int M, int N, int K, int group, const void* packed,
                 const float* bias, void* y, int* err, cudaStream_t st, const LoraArgs& lo = LoraArgs()) {
@@ -1353,10 +1369,15 @@ int w4_dispatch(const void* x, int M, int N, int K, int group, const void* packe
         case 160: return launch_w4<T, 160, 3, NF, 2>(x, M, N, K, group, packed, bias, y, err, st, lo);
         default: return launch_w4<T, 256, 3, NF, 2>(x, M, N, K, group, packed, bias, y, err, st, lo);
       }
+    } else {
+      // NF4 past M = 128: with the 16-copy pair table three 128-wide stages
+      // fit up to BT = 224 (not 256: the weight ring would be one deep)
+      switch (pick_bt(M, N, {224, 192, 160}, true)) {
+        case 192: return launch_w4<T, 192, 3, NF, 2>(x, M, N, K, group, packed, bias, y, err, st, lo);
+        case 160: return launch_w4<T, 160, 3, NF, 2>(x, M, N, K, group, packed, bias, y, err, st, lo);
+        default: return launch_w4<T, 224, 3, NF, 2>(x, M, N, K, group, packed, bias, y, err, st, lo);
+      }
     }
-    // NF4 past M = 128: its 33 KB table leaves room for three 128-wide
-    // stages only up to BT = 192, which measured slower than five 64-wide
-    // stages at BT = 224 -- fall through
   }
   if (M <= 32) return launch_w4<T, 32, 8, NF, 1>(x, M, N, K, group, packed, bias, y, err, st, lo);
   if (M <= 64) return launch_w4<T, 64, 8, NF, 1>(x, M, N, K, group, packed, bias, y, err, st, lo);
@@ -1367,6 +1388,15 @@ int w4_dispatch(const void* x, int M, int N, int K, int group, const void* packe
     case 192: return launch_w4<T, 192, S, NF, 1>(x, M, N, K, group, packed, bias, y, err, st, lo);
     default: return launch_w4<T, 256, S, NF, 1>(x, M, N, K, group, packed, bias, y, err, st, lo);
   }
+}
+
+// The token-tile width w4_dispatch launches for M > 16 tokens.
+inline int w4_token_tile(bool nf, int M, int N, int K) {
+  if (M <= 32) return 32;
+  if (M <= 64) return 64;
+  if (M <= 128) return 128;
+  if (K % (2 * kBK) == 0) return nf ? pick_bt(M, N, {224, 192, 160}, true) : pick_bt(M, N, {256, 224, 192, 160}, true);
+  return pick_bt(M, N, {256, 224, 192}, false);
 }
 
 template <typename T, typename ST>
@@ -1510,7 +1540,20 @@ extern "C" int lq_nf4_qlora_forward(const void* x, int act_dtype, int64_t M, int
              (long long)M, (long long)rank);
   LQ_REQUIRE(act_dtype == LQ_F16 || act_dtype == LQ_BF16, LQ_EDTYPE,
              "NF4 linear activations must be fp16 or bf16 (got dtype %d)", act_dtype);
-  rc = lq_lora_u(x, act_dtype, M, K, lora_a, a_dtype, rank, scaling, u, stream);
+  // The fused kernel takes a whole SM per tile, so it starts on the SMs that
+  // the down-projection leaves free.  When its last wave of tiles leaves
+  // SMs idle, the down-projection runs on that many (at most 4 token tiles
+  // each; a block's tiles run one after another, about 3 us apiece): the
+  // other SMs start the base product at once and the ones it delays have a
+  // tile fewer to run (M = 1024, N = 14336: 32 blocks, 116.5 -> 113.9 us).
+  int lu_blocks = 0;
+  if (M > 16) {
+    const int sms = num_sms(), bt = w4_token_tile(true, (int)M, (int)N, (int)K);
+    const int64_t tiles = (N / kRows) * ((M + bt - 1) / bt);
+    const int idle = (int)(tiles % sms == 0 ? 0 : sms - tiles % sms);
+    if ((int64_t)idle * 4 >= (M + 15) / 16) lu_blocks = idle;
+  }
+  rc = lora_u_launch(x, act_dtype, M, K, lora_a, a_dtype, rank, scaling, u, stream, lu_blocks);
   if (rc) return rc;
   LoraArgs lo;
   lo.u = u;

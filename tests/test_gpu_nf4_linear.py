@@ -242,12 +242,14 @@ def test_lora_b_cast_follows_updates(L):
         _check(ql(x), _reference(ql, x))
 
 
-@pytest.mark.parametrize("M", [4, 300])
-def test_two_entry_points_agree(L, M):
+@pytest.mark.parametrize("M,N", [(4, 256), (300, 256), (1000, 14336)])
+def test_two_entry_points_agree(L, M, N):
     """lq_nf4_qlora_forward (u kernel + fused kernel started behind it) and
-    lq_lora_u followed by lq_nf4_linear_lora give bit-identical outputs."""
+    lq_lora_u followed by lq_nf4_linear_lora give bit-identical outputs.  At
+    M = 1000, N = 14336 the fused kernel's last wave leaves 32 SMs idle and the
+    u kernel runs on 32 blocks of two 16-token tiles each."""
     from llm_quant_b200 import _C, nf4_linear
-    ql, g = _module(L, 256, 1024, torch.bfloat16, 64, True, seed=M + 3, rank=16)
+    ql, g = _module(L, N, 1024, torch.bfloat16, 64, True, seed=M + 3, rank=16)
     with torch.no_grad():
         ql.lora_A.copy_(torch.randn(16, 1024, generator=g) * 0.05)
     x = torch.randn(M, 1024, generator=g).to(torch.bfloat16).cuda()
@@ -257,12 +259,12 @@ def test_two_entry_points_agree(L, M):
     a = ql.lora_A.detach().to(x.dtype).contiguous()
     lb = ql.lora_B.detach().to(x.dtype).contiguous()
     u = torch.empty(M, 64, dtype=x.dtype, device="cuda")
-    y2 = torch.empty(M, 256, dtype=x.dtype, device="cuda")
+    y2 = torch.empty(M, N, dtype=x.dtype, device="cuda")
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     st = _C.stream_ptr(x)
     _C.call("lq_lora_u", x.data_ptr(), _C.dt(x), M, 1024, a.data_ptr(), _C.dt(a), 16, float(ql.scaling),
             u.data_ptr(), st)
-    _C.call("lq_nf4_linear_lora", x.data_ptr(), _C.dt(x), M, 256, 1024, packed.data_ptr(),
+    _C.call("lq_nf4_linear_lora", x.data_ptr(), _C.dt(x), M, N, 1024, packed.data_ptr(),
             ql.bias.detach().float().contiguous().data_ptr(), u.data_ptr(), lb.data_ptr(), 16, y2.data_ptr(),
             err.data_ptr(), st)
     torch.cuda.synchronize()
