@@ -56,7 +56,7 @@ NUM_LAYERS = 32
 # which is why some ratios sit below the algorithmic bytes.
 NCU_TRAFFIC = {
     "nf4": 281.4e6 / (28672 * 4096),     # nf4_pack_g64_kernel, 2.40 B per weight
-    "group": 212.4e6 / (8192 * 4096),    # group_warp_kernel, 6.33 B per element
+    "group": 215.8e6 / (8192 * 4096),    # group_warp_kernel, 6.43 B per element
     "rotquant": 222.0e6 / (16384 * 4096),  # fht3_kernel, 3.31 B per element
     "kv": 277.2e6 / (8 * 8 * 8192 * 128),  # kv_dequant_seg_kernel, 4.13 B per element
     "w4a16": 44.7e6,                     # w4a16_kernel at M = 1024, bytes per launch

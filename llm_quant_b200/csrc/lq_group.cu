@@ -87,12 +87,14 @@ struct GroupArgs {
 //         quantization through ste_round, whose zero is +0.0 either way; not
 //         float codes, which keep the sign of a zero): t0 = x * rcp is within 2^-22 |t0| of fl32(x / scale),
 //         so t0 + zp is within 2^-22 |t0| + 2^-23 |t| of the reference's
-//         t; when it lies more than W = 2^-20 (|t0| + |t|) from every
+//         t; when it lies more than 2^-20 (|t0| + |t|) from every
 //         half-integer, both round to the same integer and t0 + zp stands in
-//         for t.  Otherwise (ties, values near a tie, non-finite) it divides.
+//         for t.  The window tested is wg = tie_window(...) >= 2^-20 (|t0| +
+//         |t|) for every element of the group.  Otherwise (ties, values near
+//         a tie, non-finite) it divides.
 //   fp16: divides.
 template <typename T, bool RINT_ONLY>
-__device__ __forceinline__ float quotient_zp(float v, float scale, float rcp, float zp, bool zp0) {
+__device__ __forceinline__ float quotient_zp(float v, float scale, float rcp, float zp, bool zp0, float wg) {
   if constexpr (std::is_same<T, __nv_bfloat16>::value) {
     const float p = __fmul_rn(v, rcp);
     float t = (fabsf(p) >= 1.17549435e-38f || v == 0.0f) ? Ty<T>::round(p) : tdiv<T>(v, scale);
@@ -100,8 +102,7 @@ __device__ __forceinline__ float quotient_zp(float v, float scale, float rcp, fl
   } else if constexpr (std::is_same<T, float>::value && RINT_ONLY) {
     const float t0 = __fmul_rn(v, rcp);
     const float t = zp0 ? t0 : __fadd_rn(t0, zp);
-    const float w = __fmul_rn(__fadd_rn(fabsf(t0), fabsf(t)), 9.5367431640625e-07f);  // 2^-20
-    if (__fsub_rn(0.5f, fabsf(__fsub_rn(t, rintf(t)))) > w) return t;
+    if (__fsub_rn(0.5f, fabsf(__fsub_rn(t, rintf(t)))) > wg) return t;
     const float e = tdiv<T>(v, scale);
     return zp0 ? e : tadd<T>(e, zp);
   } else {
@@ -110,10 +111,22 @@ __device__ __forceinline__ float quotient_zp(float v, float scale, float rcp, fl
   }
 }
 
+// A bound, over a group, of the window 2^-20 (|t0| + |t|) that quotient_zp
+// tests against: |t0| = fl(|x| |rcp|) <= fl(amax |rcp|) and |t| <=
+// fl(|t0| + |zp|), and rounding is monotone, so every element's own window is
+// at most this.  NaN when the group holds a NaN or an infinity (amax or rcp
+// gives NaN): then every element divides.
+__device__ __forceinline__ float tie_window(const MinMax& r, bool sym, float rcp, float zp) {
+  const float amax = sym ? r.mx : fmax_nan(fabsf(r.mn), fabsf(r.mx));
+  const float a = __fmul_rn(amax, fabsf(rcp));
+  const float t = __fadd_rn(a, fabsf(zp));
+  return __fmul_rn(__fadd_rn(a, t), 9.5367431640625e-07f);  // 2^-20
+}
+
 template <typename T, int MODE, bool RINT_ONLY>
 __device__ __forceinline__ float apply_q(float v, float scale, float rcp, float zp, float qmin,
-                                         float qmax, bool zp0) {
-  const float t = quotient_zp<T, RINT_ONLY>(v, scale, rcp, zp, zp0);
+                                         float qmax, bool zp0, float wg) {
+  const float t = quotient_zp<T, RINT_ONLY>(v, scale, rcp, zp, zp0, wg);
   if constexpr (MODE == MODE_FAKE) {
     float q = tclamp_t<T>(tste(t), qmin, qmax);
     return tmul<T>(zp0 ? q : tsub<T>(q, zp), scale);
@@ -187,20 +200,61 @@ struct Tile {
   template <int MODE, typename OutT>
   __device__ __forceinline__ void emit(OutT* __restrict__ out, int64_t row, int64_t gcol0,
                                        const GroupArgs& a, int t, int tps, float scale,
-                                       float zp) {
+                                       float zp, const MinMax& r) {
     OutT* base = out + a.out_row(row) * a.cols + gcol0;
     const float rcp = __frcp_rn(scale);
-#pragma unroll
-    for (int k = 0; k < NVT; ++k) {
-      if (!(inb & (1u << k))) continue;
-      int64_t e = (int64_t)(k * tps + t) * V;
-      float o[V];
-#pragma unroll
-      for (int i = 0; i < V; ++i) o[i] = apply_q<T, MODE, rint_only<MODE, OutT, T>()>(v[k * V + i], scale, rcp, zp, a.qmin, a.qmax, zp0_ok<MODE, OutT, T>(a));
+    const float wg = tie_window(r, a.sym, rcp, zp);
+    constexpr bool kFast = std::is_same<T, float>::value && rint_only<MODE, OutT, T>();
+    const bool zp0 = zp0_ok<MODE, OutT, T>(a);
+    auto put = [&](int k, const float* o) {
+      const int64_t e = (int64_t)(k * tps + t) * V;
       if constexpr (VEC) {
         store_vec<OutT, T, V>(base + e, o);
       } else {
         if (gcol0 + e < a.cols) base[e] = Store<OutT, T>::cv(o[0]);
+      }
+    };
+    bool slow = !kFast;
+    if constexpr (kFast) {
+      // fp32 codes / fake quantization from the product quotient.  Where
+      // t = x rcp (+ zp) is finite and more than wg from a half-integer (the
+      // test of quotient_zp), r = rint(t) is the nearest integer and r - t is
+      // exact (Sterbenz for |t| >= 0.5, -t below), so ste_round(t) =
+      // t + (r - t) = r with a zero made +0.0 (r + 0.0), and clamp on a finite
+      // value is min / max.  A thread with any other element rewrites its
+      // outputs through apply_q below (ties, values within wg of one,
+      // non-finite groups).  (Testing rint(x rcp) and clamping it to
+      // [qmin - zp, qmax - zp] instead saves two adds per element but
+      // measured 3 % slower.)
+#pragma unroll
+      for (int k = 0; k < NVT; ++k) {
+        if (!(inb & (1u << k))) continue;
+        float o[V];
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+          const float t0 = __fmul_rn(v[k * V + i], rcp);
+          const float tq = zp0 ? t0 : __fadd_rn(t0, zp);
+          const float rq = rintf(tq);
+          slow |= !(__fsub_rn(0.5f, fabsf(__fsub_rn(tq, rq))) > wg);
+          if constexpr (MODE == MODE_FAKE) {
+            const float q = fminf(fmaxf(__fadd_rn(rq, 0.0f), a.qmin), a.qmax);
+            o[i] = __fmul_rn(zp0 ? q : __fsub_rn(q, zp), scale);
+          } else {
+            o[i] = fminf(fmaxf(rq, a.qmin), a.qmax);
+          }
+        }
+        put(k, o);
+      }
+    }
+    if (slow) {
+#pragma unroll
+      for (int k = 0; k < NVT; ++k) {
+        if (!(inb & (1u << k))) continue;
+        float o[V];
+#pragma unroll
+        for (int i = 0; i < V; ++i)
+          o[i] = apply_q<T, MODE, rint_only<MODE, OutT, T>()>(v[k * V + i], scale, rcp, zp, a.qmin, a.qmax, zp0, wg);
+        put(k, o);
       }
     }
   }
@@ -244,7 +298,7 @@ __global__ void __launch_bounds__(256) group_warp_kernel(const T* __restrict__ x
         scale_out[si] = Ty<T>::from_f(scale);
         zp_out[si] = Ty<T>::from_f(zp);
       }
-      if constexpr (MODE != MODE_QPARAMS) tile.template emit<MODE>(out, row, gcol0, a, t, tps, scale, zp);
+      if constexpr (MODE != MODE_QPARAMS) tile.template emit<MODE>(out, row, gcol0, a, t, tps, scale, zp, r);
     }
     tile = next;
   }
@@ -285,7 +339,7 @@ __global__ void __launch_bounds__(1024) group_block_kernel(const T* __restrict__
       scale_out[si] = Ty<T>::from_f(scale);
       zp_out[si] = Ty<T>::from_f(zp);
     }
-    if constexpr (MODE != MODE_QPARAMS) tile.template emit<MODE>(out, row, gcol0, a, t, tps, scale, zp);
+    if constexpr (MODE != MODE_QPARAMS) tile.template emit<MODE>(out, row, gcol0, a, t, tps, scale, zp, r);
   }
 }
 
@@ -319,8 +373,9 @@ __global__ void __launch_bounds__(1024) group_stream_kernel(const T* __restrict_
     if constexpr (MODE != MODE_QPARAMS) {
       OutT* ob = out + a.out_row(row) * a.cols + gcol0;
       const float rcp = __frcp_rn(scale);
+      const float wg = tie_window(r, a.sym, rcp, zp);
       for (int64_t e = threadIdx.x; e < a.G && gcol0 + e < a.cols; e += blockDim.x)
-        ob[e] = Store<OutT, T>::cv(apply_q<T, MODE, rint_only<MODE, OutT, T>()>(Ty<T>::to_f(base[e]), scale, rcp, zp, a.qmin, a.qmax, zp0_ok<MODE, OutT, T>(a)));
+        ob[e] = Store<OutT, T>::cv(apply_q<T, MODE, rint_only<MODE, OutT, T>()>(Ty<T>::to_f(base[e]), scale, rcp, zp, a.qmin, a.qmax, zp0_ok<MODE, OutT, T>(a), wg));
     }
   }
 }

@@ -178,3 +178,49 @@ def test_fake_quantize_gradient_flows(L):
     y = L.fake_quantize(x, n_bits=8)
     y.sum().backward()
     assert x.grad is not None and x.grad.shape == x.shape
+
+
+def _tie_groups(sym, shift, seed):
+    """16 rows x 4 groups of 128 fp32 values whose quotient x / scale lands on
+    half-integers (ties), one ulp either side of them, and on integers: each
+    group spans exactly 15 (asymmetric 4-bit: scale 1, zero point -min) or has
+    max |x| = 7 (symmetric: scale 1).  Row 3 holds a NaN, row 5 an inf."""
+    rng = np.random.default_rng(seed)
+    x = np.empty((16, 512), np.float32)
+    for r in range(16):
+        for g in range(4):
+            if sym:
+                v = rng.integers(-12, 13, 128) / 2.0
+                v[0] = 7.0 if g % 2 == 0 else -7.0
+            else:
+                v = rng.integers(2, 29, 128) / 2.0 + shift
+                v[0], v[1] = shift, 15.0 + shift
+            v = v.astype(np.float32)
+            k = rng.choice(np.arange(2, 128), 24, replace=False)
+            v[k[:12]] = np.nextafter(v[k[:12]], np.float32(np.inf))
+            v[k[12:]] = np.nextafter(v[k[12:]], np.float32(-np.inf))
+            x[r, 128 * g:128 * (g + 1)] = v
+    x[3, 77] = np.nan
+    x[5, 300] = np.inf
+    return x
+
+
+@pytest.mark.parametrize("sym,shift", [(False, 0.0), (False, -3.0), (False, -6.5), (True, 0.0)])
+def test_fp32_group_ties(L, sym, shift):
+    """fp32 per-group fake quantization and int8 codes where the quotient
+    sits on, or one ulp beside, a rounding tie: the kernel's product-quotient
+    path must hand these elements to the exact division (half to even, as the
+    reference's torch.round)."""
+    x = _tie_groups(sym, shift, seed=int(10 * shift) + 5 * sym + 100)
+    scale, _ = O.compute_qparams(x, "float32", 4, sym, "per_group", 128)
+    finite = np.isfinite(scale.reshape(16, 4))
+    assert finite[[0, 1, 2, 4, 6]].all() and np.all(scale.reshape(16, 4)[finite] == 1.0)
+    fq = L.fake_quantize(to_dev(x, "float32"), 4, sym, L.QScheme.PER_GROUP, 128)
+    assert same_bits(to_np(fq), O.fake_quantize(x, "float32", 4, sym, "per_group", 128))
+    xs = np.nan_to_num(x, nan=0.0, posinf=15.0)  # codes: finite weights
+    lin = torch.nn.Linear(512, 16, bias=False).cuda()
+    with torch.no_grad():
+        lin.weight.copy_(torch.from_numpy(xs))
+    ql = L.QuantizedLinear.from_linear(lin, 4, sym, 128)
+    wi, _, _ = O.quantized_linear_quantize_weights(xs, "float32", 4, sym, 128)
+    assert np.array_equal(to_np(ql.weight_int), wi)
