@@ -91,6 +91,17 @@ def _tensor_qparams(x: torch.Tensor, n_bits: int, symmetric: bool):
     return scale, zp
 
 
+def _check_reduce_dims(x: torch.Tensor, keep_dim: int, symmetric: bool) -> None:
+    """The reference reduces with torch.amin / amax over every dim but the
+    channel dim (core/quantizer.py:64-104), which raises IndexError for a
+    zero-size reduced dim; an empty x whose reduced dims are all non-empty
+    gives empty results instead."""
+    for d in range(x.ndim):
+        if d != keep_dim and x.shape[d] == 0:
+            op = "amax" if symmetric else "amin"
+            raise IndexError(f"{op}(): Expected reduction dim {d} to have non-zero size.")
+
+
 def _group_qparams(x2: torch.Tensor, group: int, n_bits: int, symmetric: bool):
     rows, cols = x2.shape
     ng = math.ceil(cols / group)
@@ -132,6 +143,10 @@ def compute_qparams(
             s, z = _tensor_qparams(xc, n_bits, symmetric)
             return s.reshape(keep), z.reshape(keep) if not symmetric else torch.zeros_like(s.reshape(keep))
         keep[channel_dim] = x.shape[channel_dim]
+        _check_reduce_dims(x, channel_dim, symmetric)
+        if x.numel() == 0:
+            s = torch.empty(keep, dtype=x.dtype, device=x.device)
+            return s, torch.empty_like(s)
         if channel_dim == 0:
             s, z = _group_qparams(xc.reshape(x.shape[0], -1), max(1, xc[0].numel()), n_bits, symmetric)
             return s.reshape(keep), z.reshape(keep)
@@ -256,12 +271,16 @@ def _fake_quant_forward(x, n_bits, symmetric, sch, group_size):
         return _affine(_C.AFFINE_FAKE, xc, s, z, xc.dtype, xc.dtype, n_bits, symmetric, xc.dtype)
     if sch == "per_channel":
         assert x.ndim >= 2, "per-channel requires at least 2-D tensor"
+        _check_reduce_dims(x, 0, symmetric)
         rows = x.shape[0]
         cols = xc.numel() // max(1, rows)
         group = max(1, cols)
     else:
         assert x.ndim == 2, "per-group requires a 2-D weight matrix"
         rows, cols = x.shape
+        if rows == 0:  # the reference reshapes to [out_features, -1]
+            raise RuntimeError("cannot reshape tensor of 0 elements into shape [0, -1] because the "
+                               "unspecified dimension size -1 can be any value and is ambiguous")
         group = group_size
     _C.call("lq_group_quant", xc.data_ptr(), _C.dt(xc), rows, cols, group, n_bits,
             int(symmetric), _C.MODE_FAKE, out.data_ptr(), _C.dt(out), None, None,

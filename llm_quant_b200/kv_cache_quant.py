@@ -108,12 +108,24 @@ class KVCacheQuantizer:
                 scale.data_ptr(), zp.data_ptr(), _C.stream_ptr(x))
         return out, scale, zp
 
+    def _check_reduce(self, x: torch.Tensor, g: str) -> None:
+        """The reference reduces with torch.amin / amax over the head dim
+        (per-token) or the token dim (per-channel), which raises IndexError when
+        that dim has size zero."""
+        if g == "per_group":
+            return
+        d = -1 if g == "per_token" else -2
+        if x.ndim >= 2 and x.shape[d] == 0:
+            op = "amax" if self.symmetric else "amin"
+            raise IndexError(f"{op}(): Expected reduction dim {d} to have non-zero size.")
+
     # -- reference API -----------------------------------------------------------
     def _compute_qparams(self, x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
         """Scale / zero point broadcastable to x (kv_cache_quant.py:102-139)."""
         g = _gran(self.granularity)
         if g == "per_group":
             return self._compute_qparams_grouped(x)
+        self._check_reduce(x, g)
         xc = self._prep(x, "KVCacheQuantizer")
         if g == "per_token":
             _, s, z = self._per_token(xc, _C.MODE_QPARAMS, None)
@@ -134,6 +146,7 @@ class KVCacheQuantizer:
         g = _gran(self.granularity)
         if g == "per_group":
             return self._quantize_grouped(x)
+        self._check_reduce(x, g)
         xc = self._prep(x, "KVCacheQuantizer.quantize")
         if g == "per_token":
             return self._per_token(xc, _C.MODE_CODES, self._code_dtype)
@@ -254,7 +267,7 @@ class _CacheSide:
 
     def _grow(self, need_t: int, need_g: int):
         B, H, D = self.B, self.H, self.D
-        if need_t > self.cap:
+        if need_t > self.cap or self.codes is None:  # storage exists from the first chunk on
             cap = max(need_t, 2 * self.cap, 64)
             cap = (cap + 15) // 16 * 16  # whole 16-token tiles for lq_kv_attention
             codes = torch.empty(B, H, cap, D, dtype=self.code_dtype, device=self.device)
@@ -291,6 +304,9 @@ class _CacheSide:
             raise TypeError(f"QuantizedKVCache: new chunk dtype {x.dtype} != cached {self.dtype}")
         xc = x.detach().contiguous()
         tn = xc.shape[2]
+        if tn == 0:  # nothing to store; raises where the reference's quantizer would
+            self.qz._check_reduce(xc, self.gran)
+            return
         gn = self._groups_for(tn)
         self._grow(self.T + tn, self.ng + gn)
         gcode = _GRAN_CODE[self.gran]
