@@ -804,12 +804,31 @@ __global__ void __launch_bounds__(32 * (kGvWarps + 1), 1) w4a16_gemv_kernel(cons
   int sl = 0, ch = 0, si = 0;
   uint32_t par = 0;
   float bias_r[2] = {0.0f, 0.0f};  // bias of the lane's rows of the current slab
+  // LoRA: warp w < rank / 16 adds rank columns 16 w .. 16 w + 15 of every slab
+  // (u . lora_B^T, one MMA per token tile).  Its lora_B fragment is requested
+  // at the slab's start; u is the same for every slab and read once, at the
+  // first slab's end -- right behind lq_lora_u (a.u_only_wait) only after
+  // griddepcontrol.wait, so the weights stream while u is computed.
+  const bool lora_w = lora_r > 0 && warp * 16 < lora_r;
+  uint32_t lb_r[4] = {0u, 0u, 0u, 0u};
+  uint32_t u_r[NT][2];
+  bool u_ready = false;
   for (int u = 0; u < n_units; ++u) {
     if (ch == 0 && bias) {
       // requested at the slab's start, used when (if) this warp writes it out
       const int row = (blockIdx.x + si * gridDim.x) * 16 + (lane >> 2);
       bias_r[0] = __ldg(&bias[row]);
       bias_r[1] = __ldg(&bias[row + 8]);
+    }
+    if (ch == 0 && lora_w) {
+      // A fragment: rows g, g + 8 of the slab x rank columns 2c, 2c + 8 (+1) of
+      // this warp's tile (0 past the rank)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int row = (blockIdx.x + si * gridDim.x) * 16 + g + (q & 1) * 8;
+        const int col = 16 * warp + 2 * c + (q >> 1) * 8;
+        lb_r[q] = col < lora_r ? __ldg(reinterpret_cast<const unsigned int*>(lora_b + (size_t)row * lora_r + col)) : 0u;
+      }
     }
     if (!(ok && mbar_wait(&full[sl], par))) {
       if (lane == 0) atomicExch(err, 5);
@@ -916,21 +935,19 @@ __global__ void __launch_bounds__(32 * (kGvWarps + 1), 1) w4a16_gemv_kernel(cons
     if (lane == 0) mbar_arrive(&empty[sl]);  // the slot may be refilled
     if (ch == n_chunk - 1) {
       const int slab = blockIdx.x + si * gridDim.x;
-      if (warp == 0 && lora_r > 0) {
-        // LoRA: + u[tok] . lora_B[row], 16-wide rank tiles (columns past r read as 0)
-        for (int k0 = 0; k0 < lora_r; k0 += 16) {
-          uint32_t af[4];
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int row = slab * 16 + g + (q & 1) * 8, col = k0 + 2 * c + (q >> 1) * 8;
-            af[q] = col < lora_r ? *reinterpret_cast<const uint32_t*>(lora_b + (size_t)row * lora_r + col) : 0u;
-          }
+      if (lora_w) {
+        if (!u_ready) {
+          if (a.u_only_wait) pdl_wait();
 #pragma unroll
           for (int j = 0; j < NT; ++j) {
-            const T* ur = lora_u + (size_t)(8 * j + g < a.M ? 8 * j + g : 0) * kBK + k0 + 2 * c;
-            MmaOp<T>::mma(acc[j], af, *reinterpret_cast<const uint32_t*>(ur), *reinterpret_cast<const uint32_t*>(ur + 8));
+            const T* ur = lora_u + (size_t)(8 * j + g < a.M ? 8 * j + g : 0) * kBK + 16 * warp + 2 * c;
+            u_r[j][0] = *reinterpret_cast<const uint32_t*>(ur);
+            u_r[j][1] = *reinterpret_cast<const uint32_t*>(ur + 8);
           }
+          u_ready = true;
         }
+#pragma unroll
+        for (int j = 0; j < NT; ++j) MmaOp<T>::mma(acc[j], lb_r, u_r[j][0], u_r[j][1]);
       }
       // this warp's share of the slab into its slot of buffer si % 2 (free
       // once slab si - 2 is written out); the last of the 16 adds the slots
@@ -1031,6 +1048,18 @@ int launch_gemv_nt(const W4Args& a, const void* x, const void* packed, const flo
   auto kern = w4a16_gemv_kernel<T, NF, NT, XS, SPG>;
   LQ_TRY(set_smem_once(kern, kGvSmemMax, attr_done));
   const int n_slab = a.N / 16;
+  if (a.u_only_wait) {
+    // right behind lq_lora_u (one block here): a programmatic dependent on the
+    // SMs that block leaves free, started before u is done
+    const int sms = num_sms() - 1;
+    const int grid = n_slab < sms ? n_slab : sms;
+    const cudaError_t e = launch_pdl(kern, dim3((unsigned)grid), dim3(32 * (kGvWarps + 1)), (size_t)smem, st,
+                                     static_cast<const T*>(x), static_cast<const uint8_t*>(packed), bias,
+                                     static_cast<T*>(y), a, v, err, static_cast<const T*>(lo.u),
+                                     static_cast<const T*>(lo.b), lo.r);
+    LQ_REQUIRE(e == cudaSuccess, LQ_ECUDA, "w4a16_gemv_kernel launch: %s", cudaGetErrorString(e));
+    return launched("w4a16_gemv_kernel");
+  }
   const int grid = n_slab < num_sms() ? n_slab : num_sms();
   kern<<<grid, 32 * (kGvWarps + 1), smem, st>>>(static_cast<const T*>(x), static_cast<const uint8_t*>(packed), bias,
                                                static_cast<T*>(y), a, v, err, static_cast<const T*>(lo.u),
@@ -1059,7 +1088,7 @@ int launch_gemv(const void* x, int M, int N, int K, int group, const void* packe
   a.n_kb = K / kBK;
   a.n_groups = K / group;
   a.kb_shift = kb_shift_of(group);
-  a.u_only_wait = 0;
+  a.u_only_wait = lo.r > 0 ? lo.u_only_wait : 0;
   if (M > 8 || (!NF && group > 4 * kBK)) return 1;
   // the activations are copied to shared memory when they fit and their rows
   // start on 16-byte boundaries (K is a multiple of 64)
