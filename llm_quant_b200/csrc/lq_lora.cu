@@ -84,9 +84,12 @@ __global__ void __launch_bounds__(32 * kLuWarps) lora_u_kernel(const T* __restri
                                                                float scaling) {
   constexpr int H = kLuWarps / 2;
   __shared__ float red[H][NTL][32][4];
-  // the fused linear that consumes u may start its set-up meanwhile; it waits
-  // for this grid before it touches global memory
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // launched as a programmatic dependent: wait for the kernel ahead of it (which
+  // may write x) before the first global access, and only then let the fused
+  // linear that consumes u start -- it reads x and the weights at once and
+  // waits for this grid only before it reads u
+  pdl_wait();
+  pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
   const int64_t n_tiles = (M + 15) / 16;
@@ -164,12 +167,9 @@ int lora_u_t(const void* x, int64_t M, int64_t K, const void* a, int rank, float
   const T* xp = static_cast<const T*>(x);
   const AT* ap = static_cast<const AT*>(a);
   T* up = static_cast<T*>(u);
-  if (rank <= 16)
-    lora_u_kernel<T, AT, 2><<<grid, 32 * kLuWarps, 0, st>>>(xp, ap, up, M, K, rank, scaling);
-  else if (rank <= 32)
-    lora_u_kernel<T, AT, 4><<<grid, 32 * kLuWarps, 0, st>>>(xp, ap, up, M, K, rank, scaling);
-  else
-    lora_u_kernel<T, AT, 8><<<grid, 32 * kLuWarps, 0, st>>>(xp, ap, up, M, K, rank, scaling);
+  auto kern = rank <= 16 ? lora_u_kernel<T, AT, 2> : rank <= 32 ? lora_u_kernel<T, AT, 4> : lora_u_kernel<T, AT, 8>;
+  const cudaError_t e = launch_pdl(kern, grid, dim3(32 * kLuWarps), 0, st, xp, ap, up, M, K, rank, scaling);
+  LQ_REQUIRE(e == cudaSuccess, LQ_ECUDA, "lora_u_kernel launch: %s", cudaGetErrorString(e));
   return launched("lora_u_kernel");
 }
 
