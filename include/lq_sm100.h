@@ -347,7 +347,10 @@ int lq_nf4_qlora_forward(const void* x, int act_dtype, int64_t M, int64_t N, int
  * u[M, 64] (act_dtype) = scaling * x[M, K] @ lora_a[rank, K]^T in columns
  * 0..rank-1 and zeros in rank..63; fp32 accumulation on the tensor cores,
  * rounded once to act_dtype.  lora_a in LQ_F32 or act_dtype; K % 64 == 0,
- * 1 <= rank <= 64; x and lora_a 16-byte aligned. */
+ * 1 <= rank <= 64; x and lora_a 16-byte aligned.  Launched as a programmatic
+ * dependent of the kernel ahead of it on the stream: it waits for that
+ * kernel to complete before its first memory access, so stream order holds
+ * as for an ordinary launch. */
 int lq_lora_u(const void* x, int act_dtype, int64_t M, int64_t K, const void* lora_a, int a_dtype,
               int64_t rank, float scaling, void* u, void* stream);
 
