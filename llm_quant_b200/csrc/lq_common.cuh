@@ -313,4 +313,8 @@ inline int resident_grid(K kernel, int threads, size_t smem, int64_t want) {
   return (int)(want < 1 ? 1 : (want < cap ? want : cap));
 }
 
+// lq_lora_u for at most 16 tokens runs as one cluster of this many blocks
+// (each a share of K); a kernel launched behind it leaves them their SMs.
+constexpr int kLoraUSplitBlocks = 8;
+
 }  // namespace lq

@@ -159,9 +159,128 @@ __global__ void __launch_bounds__(32 * kLuWarps) lora_u_kernel(const T* __restri
   }
 }
 
+// At most 16 tokens (one token tile): the K steps are split over a cluster
+// of kLoraUSplitBlocks blocks of 4 warps (block r takes steps [r S / B,
+// (r + 1) S / B), its warps those steps round robin), so that the 128 KB of a
+// rank-16 lora_A are read by eight SMs instead of one.  Each block adds its
+// warps' partial sums in shared memory; after a cluster barrier block r adds
+// the blocks' sums, in block order, for its share of the 16 x 64 outputs
+// through distributed shared memory, and a second barrier keeps every
+// block's shared memory alive until those reads are done.
+constexpr int kLsWarps = 4;
+
+__device__ __forceinline__ float ld_cluster_f32(const float* p, uint32_t rank) {
+  uint32_t ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
+  return v;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+template <typename T, typename AT, int NTL>
+__global__ void __launch_bounds__(32 * kLsWarps) lora_u_split_kernel(const T* __restrict__ x, const AT* __restrict__ a,
+                                                                    T* __restrict__ u, int M, int64_t K, int rank,
+                                                                    float scaling) {
+  constexpr int B = kLoraUSplitBlocks;
+  __shared__ float part[kLsWarps][NTL][32][4];
+  __shared__ float sum[NTL][32][4];
+  pdl_wait();
+  pdl_trigger();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int blk = (int)blockIdx.x;  // the cluster is the whole grid: rank = blockIdx.x
+  const int64_t r0 = min(g, M - 1), r1 = min(g + 8, M - 1);
+  float d[NTL][4];
+#pragma unroll
+  for (int nt = 0; nt < NTL; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) d[nt][e] = 0.0f;
+  const int64_t n_steps = K / 64;
+  const int64_t s_lo = n_steps * blk / B, s_hi = n_steps * (blk + 1) / B;
+#pragma unroll 2
+  for (int64_t s = s_lo + warp; s < s_hi; s += kLsWarps) {
+    const int64_t k = s * 64 + 16 * c;
+    const uint4* p0 = reinterpret_cast<const uint4*>(x + r0 * K + k);
+    const uint4* p1 = reinterpret_cast<const uint4*>(x + r1 * K + k);
+    const uint4 x0[2] = {__ldg(p0), __ldg(p0 + 1)};
+    const uint4 x1[2] = {__ldg(p1), __ldg(p1 + 1)};
+    uint4 av[NTL][2];
+#pragma unroll
+    for (int nt = 0; nt < NTL; ++nt) lu_load_a<T, AT>(a, nt * 8 + g, rank, K, k, av[nt]);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const int h = t >> 1, w0 = 2 * (t & 1);
+#pragma unroll
+      for (int nt = 0; nt < NTL; ++nt)
+        LuMma<T>::mma(d[nt], lu_word(x0[h], w0), lu_word(x1[h], w0), lu_word(x0[h], w0 + 1), lu_word(x1[h], w0 + 1),
+                      lu_word(av[nt][h], w0), lu_word(av[nt][h], w0 + 1));
+    }
+  }
+#pragma unroll
+  for (int nt = 0; nt < NTL; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) part[warp][nt][lane][e] = d[nt][e];
+  __syncthreads();
+  for (int i = threadIdx.x; i < NTL * 32 * 4; i += blockDim.x) {
+    float v = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kLsWarps; ++w) v += (&part[w][0][0][0])[i];
+    (&sum[0][0][0])[i] = v;
+  }
+  cluster_sync_all();
+  // block blk writes outputs (row, column pair) i = blk, blk + B, ... of the
+  // 16 x 32 column pairs of u (zeros past the rank)
+  for (int i = blk * blockDim.x + threadIdx.x; i < 16 * (kLuPitch / 2); i += B * blockDim.x) {
+    const int row = i / (kLuPitch / 2), pr = i % (kLuPitch / 2);
+    if (row >= M) continue;
+    const int nt = pr / 4, cc = pr % 4, ln = (row % 8) * 4 + cc, e = row >= 8 ? 2 : 0;
+    float v0 = 0.0f, v1 = 0.0f;
+    if (nt < NTL && 2 * pr < rank) {
+#pragma unroll
+      for (int r = 0; r < B; ++r) {
+        v0 += ld_cluster_f32(&sum[nt][ln][e], (uint32_t)r);
+        v1 += ld_cluster_f32(&sum[nt][ln][e + 1], (uint32_t)r);
+      }
+      v0 *= scaling;
+      v1 = 2 * pr + 1 < rank ? v1 * scaling : 0.0f;
+    }
+    reinterpret_cast<uint32_t*>(u + (int64_t)row * kLuPitch)[pr] = LuMma<T>::pack(v0, v1);
+  }
+  cluster_sync_all();  // no block leaves while others may still read its sums
+}
+
+template <typename T, typename AT>
+int lora_u_split_t(const void* x, int64_t M, int64_t K, const void* a, int rank, float scaling, void* u,
+                   cudaStream_t st) {
+  auto kern = rank <= 16 ? lora_u_split_kernel<T, AT, 2>
+                         : rank <= 32 ? lora_u_split_kernel<T, AT, 4> : lora_u_split_kernel<T, AT, 8>;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kLoraUSplitBlocks);
+  cfg.blockDim = dim3(32 * kLsWarps);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kLoraUSplitBlocks;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<const T*>(x), static_cast<const AT*>(a),
+                                           static_cast<T*>(u), (int)M, K, rank, scaling);
+  LQ_REQUIRE(e == cudaSuccess, LQ_ECUDA, "lora_u_split_kernel launch: %s", cudaGetErrorString(e));
+  return launched("lora_u_split_kernel");
+}
+
 template <typename T, typename AT>
 int lora_u_t(const void* x, int64_t M, int64_t K, const void* a, int rank, float scaling, void* u, cudaStream_t st,
              int max_blocks) {
+  if (M <= 16) return lora_u_split_t<T, AT>(x, M, K, a, rank, scaling, u, st);
   const int64_t tiles = (M + 15) / 16;
   const dim3 grid((unsigned)(max_blocks > 0 && max_blocks < tiles ? max_blocks : tiles));
   const T* xp = static_cast<const T*>(x);

@@ -1049,9 +1049,10 @@ int launch_gemv_nt(const W4Args& a, const void* x, const void* packed, const flo
   LQ_TRY(set_smem_once(kern, kGvSmemMax, attr_done));
   const int n_slab = a.N / 16;
   if (a.u_only_wait) {
-    // right behind lq_lora_u (one block here): a programmatic dependent on the
-    // SMs that block leaves free, started before u is done
-    const int sms = num_sms() - 1;
+    // right behind lq_lora_u (one cluster of kLoraUSplitBlocks blocks for these
+    // token counts): a programmatic dependent on the SMs those leave free,
+    // started before u is done
+    const int sms = num_sms() - kLoraUSplitBlocks;
     const int grid = n_slab < sms ? n_slab : sms;
     const cudaError_t e = launch_pdl(kern, dim3((unsigned)grid), dim3(32 * (kGvWarps + 1)), (size_t)smem, st,
                                      static_cast<const T*>(x), static_cast<const uint8_t*>(packed), bias,
