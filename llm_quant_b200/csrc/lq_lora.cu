@@ -14,7 +14,9 @@
 // memory; the block writes scaling * sum rounded to the activation dtype, and
 // zeros in columns rank .. 63.  (Splitting K over a cluster of blocks, summed
 // through distributed shared memory, measured slower: 12.1 against 7.9 us at
-// M = 1024, K = 4096, rank 16.)
+// M = 1024, K = 4096, rank 16.)  Up to 16 tokens there is only one tile, and
+// one block reading all of lora_A is the whole cost: there the K split over a
+// cluster of eight small blocks (lora_u_split_kernel) is used, 4.2 -> 3.2 us.
 #include <type_traits>
 
 #include "lq_common.cuh"
